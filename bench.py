@@ -1,0 +1,371 @@
+"""Selective-scan throughput benchmark (BASELINE config 2 on every GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one step = one selective-scan forward of BASELINE config 2 per GPU,
+B=64 sequences x D=1536 channels x L=2048 tokens x N=16 states, bf16 u,
+delta, B, C and y in Mamba's (B,D,L) layout, FP32 state, fused dt bias +
+softplus and D skip.  Synthetic seeded inputs with config 0's distributions
+(u, B, C, dt_pre ~ N(0,1), dt_bias = softplus^-1(logU[1e-3, 1e-1]),
+A[d,n] = -(n+1), D = 1).  Inputs (1.2 GB) exceed the 126 MB L2, so no flush is
+needed between steps.  N GPUs: batch sharding, every rank runs its own
+64-sequence shard (weak scaling), no collective on the scan path.
+
+metric "scan GB/s": algorithmic bytes (u, delta, y, B, C and the FP32
+parameters, each counted once) / time.  `value` is device-timed with CUDA
+events over K steps on the launching stream, max over ranks; `e2e` is the
+same metric through the public API with the inputs copied from pinned host
+memory and y copied back inside the timed region.  `roofline` compares the
+scan kernel against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+
+--impl reference times the reference's own CPU implementation
+(selective_scan_reference built from its sources into oracle/_ref) on all host
+cores over a bounded sample of the same workload (one batch row per thread),
+reported in the same unit by scaling with the state updates processed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, D, L, N = 64, 1536, 2048, 16
+METRIC = "scan GB/s (% HBM roofline) and tracks*frames/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+FALLBACK_HBM = 6650.0
+
+
+def algorithmic_bytes(batch=B, dim=D, length=L, state=N, elem=2) -> int:
+    """u, delta, y (batch, D, L) + B, C (batch, N, L) in `elem` bytes; A (D,N), D, dt_bias in FP32."""
+    return elem * (3 * batch * dim * length + 2 * batch * state * length) + 4 * (dim * state + 2 * dim)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per scan launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "scan_bulk_c2.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.lines: list[str] = []
+        self.proc = None
+        target = str(device_index)
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            target = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            pass
+        self.cmd = ["nvidia-smi", "-i", target, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "200"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(torch, device, seed: int, batch=B):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    bf = torch.bfloat16
+    u = torch.randn(batch, D, L, device=device, generator=g).to(bf)
+    delta = torch.randn(batch, D, L, device=device, generator=g).to(bf)
+    bm = torch.randn(batch, 1, N, L, device=device, generator=g).to(bf)
+    cm = torch.randn(batch, 1, N, L, device=device, generator=g).to(bf)
+    rng = np.random.default_rng(seed)
+    dtb = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    bias = torch.from_numpy(np.log(np.expm1(dtb)).astype(np.float32)).to(device)
+    A = -torch.arange(1, N + 1, dtype=torch.float32, device=device).repeat(D, 1).contiguous()
+    Dv = torch.ones(D, dtype=torch.float32, device=device)
+    return dict(u=u, delta=delta, B=bm, C=cm, bias=bias, A=A, D=Dv)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import saccade_v1_b200 as sb
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    sb.load_kernels()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        t = make_inputs(torch, device, 1234 + rank)
+        y = torch.empty_like(t["u"])
+    stream.synchronize()
+
+    def step():
+        sb.selective_scan_ex(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], delta_bias=t["bias"],
+                             layout="BDL", out=y, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        x = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+
+    # Device-timed region: K steps, per-launch events for the kernel duration.
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(device)
+    with Clocks(local_rank) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t1.record(stream)
+        t1.synchronize()
+    torch.cuda.synchronize(device)
+    barrier()
+    total_ms = max_over_ranks(t0.elapsed_time(t1))
+    kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    kernel_ms = max_over_ranks(kernel_ms)
+
+    # End to end through the public API: H2D of the step's inputs from pinned
+    # host memory, the scan, D2H of y, all inside the timed region.
+    host = {k: t[k].cpu().pin_memory() for k in ("u", "delta", "B", "C")}
+    y_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = y.numel() * y.element_size()
+    e2e_steps = max(2, min(args.steps, 5))
+
+    def e2e_step():
+        for k, v in host.items():
+            t[k].copy_(v, non_blocking=True)
+        step()
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        e2e_step()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    if rank != 0:
+        return None
+    nbytes = algorithmic_bytes()
+    per_step_s = total_ms / 1e3 / args.steps
+    value = nbytes * world / per_step_s / 1e9
+    peak, peak_kind = peaks()
+    achieved = nbytes / (kernel_ms / 1e3) / 1e9
+    cpu = cpu_baseline(args) if world == 1 and not args.no_cpu_baseline else None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config-0 distributions)",
+        "config": {"workload": "C2 bulk selective scan: B=64 D=1536 L=2048 N=16 bf16 (B,D,L), fp32 state, "
+                               "dt_bias+softplus+D fused, per GPU", "global_batch": B * world, "seq_len": L,
+                   "d_inner": D, "d_state": N, "parallelism": f"batch-sharded x{world}",
+                   "l2": "inputs 1.2 GB > 126 MB L2, no flush"},
+        "tracks_frames_per_s": round(B * world / per_step_s, 1),
+        "e2e": {"value": round(nbytes * world / (e2e_ms / 1e3 / e2e_steps) / 1e9, 3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": committed_traffic(), "peak_kind": peak_kind,
+                     "kernel": "scan (sacc_selective_scan_ex)", "algorithmic_bytes_per_launch": nbytes},
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps,
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+def reference_sample(threads: int):
+    """One bounded sample of the workload in the reference ABI: `threads` batch rows of (L, D) FP32."""
+    from oracle import oracle
+    rows = max(1, min(threads, B))
+    rng = np.random.default_rng(99)
+    u = rng.standard_normal((rows, L, D), dtype=np.float32)
+    dtb = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    bias = np.log(np.expm1(dtb)).astype(np.float32)
+    delta = (rng.standard_normal((rows, L, D), dtype=np.float32) + bias).astype(np.float32)  # dt_pre + dt_bias in FP32
+    b = rng.standard_normal((rows, L, N), dtype=np.float32)
+    c = rng.standard_normal((rows, L, N), dtype=np.float32)
+    a = -np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1))
+    d = np.ones(D, np.float32)
+    shape = oracle.Shape(rows, L, D, N, D, N, True)
+    return oracle, shape, [np.ascontiguousarray(x) for x in (u, delta, a, b, c, d)], rows
+
+
+def time_reference(threads: int):
+    """Runs the reference's selective_scan_reference once over the sample; returns (seconds, rows, kind)."""
+    import ctypes
+    oracle, shape, ins, rows = reference_sample(threads)
+    y = np.zeros(rows * L * D, np.float64)
+    R = oracle.ref_lib()
+    f32 = ctypes.POINTER(ctypes.c_float)
+    ptrs = [x.ctypes.data_as(f32) for x in ins]
+    t0 = time.perf_counter()
+    if R is not None:
+        rc = R.sacc_ref_selective_scan_threads(ctypes.byref(shape.c()), *ptrs,
+                                               y.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), threads)
+        kind = "reference"
+    else:  # the reference build did not travel: the C restatement, one thread
+        k = oracle.Case(shape, *ins)
+        rc, _, _ = oracle.scan_ref(k)
+        kind = "port"
+        threads = 1
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        raise RuntimeError(f"reference scan failed with status {rc}")
+    return dt, rows, kind, threads
+
+
+def cpu_baseline(args):
+    threads = os.cpu_count() or 1
+    dt, rows, kind, used = time_reference(threads)
+    value = algorithmic_bytes(batch=rows) / dt / 1e9
+    return {"value": round(value, 4), "unit": UNIT, "cores": used, "kind": kind,
+            "sample": f"{rows} of {B} batch rows (L={L}, D={D}, N={N}), one row per thread, FP32 reference ABI; "
+                      f"value scaled by the C2 bf16 algorithmic bytes of the rows processed; {dt:.2f} s"}
+
+
+def run_reference(args):
+    threads = os.cpu_count() or 1
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt, rows, kind, used = time_reference(threads)
+        if i >= args.warmup:
+            times.append(dt)
+    per = statistics.mean(times)
+    value = algorithmic_bytes(batch=rows) / per / 1e9
+    sample = (f"{rows} of {B} batch rows (L={L}, D={D}, N={N}) per step, one row per thread, FP32 reference ABI; "
+              f"scaled by the C2 bf16 algorithmic bytes of the rows processed")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64 (reference binary64 on f32 inputs)",
+        "data": "synthetic (seeded, config-0 distributions)",
+        "config": {"workload": "C2 bulk selective scan: B=64 D=1536 L=2048 N=16, sample on host cores",
+                   "global_batch": B, "seq_len": L, "d_inner": D, "d_state": N, "parallelism": f"{used} host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": used, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

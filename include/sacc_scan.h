@@ -1,0 +1,161 @@
+/*
+ * sacc_scan.h -- C ABI of the B200 selective-scan library (libsacc_scan.so).
+ *
+ * Drop-in boundary for saccade_v1's selective-scan hot path.  Every entry
+ * point takes plain pointers and sizes, never throws, and returns SACC_OK or
+ * an error code; the message of the last failure on the calling thread is
+ * sacc_last_error().  All GPU work is enqueued on the caller's stream only;
+ * no entry point allocates, synchronises or reads back to the host (once the
+ * kernels are loaded), so every call is capturable in a CUDA graph.
+ *
+ * Reference interfaces replaced (paths in the saccade_v1 project):
+ *   SaccScanStatus / SACC_SCAN_*    include/saccade/selective_scan_cuda.hpp:21-46
+ *   SaccScanShape                   include/saccade/selective_scan.hpp:19-27
+ *   SaccScanInputs                  include/saccade/selective_scan_cuda.hpp:48-55
+ *   sacc_scan_load_kernels          selective_scan_cuda_load_kernels, cuda/selective_scan.cu:341-357
+ *   sacc_selective_scan_f32         selective_scan_cuda, cuda/selective_scan.cu:359-400
+ *   sacc_cross_scan_expand_f32      cross_scan_expand_cuda, cuda/selective_scan.cu:402-417
+ *   sacc_cross_scan_merge_f32       cross_scan_merge_cuda, cuda/selective_scan.cu:419-434
+ *   sacc_scan_identity              selective_scan_cuda_identity, cuda/selective_scan.cu:436-446
+ * The reference throws std::invalid_argument (host rejection, nothing
+ * enqueued) and std::runtime_error (a CUDA API call failed); here those are
+ * SACC_EINVAL and SACC_ECUDA with the same diagnostic text.
+ */
+#ifndef SACC_SCAN_H
+#define SACC_SCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SACC_OK 0
+#define SACC_EINVAL 1 /* host rejection before any GPU work (reference: std::invalid_argument) */
+#define SACC_ECUDA 2  /* a CUDA API call failed (reference: std::runtime_error) */
+
+/* Device-side outcome of one call, in caller-owned device memory.  Cleared on
+ * the stream before any other work; `done` is written last.  An output is
+ * valid only when done == SACC_SCAN_DONE and flags == 0; on failure every
+ * output element is the quiet NaN 0x7fc00000. */
+typedef struct SaccScanStatus {
+    uint32_t flags;
+    uint32_t done;
+} SaccScanStatus;
+#define SACC_SCAN_DONE 0x4E414353u /* "SCAN" */
+
+/* Input bits: exact, set iff that tensor holds a NaN or an infinity.
+ * Range bits: per (batch, channel) lane, the first quantity in the
+ * reference's order (decay, drive, state, C*state, then D*u, output) whose
+ * FP32 value left the finite range, united over lanes. */
+#define SACC_SCAN_NONFINITE_U (1u << 0)
+#define SACC_SCAN_NONFINITE_DELTA (1u << 1)
+#define SACC_SCAN_NONFINITE_A (1u << 2)
+#define SACC_SCAN_NONFINITE_B (1u << 3)
+#define SACC_SCAN_NONFINITE_C (1u << 4)
+#define SACC_SCAN_NONFINITE_D (1u << 5)
+#define SACC_SCAN_DECAY_RANGE (1u << 8)
+#define SACC_SCAN_DRIVE_RANGE (1u << 9)
+#define SACC_SCAN_STATE_RANGE (1u << 10)
+#define SACC_SCAN_TERM_RANGE (1u << 11)
+#define SACC_SCAN_SKIP_RANGE (1u << 12)
+#define SACC_SCAN_OUTPUT_RANGE (1u << 13)
+#define SACC_CROSS_SCAN_NONFINITE_INPUT (1u << 16)
+#define SACC_SCAN_INPUT_FAILURES 0x3Fu
+#define SACC_SCAN_RANGE_FAILURES 0x3F00u
+
+/* Reference ABI: dense row-major FP32,
+ *   u, delta, y (batch, length, channels)   delta raw, before softplus
+ *   a (a_rows, state)                       a_rows = 1 or channels
+ *   b (batch, length, state)
+ *   c (batch, length, c_width)              c_width = 1 or state
+ *   d (channels)                            only when has_d
+ * state is a power of two in [1, 32]; length 0 is valid (empty output);
+ * every tensor holds at most INT32_MAX elements; zero initial state. */
+typedef struct SaccScanShape {
+    uint64_t batch, length, channels, state, a_rows, c_width;
+    int32_t has_d;
+} SaccScanShape;
+
+typedef struct SaccScanInputs {
+    const float *u, *delta, *a, *b, *c, *d;
+} SaccScanInputs;
+
+/* Loads every kernel of the library in the current CUDA context (defeats lazy
+ * loading, which would otherwise wait for device work at the first launch).
+ * Call once per context during initialisation.  Writes one line per kernel
+ * (registers, local, shared, max threads) into `report` when it is non-NULL. */
+int sacc_scan_load_kernels(char* report, size_t report_bytes);
+
+/* Validates on the host, then enqueues on `stream` only: status clear, input
+ * check + scan (one kernel), finalize.  `stream` must be an explicit
+ * non-default stream.  Zero workspace.  Pointers must be 4-byte aligned;
+ * y and status must not overlap an input or each other. */
+int sacc_selective_scan_f32(const SaccScanShape* shape, const SaccScanInputs* inputs, float* y, SaccScanStatus* status,
+                            cudaStream_t stream);
+
+/* Cross-Scan (x (batch, channels, height, width) <-> tokens (4 batch,
+ * height*width, channels), direction-major rows; direction 0 identity, 1 flip
+ * H and W, 2 flip W, 3 flip H).  Merge averages ((y0+y1)+y2)+y3 times 0.25. */
+typedef struct SaccCrossScanShape {
+    uint64_t batch, channels, height, width;
+} SaccCrossScanShape;
+int sacc_cross_scan_expand_f32(const SaccCrossScanShape* shape, const float* x, float* tokens, SaccScanStatus* status,
+                               cudaStream_t stream);
+int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, float* out, SaccScanStatus* status,
+                              cudaStream_t stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* sacc_last_error(void);
+
+/* Build identity: nvcc version, flags, target architectures, one key=value per line. */
+const char* sacc_scan_identity(void);
+
+/* ------------------------------------------------------------------------
+ * Extended scan (no counterpart in the reference, whose contract has zero
+ * initial state, no final state and FP32 only): the Mamba selective-scan
+ * forward with bf16/fp16/fp32 activations and FP32 state.
+ *
+ * layout SACC_LAYOUT_BLD (reference order):
+ *   u, delta, z, y (batch, length, channels); b (batch, length, groups, state);
+ *   c (batch, length, groups, c_width)
+ * layout SACC_LAYOUT_BDL (Mamba order):
+ *   u, delta, z, y (batch, channels, length); b (batch, groups, state, length);
+ *   c (batch, groups, c_width, length)
+ * a (a_rows, state) FP32; d, delta_bias (channels) FP32, each optional.
+ * Delta = softplus(delta + delta_bias) when delta_softplus, else delta + delta_bias.
+ * y = (sum_n C_n h_n + D u) * silu(z) (gate only when z is given).
+ * h0 / h_final (nseq, channels, state) FP32, each optional.
+ * cu_seqlens (nseq + 1 int32, batch must be 1): sequence k is tokens
+ * [cu_seqlens[k], cu_seqlens[k+1]) of the length axis and starts from h0[k]
+ * (or zero); without cu_seqlens nseq = batch.
+ * No status words: non-finite values propagate into y as IEEE arithmetic does.
+ * Pointers of 16-bit tensors must be 16-byte aligned and channels * 2 bytes
+ * (BLD) or length * 2 bytes (BDL) a multiple of 16, for the TMA staging.
+ * ------------------------------------------------------------------------ */
+#define SACC_DTYPE_F32 0
+#define SACC_DTYPE_BF16 1
+#define SACC_DTYPE_F16 2
+#define SACC_LAYOUT_BLD 0
+#define SACC_LAYOUT_BDL 1
+
+typedef struct SaccScanExArgs {
+    uint64_t batch, length, channels, state, groups, a_rows, c_width;
+    int32_t layout, dtype, delta_softplus, nseq;
+    const void *u, *delta, *b, *c, *z; /* activations, `dtype` */
+    const float *a, *d, *delta_bias;   /* parameters, FP32 */
+    const float* h0;                   /* optional (nseq, channels, state) */
+    float* h_final;                    /* optional (nseq, channels, state) */
+    const int32_t* cu_seqlens;         /* optional (nseq + 1) */
+    void* y;                           /* output, `dtype` */
+} SaccScanExArgs;
+
+int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SACC_SCAN_H */

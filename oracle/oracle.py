@@ -65,7 +65,7 @@ def lib():
         L.sacc_oracle_scan_bound.restype = None
         L.sacc_oracle_scan_bound.argtypes = [ctypes.POINTER(_Shape)] + [_f32p] * 6 + [_f64p]
         L.sacc_oracle_scan_ex.restype = None
-        L.sacc_oracle_scan_ex.argtypes = [ctypes.POINTER(_ExShape)] + [_f32p] * 9 + [_i32p, _f64p, _f64p]
+        L.sacc_oracle_scan_ex.argtypes = [ctypes.POINTER(_ExShape)] + [_f32p] * 9 + [_i32p, _f64p, _f64p, _f64p]
         L.sacc_oracle_cross_scan_source.restype = ctypes.c_size_t
         L.sacc_oracle_cross_scan_source.argtypes = [ctypes.c_size_t] * 4
         L.sacc_oracle_cross_scan_expand.restype = None
@@ -287,13 +287,16 @@ def scan_bound(k: Case) -> np.ndarray:
 
 
 def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bias=None, softplus: bool = True,
-            h0=None, want_final: bool = False, cu_seqlens=None, groups: int = 1, c_width: int | None = None):
+            h0=None, want_final: bool = False, cu_seqlens=None, groups: int = 1, c_width: int | None = None,
+            want_scale: bool = False):
     """Extended scan in binary64 (see scan_oracle.c sacc_oracle_scan_ex).
 
     Shapes, layout "BLD": u/delta/z (B, L, D); b (B, L, G, N); c (B, L, G, CW).
     Layout "BDL": u/delta/z (B, D, L); b (B, G, N, L); c (B, G, CW, L).
     a (D or 1, N); d, delta_bias (D,); h0 (nseq, D, N).
-    Returns (y float64 with u's shape, h_final float64 (nseq, D, N) or None).
+    Returns (y float64 with u's shape, h_final float64 (nseq, D, N) or None),
+    plus the per-element term magnitude sum_n |C h| + |D u| (times |silu(z)|)
+    when want_scale.
     """
     u = np.ascontiguousarray(u, np.float32)
     if layout == "BLD":
@@ -310,14 +313,16 @@ def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bia
                   int(z is not None), int(delta_bias is not None), int(softplus), int(h0 is not None),
                   int(want_final), nseq)
     y = np.zeros(u.shape, np.float64)
+    sc = np.zeros(u.shape, np.float64) if want_scale else None
     hf = np.zeros((nseq, D, N), np.float64) if want_final else None
     conv = lambda t: None if t is None else np.ascontiguousarray(t, np.float32)
     cu = None if cu_seqlens is None else np.ascontiguousarray(cu_seqlens, np.int32)
     tensors = [u, conv(delta), a, conv(b), conv(c), conv(d), conv(z), conv(delta_bias), conv(h0)]
     lib().sacc_oracle_scan_ex(ctypes.byref(sh), *[_fp(t) for t in tensors],
                               ctypes.cast(None, _i32p) if cu is None else cu.ctypes.data_as(_i32p),
-                              _dp(y), _dp(hf) if hf is not None else ctypes.cast(None, _f64p))
-    return y, hf
+                              _dp(y), _dp(hf) if hf is not None else ctypes.cast(None, _f64p),
+                              _dp(sc) if sc is not None else ctypes.cast(None, _f64p))
+    return (y, hf, sc) if want_scale else (y, hf)
 
 
 def cross_scan_source(direction: int, token: int, height: int, width: int) -> int:

@@ -221,7 +221,7 @@ typedef struct {
 
 void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* delta, const float* a, const float* b,
                          const float* c, const float* d, const float* z, const float* bias, const float* h0,
-                         const int32_t* cu_seqlens, double* y, double* h_final) {
+                         const int32_t* cu_seqlens, double* y, double* h_final, double* scale) {
     const size_t Bt = s->batch, L = s->length, D = s->channels, N = s->state, G = s->groups, CW = s->c_width;
     const size_t per_group = D / G;
     const size_t nseq = cu_seqlens ? (size_t)s->nseq : Bt;
@@ -248,19 +248,28 @@ void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* de
                 double raw = delta[at];
                 if (s->has_bias) raw += (double)bias[ch];
                 const double dt = s->apply_softplus ? sacc_oracle_softplus(raw) : raw;
-                double acc = 0.0;
+                double acc = 0.0, mag = 0.0;
                 for (size_t n = 0; n < N; ++n) {
                     const double decay = exp(dt * a_row[n]);
                     const double drive = dt * b[bat0 + n * bstride] * uu;
                     h[n] = decay * h[n] + drive;
-                    acc += c[cat0 + (CW == 1 ? 0 : n) * cstride] * h[n];
+                    const double term = c[cat0 + (CW == 1 ? 0 : n) * cstride] * h[n];
+                    acc += term;
+                    mag += fabs(term);
                 }
-                if (s->has_d) acc += (double)d[ch] * uu;
+                if (s->has_d) {
+                    acc += (double)d[ch] * uu;
+                    mag += fabs((double)d[ch] * uu);
+                }
                 if (s->has_z) {
-                    const double zz = z[at];
-                    acc *= zz / (1.0 + exp(-zz));
+                    const double zz = z[at], gate = zz / (1.0 + exp(-zz));
+                    acc *= gate;
+                    mag *= fabs(gate);
                 }
                 y[at] = acc;
+                /* Term magnitude sum_n |C_n h_n| + |D u| (times |silu(z)|): the
+                 * scale that FP32 rounding errors of y grow with. */
+                if (scale) scale[at] = mag;
             }
             if (s->want_final)
                 for (size_t n = 0; n < N; ++n) h_final[(seq * D + ch) * N + n] = h[n];

@@ -1,0 +1,89 @@
+"""ctypes binding of libsacc_scan.so (the C ABI declared in include/sacc_scan.h).
+
+The library is built in-tree (saccade_v1_b200/libsacc_scan.so).  There is no
+fallback: if the library is missing or does not load, every entry point
+raises, so a GPU caller can never silently run something else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsacc_scan.so")
+
+SACC_OK, SACC_EINVAL, SACC_ECUDA = 0, 1, 2
+SCAN_DONE = 0x4E414353
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+LAYOUT_BLD, LAYOUT_BDL = 0, 1
+
+# Exported symbols, in the order include/sacc_scan.h declares them.
+EXPORTS = (
+    "sacc_scan_load_kernels",
+    "sacc_selective_scan_f32",
+    "sacc_cross_scan_expand_f32",
+    "sacc_cross_scan_merge_f32",
+    "sacc_last_error",
+    "sacc_scan_identity",
+    "sacc_selective_scan_ex",
+)
+
+
+class ScanShape(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_uint64), ("length", ctypes.c_uint64), ("channels", ctypes.c_uint64),
+                ("state", ctypes.c_uint64), ("a_rows", ctypes.c_uint64), ("c_width", ctypes.c_uint64),
+                ("has_d", ctypes.c_int32)]
+
+
+class ScanInputs(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_void_p) for k in ("u", "delta", "a", "b", "c", "d")]
+
+
+class CrossScanShape(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_uint64) for k in ("batch", "channels", "height", "width")]
+
+
+class ScanExArgs(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_uint64), ("length", ctypes.c_uint64), ("channels", ctypes.c_uint64),
+                ("state", ctypes.c_uint64), ("groups", ctypes.c_uint64), ("a_rows", ctypes.c_uint64),
+                ("c_width", ctypes.c_uint64), ("layout", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("delta_softplus", ctypes.c_int32), ("nseq", ctypes.c_int32),
+                ("u", ctypes.c_void_p), ("delta", ctypes.c_void_p), ("b", ctypes.c_void_p), ("c", ctypes.c_void_p),
+                ("z", ctypes.c_void_p), ("a", ctypes.c_void_p), ("d", ctypes.c_void_p),
+                ("delta_bias", ctypes.c_void_p), ("h0", ctypes.c_void_p), ("h_final", ctypes.c_void_p),
+                ("cu_seqlens", ctypes.c_void_p), ("y", ctypes.c_void_p)]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libsacc_scan.so; raises if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `python -m saccade_v1_b200.build` "
+                          "(the selective-scan library has no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, sz, i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+    L.sacc_scan_load_kernels.argtypes = [ctypes.c_char_p, sz]
+    L.sacc_scan_load_kernels.restype = i
+    L.sacc_selective_scan_f32.argtypes = [ctypes.POINTER(ScanShape), ctypes.POINTER(ScanInputs), vp, vp, vp]
+    L.sacc_selective_scan_f32.restype = i
+    L.sacc_cross_scan_expand_f32.argtypes = [ctypes.POINTER(CrossScanShape), vp, vp, vp, vp]
+    L.sacc_cross_scan_expand_f32.restype = i
+    L.sacc_cross_scan_merge_f32.argtypes = [ctypes.POINTER(CrossScanShape), vp, vp, vp, vp]
+    L.sacc_cross_scan_merge_f32.restype = i
+    L.sacc_last_error.argtypes = []
+    L.sacc_last_error.restype = ctypes.c_char_p
+    L.sacc_scan_identity.argtypes = []
+    L.sacc_scan_identity.restype = ctypes.c_char_p
+    L.sacc_selective_scan_ex.argtypes = [ctypes.POINTER(ScanExArgs), vp]
+    L.sacc_selective_scan_ex.restype = i
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return load().sacc_last_error().decode()

@@ -1,0 +1,302 @@
+// capi.cpp -- extern "C" entry points of libsacc_scan.so (include/sacc_scan.h).
+//
+// Host validation restates the reference's selective_scan_cuda host side
+// (cuda/selective_scan.cu:285-400) with the same diagnostics, but reports
+// them as return codes plus a thread-local message instead of exceptions.
+// A rejected call enqueues nothing, so the caller's status words stay as they
+// were.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <initializer_list>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+
+#ifndef SACC_BUILD_FLAGS
+#define SACC_BUILD_FLAGS "unknown"
+#endif
+
+namespace sacc {
+namespace {
+
+thread_local std::string g_error;
+
+int set_error(int code, const std::string& what) {
+    g_error = what;
+    return code;
+}
+
+struct Reject {
+    std::string what;
+};
+
+[[noreturn]] void reject(const char* api, const std::string& what) { throw Reject{std::string(api) + ": " + what}; }
+
+std::size_t elements(const char* api, std::initializer_list<std::uint64_t> dims, const char* tensor) {
+    std::size_t product = 1;
+    for (const auto dim : dims) {
+        if (dim != 0 && product > kMaxElements / dim) reject(api, std::string(tensor) + " element count exceeds int32 capacity");
+        product *= static_cast<std::size_t>(dim);
+    }
+    return product;
+}
+
+void require_stream(const char* api, cudaStream_t stream) {
+    if (stream == nullptr || stream == cudaStreamLegacy || stream == cudaStreamPerThread)
+        reject(api, "an explicit non-default stream is required");
+}
+
+struct Region {
+    const void* data;
+    std::size_t bytes;
+    const char* name;
+};
+
+void require_pointer(const char* api, const Region& r, std::size_t align = alignof(float)) {
+    if (r.bytes == 0) return;
+    if (r.data == nullptr) reject(api, std::string(r.name) + " is null");
+    if (reinterpret_cast<std::uintptr_t>(r.data) % align != 0)
+        reject(api, std::string(r.name) + " is not " + std::to_string(align) + "-byte aligned");
+}
+
+bool overlaps(const Region& a, const Region& b) {
+    if (a.bytes == 0 || b.bytes == 0) return false;
+    const auto a0 = reinterpret_cast<std::uintptr_t>(a.data), b0 = reinterpret_cast<std::uintptr_t>(b.data);
+    return a0 < b0 + b.bytes && b0 < a0 + a.bytes;
+}
+
+// Outputs (output tensor, status) must not overlap inputs or each other
+// (reference cuda/selective_scan.cu:315-325).
+void require_regions(const char* api, std::initializer_list<Region> inputs, const Region& out, const Region& status) {
+    for (const auto& r : inputs) require_pointer(api, r);
+    require_pointer(api, out);
+    require_pointer(api, status);
+    for (const auto& r : inputs) {
+        if (overlaps(out, r)) reject(api, std::string(out.name) + " overlaps " + r.name);
+        if (overlaps(status, r)) reject(api, std::string("status overlaps ") + r.name);
+    }
+    if (overlaps(status, out)) reject(api, std::string("status overlaps ") + out.name);
+}
+
+struct CudaFail {
+    std::string what;
+};
+void ck(cudaError_t e, const char* call) {
+    if (e != cudaSuccess) throw CudaFail{std::string(call) + ": " + cudaGetErrorString(e)};
+}
+#define CK(call) ck((call), #call)
+
+// SM count of the current device, cached per device ordinal.
+int sm_count() {
+    static std::mutex mu;
+    static int cached[64] = {0};
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) {
+        int n = 0;
+        CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        return n;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == 0) CK(cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev));
+    return cached[dev];
+}
+
+template <typename F>
+int guarded(F&& body) {
+    try {
+        body();
+        g_error.clear();
+        return SACC_OK;
+    } catch (const Reject& r) {
+        return set_error(SACC_EINVAL, r.what);
+    } catch (const CudaFail& f) {
+        return set_error(SACC_ECUDA, f.what);
+    } catch (const std::exception& e) {
+        return set_error(SACC_ECUDA, e.what());
+    }
+}
+
+std::size_t dtype_bytes(int dtype) { return dtype == SACC_DTYPE_F32 ? 4 : 2; }
+
+} // namespace
+} // namespace sacc
+
+using namespace sacc;
+
+extern "C" {
+
+const char* sacc_last_error(void) { return g_error.c_str(); }
+
+const char* sacc_scan_identity(void) {
+    static const std::string id = [] {
+        std::string s = "library=libsacc_scan\nnvcc=" + std::to_string(__CUDACC_VER_MAJOR__) + "." +
+                        std::to_string(__CUDACC_VER_MINOR__) + "." + std::to_string(__CUDACC_VER_BUILD__) +
+                        "\nflags=" SACC_BUILD_FLAGS "\narch=sm_100a\n";
+        int rt = 0;
+        if (cudaRuntimeGetVersion(&rt) == cudaSuccess) s += "cudart=" + std::to_string(rt) + "\n";
+        return s;
+    }();
+    return id.c_str();
+}
+
+int sacc_scan_load_kernels(char* report, size_t report_bytes) {
+    return guarded([&] {
+        std::string text;
+        CK(load_scan_f32_kernels(text));
+        CK(load_cross_kernels(text));
+        CK(load_scan_ex_kernels(text));
+        (void)sm_count();
+        if (report && report_bytes) {
+            std::snprintf(report, report_bytes, "%s", text.c_str());
+        }
+    });
+}
+
+// reference cuda/selective_scan.cu:359-400
+int sacc_selective_scan_f32(const SaccScanShape* shape, const SaccScanInputs* in, float* y, SaccScanStatus* status,
+                            cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "selective_scan_cuda";
+        if (shape == nullptr || in == nullptr) reject(api, "shape and inputs are required");
+        const SaccScanShape& s = *shape;
+        require_stream(api, stream);
+        if (s.batch == 0 || s.channels == 0) reject(api, "batch and channels must be positive");
+        if (s.state == 0 || s.state > 32 || (s.state & (s.state - 1)) != 0)
+            reject(api, "state " + std::to_string(s.state) + " must be a power of two in [1, 32]");
+        if (s.a_rows != 1 && s.a_rows != s.channels) reject(api, "A rows must be 1 or channels");
+        if (s.c_width != 1 && s.c_width != s.state) reject(api, "C width must be 1 or state");
+        const auto ud = elements(api, {s.batch, s.length, s.channels}, "u/delta/y");
+        const auto bn = elements(api, {s.batch, s.length, s.state}, "B");
+        const auto cn = elements(api, {s.batch, s.length, s.c_width}, "C");
+        const auto an = elements(api, {s.a_rows, s.state}, "A");
+        const std::size_t dn = s.has_d ? static_cast<std::size_t>(s.channels) : 0;
+        constexpr auto f = sizeof(float);
+        require_regions(api,
+                        {{in->u, ud * f, "u"}, {in->delta, ud * f, "delta"}, {in->a, an * f, "A"}, {in->b, bn * f, "B"},
+                         {in->c, cn * f, "C"}, {in->d, dn * f, "D"}},
+                        {y, ud * f, "y"}, {status, sizeof(SaccScanStatus), "status"});
+        const int sms = sm_count();
+        CK(cudaMemsetAsync(status, 0, sizeof(SaccScanStatus), stream));
+        CheckList list{{{in->u, ud, SACC_SCAN_NONFINITE_U},
+                        {in->delta, ud, SACC_SCAN_NONFINITE_DELTA},
+                        {in->a, an, SACC_SCAN_NONFINITE_A},
+                        {in->b, bn, SACC_SCAN_NONFINITE_B},
+                        {in->c, cn, SACC_SCAN_NONFINITE_C},
+                        {in->d, dn, SACC_SCAN_NONFINITE_D}},
+                       6};
+        if (s.length > 0) {
+            ScanF32Launch p{in->u, in->delta, in->a, in->b, in->c, in->d, y, s.batch, s.length, s.channels,
+                            s.batch * s.channels, static_cast<unsigned>(s.state), s.a_rows == 1, s.c_width != 1,
+                            s.has_d != 0, list};
+            CK(launch_scan_f32(p, status, sms, stream));
+        } else {
+            CK(launch_check(list, status, sms, stream));
+        }
+        CK(launch_finalize(y, ud, status, sms, stream));
+    });
+}
+
+static std::size_t cross_total(const char* api, const SaccCrossScanShape& s) {
+    if (s.batch == 0 || s.channels == 0 || s.height == 0 || s.width == 0) reject(api, "dimensions must be positive");
+    return elements(api, {4, s.batch, s.height, s.width, s.channels}, "tokens");
+}
+
+// reference cuda/selective_scan.cu:402-417
+int sacc_cross_scan_expand_f32(const SaccCrossScanShape* shape, const float* x, float* tokens, SaccScanStatus* status,
+                               cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "cross_scan_expand_cuda";
+        if (shape == nullptr) reject(api, "shape is required");
+        require_stream(api, stream);
+        const auto total = cross_total(api, *shape);
+        require_regions(api, {{x, total / 4 * sizeof(float), "x"}}, {tokens, total * sizeof(float), "tokens"},
+                        {status, sizeof(SaccScanStatus), "status"});
+        const int sms = sm_count();
+        CK(cudaMemsetAsync(status, 0, sizeof(SaccScanStatus), stream));
+        const CheckList list{{{x, total / 4, SACC_CROSS_SCAN_NONFINITE_INPUT}}, 1};
+        CK(launch_check(list, status, sms, stream));
+        const CrossLaunch p{shape->batch, shape->channels, shape->height, shape->width};
+        CK(launch_cross_expand(p, x, tokens, sms, stream));
+        CK(launch_finalize(tokens, total, status, sms, stream));
+    });
+}
+
+// reference cuda/selective_scan.cu:419-434
+int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, float* out, SaccScanStatus* status,
+                              cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "cross_scan_merge_cuda";
+        if (shape == nullptr) reject(api, "shape is required");
+        require_stream(api, stream);
+        const auto total = cross_total(api, *shape);
+        require_regions(api, {{y, total * sizeof(float), "y"}}, {out, total / 4 * sizeof(float), "out"},
+                        {status, sizeof(SaccScanStatus), "status"});
+        const int sms = sm_count();
+        CK(cudaMemsetAsync(status, 0, sizeof(SaccScanStatus), stream));
+        const CheckList list{{{y, total, SACC_CROSS_SCAN_NONFINITE_INPUT}}, 1};
+        CK(launch_check(list, status, sms, stream));
+        const CrossLaunch p{shape->batch, shape->channels, shape->height, shape->width};
+        CK(launch_cross_merge(p, y, out, sms, stream));
+        CK(launch_finalize(out, total / 4, status, sms, stream));
+    });
+}
+
+int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "selective_scan_ex";
+        if (args == nullptr) reject(api, "args are required");
+        const SaccScanExArgs& a = *args;
+        require_stream(api, stream);
+        if (a.dtype != SACC_DTYPE_F32 && a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16)
+            reject(api, "dtype must be f32, bf16 or f16");
+        if (a.layout != SACC_LAYOUT_BLD && a.layout != SACC_LAYOUT_BDL) reject(api, "layout must be BLD or BDL");
+        if (a.batch == 0 || a.channels == 0) reject(api, "batch and channels must be positive");
+        if (a.state == 0 || a.state > 32 || (a.state & (a.state - 1)) != 0)
+            reject(api, "state " + std::to_string(a.state) + " must be a power of two in [1, 32]");
+        if (a.groups == 0 || a.channels % a.groups != 0) reject(api, "groups must divide channels");
+        if (a.a_rows != 1 && a.a_rows != a.channels) reject(api, "A rows must be 1 or channels");
+        if (a.c_width != 1 && a.c_width != a.state) reject(api, "C width must be 1 or state");
+        std::uint64_t nseq = a.batch;
+        if (a.cu_seqlens) {
+            if (a.batch != 1) reject(api, "cu_seqlens needs batch 1");
+            if (a.nseq <= 0) reject(api, "nseq must be positive with cu_seqlens");
+            nseq = static_cast<std::uint64_t>(a.nseq);
+        }
+        // Kernels index in 64 bits; the 32-bit limit here is per tensor, as in
+        // the reference ABI, so the int32 sequence offsets stay valid.
+        const auto ud = elements(api, {a.batch, a.length, a.channels}, "u/delta/y");
+        const auto bn = elements(api, {a.batch, a.length, a.groups, a.state}, "B");
+        const auto cn = elements(api, {a.batch, a.length, a.groups, a.c_width}, "C");
+        const auto an = elements(api, {a.a_rows, a.state}, "A");
+        const auto hn = elements(api, {nseq, a.channels, a.state}, "state");
+        const std::size_t e = dtype_bytes(a.dtype), f = sizeof(float);
+        const std::size_t dn = a.d ? a.channels : 0, bias_n = a.delta_bias ? a.channels : 0;
+        const std::size_t align = a.dtype == SACC_DTYPE_F32 ? 4 : 2;
+        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}, Region{a.y, ud * e, "y"}})
+            require_pointer(api, r, align);
+        for (const Region& r : {Region{a.a, an * f, "A"}, Region{a.d, dn * f, "D"}, Region{a.delta_bias, bias_n * f, "delta_bias"},
+                                Region{a.h0, a.h0 ? hn * f : 0, "h0"}, Region{a.h_final, a.h_final ? hn * f : 0, "h_final"},
+                                Region{a.cu_seqlens, a.cu_seqlens ? (nseq + 1) * sizeof(std::int32_t) : 0, "cu_seqlens"}})
+            require_pointer(api, r);
+        if (a.u == nullptr || a.delta == nullptr || a.a == nullptr || a.y == nullptr) reject(api, "u, delta, A and y are required");
+        if (a.length > 0 && (a.b == nullptr || a.c == nullptr)) reject(api, "B and C are required");
+        const Region yr{a.y, ud * e, "y"};
+        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}})
+            if (overlaps(yr, r)) reject(api, std::string("y overlaps ") + r.name);
+        if (a.h_final) {
+            const Region hr{a.h_final, hn * f, "h_final"};
+            if (overlaps(hr, yr)) reject(api, "h_final overlaps y");
+        }
+        CK(launch_scan_ex(a, sm_count(), stream));
+    });
+}
+
+} // extern "C"

@@ -1,0 +1,64 @@
+// internal.h -- declarations shared by the CUDA translation units and the
+// C-ABI layer (capi.cpp).  Not part of the public interface (include/).
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/sacc_scan.h"
+
+namespace sacc {
+
+// int32 element capacity of every tensor of the reference ABI
+// (reference src/selective_scan.cpp:79, cuda/selective_scan.cu:119).
+constexpr std::size_t kMaxElements = 2147483647u;
+
+struct CheckedTensor {
+    const float* data;
+    unsigned long long count;
+    std::uint32_t bit;
+};
+struct CheckList {
+    CheckedTensor tensor[6];
+    unsigned size;
+};
+
+// One reference-ABI call, resolved on the host.
+struct ScanF32Launch {
+    const float *u, *delta, *a, *b, *c, *d;
+    float* y;
+    unsigned long long batch, length, channels, lanes;
+    unsigned state;
+    bool a_shared, c_full, has_d;
+    CheckList check;
+};
+
+// Enqueues the fused input-check + scan kernel on `stream` (status already
+// cleared by the caller).  Returns a CUDA error (launch only).
+cudaError_t launch_scan_f32(const ScanF32Launch& p, SaccScanStatus* status, int sm_count, cudaStream_t stream);
+// Poisons `count` outputs with quiet NaN when flags != 0, then writes done.
+cudaError_t launch_finalize(float* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream);
+// Input check only (Cross-Scan and L = 0 paths).
+cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream);
+
+struct CrossLaunch {
+    unsigned long long batch, channels, height, width;
+};
+cudaError_t launch_cross_expand(const CrossLaunch& p, const float* x, float* tokens, int sm_count, cudaStream_t stream);
+cudaError_t launch_cross_merge(const CrossLaunch& p, const float* y, float* out, int sm_count, cudaStream_t stream);
+
+// Extended scan (bf16/fp16/fp32 activations, FP32 state).
+cudaError_t launch_scan_ex(const SaccScanExArgs& a, int sm_count, cudaStream_t stream);
+cudaError_t launch_scan_general(const SaccScanExArgs& a, cudaStream_t stream);
+cudaError_t load_scan_general_kernels(std::string& report);
+
+// Loads every kernel (cudaFuncGetAttributes) and sets shared-memory limits;
+// appends one report line per kernel.
+cudaError_t load_scan_f32_kernels(std::string& report);
+cudaError_t load_cross_kernels(std::string& report);
+cudaError_t load_scan_ex_kernels(std::string& report);
+
+} // namespace sacc

@@ -1,0 +1,47 @@
+// scan_common.cuh -- device helpers shared by the extended scan kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace sacc {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// softplus with the reference's threshold (x > 20 passes through,
+// src/selective_scan.cpp:123), FP32 library functions.
+__device__ __forceinline__ float softplus_precise(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// Same threshold; e^x from the special-function unit, log1p from the library
+// (log1p keeps full relative precision where 1 + e^x rounds to 1).
+__device__ __forceinline__ float softplus_fast(float x) {
+    return x > 20.0f ? x : log1pf(fast_exp2(__fmul_rn(x, kLog2e)));
+}
+
+// x * sigmoid(x) = x / (1 + e^-x); __fdividef returns 0 when e^-x overflows.
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, __fadd_rn(1.0f, fast_exp2(__fmul_rn(-x, kLog2e)))); }
+
+} // namespace sacc

@@ -1,0 +1,441 @@
+// scan_f32.cu -- reference-ABI FP32 selective scan for sm_100a.
+//
+// Contract: reference cuda/selective_scan.cu:359-400 (selective_scan_cuda),
+// arithmetic: cuda/selective_scan.cu:130-221.  Layouts (B,L,Dc) row-major FP32.
+//
+// B200 design (differs from the reference's one-thread-per-(b,d,n) kernel):
+//  * one thread owns a (batch, channel) lane and keeps all N states of that
+//    lane in registers, so per-token work (softplus, u/delta loads, D skip,
+//    output store) is done once per lane instead of N times and the state sum
+//    needs no shuffles;
+//  * the length axis is split into K chunks (K a power of two) when there are
+//    too few lanes to fill 148 SMs.  Chunk k of a lane first runs the
+//    recurrence from zero over its tokens (pass 1) and publishes
+//    (product of decays, local state) per state in shared memory; every chunk
+//    then folds its predecessors' carries into its true starting state and
+//    reruns its tokens with outputs (pass 2).  All chunks of a lane live in one
+//    CTA: no workspace, one kernel;
+//  * the input finiteness check runs in the same launch (extra CTAs after the
+//    scan CTAs), so one call is memset + 1 kernel + finalize.
+//
+// Per-token arithmetic keeps the reference's FP32 algorithm, so its running
+// error bound (docs/SCAN_CUDA.md section 5 of the reference) applies: the plain
+// FP32 products are used whenever they provably equal the reference's
+// mantissa/exponent-scaled products (Delta, Delta*B and Delta*B*u normal), and
+// the scaled form is evaluated otherwise.  With K = 1 the outputs are the
+// reference algorithm's bits (same operations, same summation tree).
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <climits>
+#include <cstdint>
+#include <string>
+
+#include "internal.h"
+
+namespace sacc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr unsigned kDecay = SACC_SCAN_DECAY_RANGE, kDrive = SACC_SCAN_DRIVE_RANGE, kState = SACC_SCAN_STATE_RANGE,
+                   kTerm = SACC_SCAN_TERM_RANGE, kSkip = SACC_SCAN_SKIP_RANGE, kOutput = SACC_SCAN_OUTPUT_RANGE;
+
+__device__ __forceinline__ bool finite32(float x) { return fabsf(x) <= FLT_MAX; } // false for NaN and +-inf
+
+// value = m * 2^e with m in [0.5, 1) or m == 0 (frexpf / ldexpf are exact).
+struct Scaled {
+    float m;
+    int e;
+};
+__device__ __forceinline__ Scaled split(float x) {
+    int e = 0;
+    const float m = frexpf(x, &e);
+    return {m, e};
+}
+
+// softplus(x) with the reference's threshold (x > 20 passes through), kept as
+// (m, e) so that a Delta below the FP32 normal range keeps full precision
+// (reference cuda/selective_scan.cu:49-59).  For -1024 <= x < -80 the result is
+// e^x (log1p(e^x) = e^x to 1e-35 relative there), formed as e^r * 2^k with the
+// Cody-Waite reduction k = rint(x / ln2), r = (x - k ln2_hi) - k ln2_lo
+// (ln2_hi = 0x3f317200 has 16 significant bits, so k * ln2_hi is exact).
+__device__ Scaled softplus_scaled(float x) {
+    if (x > 20.0f) return split(x);
+    if (x >= -80.0f) return split(log1pf(expf(x)));
+    if (x < -1024.0f) return {0.0f, 0};
+    const float ln2_hi = __int_as_float(0x3f317200), ln2_lo = 1.42860677e-6f;
+    const float k = rintf(__fmul_rn(x, 1.44269504f));
+    const float r = __fmaf_rn(-k, ln2_lo, __fmaf_rn(-k, ln2_hi, x));
+    Scaled s = split(expf(r));
+    s.e += static_cast<int>(k);
+    return s;
+}
+
+// Sum of N values with the association of an xor butterfly over N lanes
+// (offset N/2 first), i.e. the reference's group_sum order; destroys v.
+template <int N>
+__device__ __forceinline__ float tree_sum(float (&v)[N]) {
+#pragma unroll
+    for (int w = N / 2; w > 0; w /= 2)
+#pragma unroll
+        for (int i = 0; i < w; ++i) v[i] = __fadd_rn(v[i], v[i + w]);
+    return v[0];
+}
+
+struct Params {
+    const float *u, *delta, *a, *b, *c, *d;
+    float* y;
+    unsigned long long length, channels, lanes;
+    int a_shared, c_full, has_d, vec_b, vec_c;
+    int chunks, lanes_per_cta;
+    unsigned scan_blocks;
+    CheckList check;
+};
+
+template <int N>
+__device__ __forceinline__ void load_row(const float* p, float (&out)[N], bool vec) {
+    if constexpr (N % 4 == 0) {
+        if (vec) {
+#pragma unroll
+            for (int i = 0; i < N; i += 4) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i / 4);
+                out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = __ldg(p + i);
+}
+
+// Operands of one token of one lane.
+template <int N>
+struct Token {
+    float u, x;
+    float b[N];
+    float c[N];
+};
+
+template <int N>
+__device__ __forceinline__ void load_token(const Params& p, unsigned long long token, unsigned long long d, Token<N>& k) {
+    const unsigned long long at = token * p.channels + d;
+    k.u = __ldg(p.u + at);
+    k.x = __ldg(p.delta + at);
+    load_row<N>(p.b + token * N, k.b, p.vec_b);
+    if (p.c_full) {
+        load_row<N>(p.c + token * N, k.c, p.vec_c);
+    } else {
+        const float cv = __ldg(p.c + token);
+#pragma unroll
+        for (int n = 0; n < N; ++n) k.c[n] = cv;
+    }
+}
+
+// New states of one token; returns false when the plain FP32 products may
+// differ from the reference's scaled ones (then the caller uses the scaled form).
+template <int N>
+__device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a)[N], const Token<N>& k, float (&hn)[N],
+                                            float (&decay)[N], float (&drive)[N]) {
+    if (!(k.x >= -80.0f)) return false;
+    const float dv = k.x > 20.0f ? k.x : log1pf(expf(k.x));
+    bool fast = true;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        decay[n] = expf(__fmul_rn(dv, a[n]));
+        const float db = __fmul_rn(dv, k.b[n]);
+        drive[n] = __fmul_rn(db, k.u);
+        fast = fast & (fabsf(db) >= 0x1p-126f) & (fabsf(drive[n]) >= 0x1p-126f) & (fabsf(drive[n]) <= FLT_MAX);
+        hn[n] = __fmaf_rn(decay[n], h[n], drive[n]);
+    }
+    return fast;
+}
+
+// The reference's scaled per-token state update (cuda/selective_scan.cu:189-192).
+template <int N>
+__device__ __forceinline__ void states_scaled(const float (&h)[N], const float (&a)[N], const Token<N>& k, float (&hn)[N],
+                                           float (&decay)[N], float (&drive)[N]) {
+    const Scaled dl = softplus_scaled(k.x), su = split(k.u);
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const Scaled sb = split(k.b[n]);
+        decay[n] = expf(ldexpf(__fmul_rn(dl.m, a[n]), dl.e));
+        drive[n] = ldexpf(__fmul_rn(__fmul_rn(dl.m, sb.m), su.m), dl.e + sb.e + su.e);
+        hn[n] = __fmaf_rn(decay[n], h[n], drive[n]);
+    }
+}
+
+// Pass 1: state update without outputs, accumulating the decay product.
+template <int N>
+__device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], const float (&a)[N], const Token<N>& k) {
+    float hn[N], decay[N], drive[N];
+    if (!states_fast<N>(h, a, k, hn, decay, drive)) states_scaled<N>(h, a, k, hn, decay, drive);
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        h[n] = hn[n];
+        prod[n] = __fmul_rn(prod[n], decay[n]);
+    }
+}
+
+// Pass 2: one token with output and the reference's failure order
+// (cuda/selective_scan.cu:193-212).  Returns the failure bits (0 = ok).
+template <int N>
+__device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N], const Token<N>& k, bool has_d, float skip_d,
+                                             float& y) {
+    float hn[N], decay[N], drive[N];
+    if (!states_fast<N>(h, a, k, hn, decay, drive)) states_scaled<N>(h, a, k, hn, decay, drive);
+    unsigned fail = 0;
+    float term[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        term[n] = __fmul_rn(k.c[n], hn[n]);
+        fail |= !finite32(decay[n]) ? kDecay : !finite32(drive[n]) ? kDrive : !finite32(hn[n]) ? kState
+              : !finite32(term[n]) ? kTerm : 0u;
+        h[n] = hn[n];
+    }
+    if (fail) return fail;
+    float s[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) s[n] = term[n];
+    const float sum = tree_sum<N>(s);
+    const float skip = __fmul_rn(skip_d, k.u);
+    if (has_d && !finite32(skip)) return kSkip;
+    float out = has_d ? __fadd_rn(sum, skip) : sum;
+    if (!finite32(out)) {
+        // Every term is finite but a partial sum left the FP32 range: repeat
+        // with exact power-of-two scaling (reference cuda/selective_scan.cu:205-211).
+#pragma unroll
+        for (int n = 0; n < N; ++n) s[n] = __fmul_rn(term[n], 0x1p-8f);
+        const float scaled = tree_sum<N>(s);
+        out = has_d ? __fadd_rn(scaled, __fmul_rn(skip, 0x1p-8f)) : scaled;
+        if (fabsf(out) <= FLT_MAX * 0x1p-8f) out = __fmul_rn(out, 0x1p8f);
+        else return kOutput;
+    }
+    y = out;
+    return 0;
+}
+
+// Exact NaN/Inf test over the listed tensors (reference cuda/selective_scan.cu:226-234).
+__device__ void check_tensors(const CheckList& list, unsigned long long first, unsigned long long stride,
+                              SaccScanStatus* status) {
+    std::uint32_t found = 0;
+    for (unsigned t = 0; t < list.size; ++t) {
+        const CheckedTensor ct = list.tensor[t];
+        const float* data = ct.data;
+        unsigned long long i0 = 0;
+        const bool aligned = (reinterpret_cast<std::uintptr_t>(data) & 15u) == 0;
+        if (aligned) {
+            const unsigned long long quads = ct.count / 4;
+            const float4* q = reinterpret_cast<const float4*>(data);
+            bool bad = false;
+            for (unsigned long long i = first; i < quads; i += stride) {
+                const float4 v = __ldg(q + i);
+                bad |= !(finite32(v.x) & finite32(v.y) & finite32(v.z) & finite32(v.w));
+            }
+            if (bad) found |= ct.bit;
+            i0 = quads * 4;
+        }
+        bool bad = false;
+        for (unsigned long long i = i0 + first; i < ct.count; i += stride) bad |= !finite32(__ldg(data + i));
+        if (bad) found |= ct.bit;
+    }
+    if (found) atomicOr(&status->flags, found);
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanStatus* status) {
+    if (blockIdx.x >= p.scan_blocks) {
+        const unsigned long long first = static_cast<unsigned long long>(blockIdx.x - p.scan_blocks) * kThreads + threadIdx.x;
+        const unsigned long long stride = static_cast<unsigned long long>(gridDim.x - p.scan_blocks) * kThreads;
+        check_tensors(p.check, first, stride, status);
+        return;
+    }
+    extern __shared__ float2 carry[]; // [chunk][lane in CTA][state]: (decay product, local state)
+    __shared__ int chunk_failed[kThreads];
+    const int K = p.chunks, LPC = p.lanes_per_cta;
+    const int tid = threadIdx.x, li = tid % LPC, k = tid / LPC;
+    const unsigned long long lane = static_cast<unsigned long long>(blockIdx.x) * LPC + li;
+    const bool active = lane < p.lanes;
+    const unsigned long long L = p.length, Dc = p.channels;
+    const unsigned long long bb = active ? lane / Dc : 0, d = active ? lane % Dc : 0;
+    const unsigned long long t0 = L * k / K, t1 = L * (k + 1) / K;
+
+    float a[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) a[n] = active ? __ldg(p.a + (p.a_shared ? 0 : d * N) + n) : 0.0f;
+    const float skip_d = (active && p.has_d) ? __ldg(p.d + d) : 0.0f;
+    float h[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) h[n] = 0.0f;
+
+    if (K > 1) {
+        float prod[N];
+#pragma unroll
+        for (int n = 0; n < N; ++n) prod[n] = 1.0f;
+        if (active && k < K - 1) {
+            Token<N> cur;
+            if (t0 < t1) load_token<N>(p, bb * L + t0, d, cur);
+            for (unsigned long long t = t0; t < t1; ++t) {
+                Token<N> nxt;
+                if (t + 1 < t1) load_token<N>(p, bb * L + t + 1, d, nxt);
+                step_carry<N>(h, prod, a, cur);
+                cur = nxt;
+            }
+        }
+        float2* mine = carry + (static_cast<size_t>(k) * LPC + li) * N;
+#pragma unroll
+        for (int n = 0; n < N; ++n) mine[n] = make_float2(prod[n], h[n]);
+        __syncthreads();
+        // Fold the carries of chunks 0..k-1: H = prod_j * H + local_j.
+#pragma unroll
+        for (int n = 0; n < N; ++n) h[n] = 0.0f;
+        for (int j = 0; j < k; ++j) {
+            const float2* cj = carry + (static_cast<size_t>(j) * LPC + li) * N;
+#pragma unroll
+            for (int n = 0; n < N; ++n) {
+                const float2 v = cj[n];
+                h[n] = h[n] == 0.0f ? v.y : __fmaf_rn(v.x, h[n], v.y);
+            }
+        }
+    }
+
+    unsigned fail = 0;
+    if (active && t0 < t1) {
+        Token<N> cur;
+        load_token<N>(p, bb * L + t0, d, cur);
+        for (unsigned long long t = t0; t < t1; ++t) {
+            Token<N> nxt;
+            if (t + 1 < t1) load_token<N>(p, bb * L + t + 1, d, nxt);
+            float y = 0.0f;
+            fail = step_out<N>(h, a, cur, p.has_d != 0, skip_d, y);
+            if (fail) break;
+            p.y[(bb * L + t) * Dc + d] = y;
+            cur = nxt;
+        }
+    }
+    if (K > 1) {
+        // A lane reports the failure of its earliest failing chunk only, as the
+        // sequential recurrence stops at its first failure.
+        chunk_failed[tid] = fail ? 1 : 0;
+        __syncthreads();
+        if (fail) {
+            bool earlier = false;
+            for (int j = 0; j < k; ++j) earlier |= chunk_failed[j * LPC + li] != 0;
+            if (!earlier) atomicOr(&status->flags, fail);
+        }
+    } else if (fail) {
+        atomicOr(&status->flags, fail);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) check_kernel(CheckList list, SaccScanStatus* status) {
+    check_tensors(list, static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x,
+                  static_cast<unsigned long long>(gridDim.x) * kThreads, status);
+}
+
+// Last kernel of every call: poison every output on failure, then write done
+// (reference cuda/selective_scan.cu:238-244).
+__global__ void __launch_bounds__(kThreads) finalize_kernel(float* out, unsigned long long count, SaccScanStatus* status) {
+    const unsigned long long first = static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x;
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * kThreads;
+    if (status->flags)
+        for (unsigned long long i = first; i < count; i += stride) out[i] = __int_as_float(0x7fc00000);
+    if (first == 0) status->done = SACC_SCAN_DONE;
+}
+
+template <int N>
+const void* scan_kernel_ptr() {
+    return reinterpret_cast<const void*>(scan_f32_kernel<N>);
+}
+
+const void* pick_kernel(unsigned state) {
+    switch (state) {
+    case 1: return scan_kernel_ptr<1>();
+    case 2: return scan_kernel_ptr<2>();
+    case 4: return scan_kernel_ptr<4>();
+    case 8: return scan_kernel_ptr<8>();
+    case 16: return scan_kernel_ptr<16>();
+    default: return scan_kernel_ptr<32>();
+    }
+}
+
+unsigned long long total_checked(const CheckList& l) {
+    unsigned long long n = 0;
+    for (unsigned i = 0; i < l.size; ++i) n += l.tensor[i].count;
+    return n;
+}
+
+unsigned check_blocks(unsigned long long elements, int sm_count) {
+    const unsigned long long want = (elements + kThreads * 16ull - 1) / (kThreads * 16ull);
+    const unsigned long long cap = 2ull * static_cast<unsigned long long>(sm_count);
+    return static_cast<unsigned>(want < 1 ? 1 : want > cap ? cap : want);
+}
+
+} // namespace
+
+cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
+    Params p{};
+    p.u = s.u; p.delta = s.delta; p.a = s.a; p.b = s.b; p.c = s.c; p.d = s.d; p.y = s.y;
+    p.length = s.length; p.channels = s.channels; p.lanes = s.lanes;
+    p.a_shared = s.a_shared; p.c_full = s.c_full; p.has_d = s.has_d;
+    p.vec_b = (reinterpret_cast<std::uintptr_t>(s.b) & 15u) == 0;
+    p.vec_c = (reinterpret_cast<std::uintptr_t>(s.c) & 15u) == 0;
+    p.check = s.check;
+    // Chunks: enough (lane, chunk) threads for ~4 warps per SM scheduler, at
+    // least 4 tokens per chunk, at most 64 chunks; one chunk when lanes suffice.
+    const unsigned long long target = static_cast<unsigned long long>(sm_count) * 512ull;
+    int K = 1;
+    while (K < 64 && s.lanes * static_cast<unsigned long long>(K) < target &&
+           s.length >= static_cast<unsigned long long>(K) * 2ull * 4ull)
+        K *= 2;
+    p.chunks = K;
+    p.lanes_per_cta = kThreads / K;
+    const unsigned long long blocks = (s.lanes + p.lanes_per_cta - 1) / p.lanes_per_cta;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidValue;
+    p.scan_blocks = static_cast<unsigned>(blocks);
+    const unsigned extra = check_blocks(total_checked(s.check), sm_count);
+    const size_t smem = K > 1 ? static_cast<size_t>(kThreads) * s.state * sizeof(float2) : 0;
+    void* args[] = {&p, &status};
+    return cudaLaunchKernel(pick_kernel(s.state), dim3(p.scan_blocks + extra), dim3(kThreads), args, smem, stream);
+}
+
+cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
+    check_kernel<<<check_blocks(total_checked(list), sm_count), kThreads, 0, stream>>>(list, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(float* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
+    const unsigned long long want = (count + kThreads * 8ull - 1) / (kThreads * 8ull);
+    const unsigned long long cap = 4ull * static_cast<unsigned long long>(sm_count);
+    const unsigned blocks = static_cast<unsigned>(want < 1 ? 1 : want > cap ? cap : want);
+    finalize_kernel<<<blocks, kThreads, 0, stream>>>(out, count, status);
+    return cudaGetLastError();
+}
+
+cudaError_t load_scan_f32_kernels(std::string& report) {
+    struct Entry { const char* name; const void* fn; size_t smem; };
+    const Entry kernels[] = {
+        {"scan_f32_n1", scan_kernel_ptr<1>(), kThreads * 1 * sizeof(float2)},
+        {"scan_f32_n2", scan_kernel_ptr<2>(), kThreads * 2 * sizeof(float2)},
+        {"scan_f32_n4", scan_kernel_ptr<4>(), kThreads * 4 * sizeof(float2)},
+        {"scan_f32_n8", scan_kernel_ptr<8>(), kThreads * 8 * sizeof(float2)},
+        {"scan_f32_n16", scan_kernel_ptr<16>(), kThreads * 16 * sizeof(float2)},
+        {"scan_f32_n32", scan_kernel_ptr<32>(), kThreads * 32 * sizeof(float2)},
+        {"check", reinterpret_cast<const void*>(check_kernel), 0},
+        {"finalize", reinterpret_cast<const void*>(finalize_kernel), 0},
+    };
+    for (const auto& k : kernels) {
+        cudaFuncAttributes attr{};
+        cudaError_t e = cudaFuncGetAttributes(&attr, k.fn);
+        if (e != cudaSuccess) return e;
+        if (k.smem > 48 * 1024) {
+            e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(k.smem));
+            if (e != cudaSuccess) return e;
+        }
+        report += std::string("kernel=") + k.name + " registers=" + std::to_string(attr.numRegs) +
+                  " local_bytes=" + std::to_string(attr.localSizeBytes) + " shared_bytes=" +
+                  std::to_string(attr.sharedSizeBytes) + " max_threads=" + std::to_string(attr.maxThreadsPerBlock) + "\n";
+    }
+    return cudaSuccess;
+}
+
+} // namespace sacc

@@ -1,0 +1,168 @@
+"""Host-side front end of the selective-scan library for torch device buffers.
+
+Mirrors the reference's C++ API (include/saccade/selective_scan_cuda.hpp):
+  load_kernels()          selective_scan_cuda_load_kernels   (:57-62)
+  selective_scan_cuda()   selective_scan_cuda                (:64-71)
+  cross_scan_expand_cuda / cross_scan_merge_cuda             (:73-83)
+with the same argument meaning and error behaviour: a host rejection raises
+ScanInvalidArgument (the reference's std::invalid_argument) before anything is
+enqueued; a failed CUDA call raises ScanCudaError (std::runtime_error).
+Numeric failures are reported through the device status words, never raised.
+
+selective_scan_ex() is the extended Mamba-layout entry (bf16/fp16/fp32
+activations, FP32 state, fused bias/softplus/gate, state in/out, varlen).
+
+Everything goes through libsacc_scan.so; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+SCAN_DONE = _lib.SCAN_DONE
+
+
+class ScanInvalidArgument(ValueError):
+    """Host rejection (shape, capacity, pointer, overlap or stream); nothing was enqueued."""
+
+
+class ScanCudaError(RuntimeError):
+    """A CUDA API call failed; the status never reaches done."""
+
+
+def _check(rc: int) -> None:
+    if rc == _lib.SACC_OK:
+        return
+    msg = _lib.last_error()
+    if rc == _lib.SACC_EINVAL:
+        raise ScanInvalidArgument(msg)
+    raise ScanCudaError(msg)
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr() if t.numel() else None
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def load_kernels() -> str:
+    """Loads every kernel in the current CUDA context; returns the resource report."""
+    L = _lib.load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    _check(L.sacc_scan_load_kernels(buf, len(buf)))
+    return buf.value.decode()
+
+
+def identity() -> str:
+    return _lib.load().sacc_scan_identity().decode()
+
+
+@dataclass
+class SelectiveScanShape:
+    """include/saccade/selective_scan.hpp:19-27."""
+    batch: int = 0
+    length: int = 0
+    channels: int = 0
+    state: int = 0
+    a_rows: int = 1
+    c_width: int = 1
+    has_d: bool = True
+
+    def c(self) -> _lib.ScanShape:
+        return _lib.ScanShape(self.batch, self.length, self.channels, self.state, self.a_rows, self.c_width,
+                              int(self.has_d))
+
+
+def selective_scan_cuda(shape: SelectiveScanShape, u, delta, a, b, c, d, y, status, stream=None) -> None:
+    """Reference-ABI FP32 scan on device buffers (dense row-major float32 tensors).
+
+    status is a device tensor of two 32-bit words {flags, done}.  Enqueues on
+    `stream` (default: torch's current stream, which must not be the default
+    stream) and returns without synchronising.
+    """
+    L = _lib.load()
+    ins = _lib.ScanInputs(_ptr(u), _ptr(delta), _ptr(a), _ptr(b), _ptr(c), _ptr(d))
+    _check(L.sacc_selective_scan_f32(ctypes.byref(shape.c()), ctypes.byref(ins), _ptr(y), _ptr(status),
+                                     _stream_handle(stream)))
+
+
+@dataclass
+class CrossScanShape:
+    batch: int = 0
+    channels: int = 0
+    height: int = 0
+    width: int = 0
+
+    def c(self) -> _lib.CrossScanShape:
+        return _lib.CrossScanShape(self.batch, self.channels, self.height, self.width)
+
+
+def cross_scan_expand_cuda(shape: CrossScanShape, x, tokens, status, stream=None) -> None:
+    _check(_lib.load().sacc_cross_scan_expand_f32(ctypes.byref(shape.c()), _ptr(x), _ptr(tokens), _ptr(status),
+                                                  _stream_handle(stream)))
+
+
+def cross_scan_merge_cuda(shape: CrossScanShape, y, out, status, stream=None) -> None:
+    _check(_lib.load().sacc_cross_scan_merge_f32(ctypes.byref(shape.c()), _ptr(y), _ptr(out), _ptr(status),
+                                                 _stream_handle(stream)))
+
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+
+
+def selective_scan_ex(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta_softplus: bool = True,
+                      h0=None, h_final=None, cu_seqlens=None, layout: str = "BDL", out=None, stream=None):
+    """Extended selective scan (Mamba's selective_scan forward), returns y.
+
+    layout "BDL": u, delta, z (batch, D, L); B, C (batch, groups, N|1, L).
+    layout "BLD": u, delta, z (batch, L, D); B, C (batch, L, groups, N|1).
+    B and C may also be given without the groups axis (groups = 1).
+    A (D, N) or (1, N) float32; D, delta_bias (D,) float32.
+    h0, h_final: (nseq, D, N) float32 device tensors (h_final is written).
+    cu_seqlens: int32 (nseq + 1) with batch 1, packing sequences along L.
+    """
+    if layout not in ("BDL", "BLD"):
+        raise ScanInvalidArgument("selective_scan_ex: layout must be BLD or BDL")
+    if u.dtype not in _DTYPES:
+        raise ScanInvalidArgument("selective_scan_ex: dtype must be f32, bf16 or f16")
+    for name, t in (("delta", delta), ("B", B), ("C", C), ("z", z)):
+        if t is not None and t.dtype != u.dtype:
+            raise ScanInvalidArgument(f"selective_scan_ex: {name} dtype differs from u")
+    if layout == "BDL":
+        batch, dim, length = u.shape
+        if B.dim() == 3:
+            B, C = B.unsqueeze(1), C.unsqueeze(1)
+        groups, state = B.shape[1], B.shape[2]
+        c_width = C.shape[2]
+    else:
+        batch, length, dim = u.shape
+        if B.dim() == 3:
+            B, C = B.unsqueeze(2), C.unsqueeze(2)
+        groups, state = B.shape[2], B.shape[3]
+        c_width = C.shape[3]
+    for name, t in (("u", u), ("delta", delta), ("B", B), ("C", C), ("z", z), ("A", A), ("D", D),
+                    ("delta_bias", delta_bias), ("h0", h0), ("h_final", h_final), ("cu_seqlens", cu_seqlens)):
+        if t is not None and not t.is_contiguous():
+            raise ScanInvalidArgument(f"selective_scan_ex: {name} must be contiguous")
+    if out is None:
+        out = torch.empty_like(u)
+    nseq = (cu_seqlens.numel() - 1) if cu_seqlens is not None else batch
+    args = _lib.ScanExArgs(batch, length, dim, state, groups, A.shape[0] if A.dim() == 2 else 1, c_width,
+                           _lib.LAYOUT_BDL if layout == "BDL" else _lib.LAYOUT_BLD, _DTYPES[u.dtype],
+                           int(delta_softplus), nseq,
+                           _ptr(u), _ptr(delta), _ptr(B), _ptr(C), _ptr(z), _ptr(A), _ptr(D), _ptr(delta_bias),
+                           _ptr(h0), _ptr(h_final), _ptr(cu_seqlens), _ptr(out))
+    _check(_lib.load().sacc_selective_scan_ex(ctypes.byref(args), _stream_handle(stream)))
+    return out

@@ -1,0 +1,194 @@
+"""GPU parity of the extended scan (sacc_selective_scan_ex) against the oracle.
+
+Tolerances (fixed before the first GPU run):
+  fp32 activations: |gpu - ref| <= max(2 E, 1e-5 S) + 1e-5 |ref|, where E is
+      the reference's running error bound (oracle scan_bound) when the case is
+      expressible in the reference ABI and S the term magnitude
+      sum_n |C h| + |D u| (times |silu(z)|), i.e. rtol 1e-5 with an absolute
+      floor on the scale rounding errors grow with;
+  bf16 / fp16 activations: |gpu - ref| <= 1e-3 + 1e-2 |ref| against the
+      binary64 oracle on the same 16-bit-rounded inputs (FP32 state).
+Extensions are pinned by contract equalities derived from the reference
+recurrence: state chaining across a split, packed varlen == separate calls,
+L = 1 step == last row of a rescan, BDL == transposed BLD.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import saccade_v1_b200 as sb  # noqa: E402
+
+TORCH = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def rounded(x, dt):
+    """FP32 value of x after rounding to dtype dt (what the device reads)."""
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(TORCH[dt]).float().numpy()
+
+
+def make(seed, B, L, D, N, G=1, layout="BDL", dt="bf16", c_full=True, a_rows=None, spread=1.0):
+    """BASELINE config-0 distributions: u, z, B, C, dt_pre ~ N(0,1); dt_bias = softplus^-1(logU[1e-3, 1e-1]);
+    A[d, n] = -(n + 1); D = 1."""
+    r = np.random.default_rng(seed)
+    f = lambda *s: (r.standard_normal(s) * spread).astype(np.float32)
+    if layout == "BDL":
+        u, delta, z = f(B, D, L), f(B, D, L), f(B, D, L)
+        b, c = f(B, G, N, L), f(B, G, N if c_full else 1, L)
+    else:
+        u, delta, z = f(B, L, D), f(B, L, D), f(B, L, D)
+        b, c = f(B, L, G, N), f(B, L, G, N if c_full else 1)
+    dtb = np.exp(r.uniform(np.log(1e-3), np.log(1e-1), D))
+    bias = np.log(np.expm1(dtb)).astype(np.float32)
+    A = -np.tile(np.arange(1, N + 1, dtype=np.float32), (D if a_rows is None else a_rows, 1))
+    Dv = np.ones(D, np.float32)
+    t = dict(u=u, delta=delta, z=z, b=b, c=c, bias=bias, A=A, D=Dv)
+    for k in ("u", "delta", "z", "b", "c"):
+        t[k] = rounded(t[k], dt)
+    return t
+
+
+def gpu_run(t, dt, layout, use=("D", "z", "bias"), h0=None, want_final=False, cu=None, stream=None):
+    s = stream or torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        g = lambda k: torch.from_numpy(np.ascontiguousarray(t[k])).to(device="cuda", dtype=TORCH[dt])
+        f32 = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+        nseq = t["u"].shape[0] if cu is None else len(cu) - 1
+        N = t["A"].shape[1]
+        hf = torch.full((nseq, t["D"].size, N), np.nan, device="cuda") if want_final else None
+        y = sb.selective_scan_ex(g("u"), g("delta"), f32(t["A"]), g("b"), g("c"),
+                                 D=f32(t["D"]) if "D" in use else None, z=g("z") if "z" in use else None,
+                                 delta_bias=f32(t["bias"]) if "bias" in use else None, h0=f32(h0), h_final=hf,
+                                 cu_seqlens=None if cu is None else torch.tensor(cu, dtype=torch.int32, device="cuda"),
+                                 layout=layout, stream=s)
+    s.synchronize()
+    return y.float().cpu().numpy(), (hf.cpu().numpy() if hf is not None else None)
+
+
+def oracle_run(t, layout, use=("D", "z", "bias"), h0=None, want_final=False, cu=None, groups=1):
+    return oracle.scan_ex(t["u"], t["delta"], t["A"], t["b"], t["c"], layout=layout,
+                          d=t["D"] if "D" in use else None, z=t["z"] if "z" in use else None,
+                          delta_bias=t["bias"] if "bias" in use else None, h0=h0, want_final=want_final,
+                          cu_seqlens=cu, groups=groups, want_scale=True)
+
+
+def check_16bit(name, gpu, ref):
+    err = np.abs(gpu.astype(np.float64) - ref)
+    tol = 1e-3 + 1e-2 * np.abs(ref)
+    bad = ~(err <= tol)
+    assert not bad.any(), f"{name}: {int(bad.sum())}/{gpu.size} beyond 1e-3 + 1e-2|ref|; max err {err.max():.3g}"
+
+
+def check_f32(name, gpu, ref, scale, bound=None):
+    floor = 1e-5 * scale if bound is None else np.maximum(2 * bound, 1e-5 * scale)
+    err = np.abs(gpu.astype(np.float64) - ref)
+    tol = floor + 1e-5 * np.abs(ref)
+    bad = ~(err <= tol)
+    assert not bad.any(), f"{name}: {int(bad.sum())}/{gpu.size} beyond tolerance; max err {err.max():.3g}"
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("layout", ["BDL", "BLD"])
+def test_16bit_matches_oracle(dt, layout):
+    for seed, (B, L, D, N, G) in enumerate([(1, 16, 64, 16, 1), (2, 37, 48, 16, 2), (3, 129, 32, 8, 1),
+                                            (2, 64, 64, 32, 1), (1, 10, 24, 4, 1)]):
+        t = make(seed, B, L, D, N, G, layout, dt)
+        y, _ = gpu_run(t, dt, layout)
+        ref, _, _ = oracle_run(t, layout, groups=G)
+        check_16bit(f"{dt}_{layout}_{B}x{L}x{D}x{N}", y, ref)
+
+
+def test_config0_fp32_with_final_state():
+    """B=1, D=64, L=16, N=16, fp32, y (B,D,L) and final state (B,D,N)."""
+    t = make(0, 1, 16, 64, 16, 1, "BDL", "f32")
+    y, hf = gpu_run(t, "f32", "BDL", want_final=True)
+    ref, hr, scale = oracle_run(t, "BDL", want_final=True)
+    check_f32("config0_y", y, ref, scale)
+    np.testing.assert_allclose(hf, hr, rtol=1e-5, atol=1e-6)
+
+
+def test_fp32_reduces_to_reference_abi():
+    """No bias / gate / state: the extended scan is the reference operator."""
+    k = oracle.random_case(oracle.Shape(2, 37, 5, 16, 5, 16, True), 0x5eed0701)
+    s = k.shape
+    t = dict(u=k.u.reshape(2, 37, 5), delta=k.delta.reshape(2, 37, 5), b=k.b.reshape(2, 37, 1, 16),
+             c=k.c.reshape(2, 37, 1, 16), A=k.a.reshape(5, 16), D=k.d, z=None, bias=None)
+    y, _ = gpu_run(t, "f32", "BLD", use=("D",))
+    check_f32("ref_abi", y.reshape(-1), oracle.run(k), np.abs(oracle.run(k)), oracle.scan_bound(k))
+
+
+@pytest.mark.parametrize("layout", ["BDL", "BLD"])
+def test_state_chains_across_split(layout):
+    t = make(5, 2, 50, 32, 16, 1, layout, "f32")
+    h0 = np.random.default_rng(1).standard_normal((2, 32, 16)).astype(np.float32) * 0.5
+    y, hf = gpu_run(t, "f32", layout, h0=h0, want_final=True)
+    ref, hr, scale = oracle_run(t, layout, h0=h0, want_final=True)
+    check_f32("full", y, ref, scale)
+    cut = 21
+    ax = 2 if layout == "BDL" else 1
+    sl = lambda a, lo, hi: np.ascontiguousarray(np.take(a, np.arange(lo, hi), axis=ax))
+    part = lambda lo, hi: dict(t, u=sl(t["u"], lo, hi), delta=sl(t["delta"], lo, hi), z=sl(t["z"], lo, hi),
+                               b=sl(t["b"], lo, hi) if layout == "BLD" else np.ascontiguousarray(t["b"][..., lo:hi]),
+                               c=sl(t["c"], lo, hi) if layout == "BLD" else np.ascontiguousarray(t["c"][..., lo:hi]))
+    y1, h1 = gpu_run(part(0, cut), "f32", layout, h0=h0, want_final=True)
+    y2, h2 = gpu_run(part(cut, 50), "f32", layout, h0=h1, want_final=True)
+    np.testing.assert_allclose(np.concatenate([y1, y2], axis=ax), y, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(h2, hf, rtol=1e-5, atol=1e-5)
+
+
+def test_varlen_equals_separate_calls():
+    t = make(7, 1, 60, 32, 16, 1, "BLD", "f32")
+    cu = [0, 7, 8, 33, 60]
+    h0 = np.random.default_rng(2).standard_normal((4, 32, 16)).astype(np.float32)
+    y, hf = gpu_run(t, "f32", "BLD", h0=h0, want_final=True, cu=cu)
+    ref, hr, scale = oracle_run(t, "BLD", h0=h0, want_final=True, cu=np.array(cu, np.int32))
+    check_f32("varlen", y, ref, scale)
+    np.testing.assert_allclose(hf, hr, rtol=1e-5, atol=1e-5)
+
+
+def test_step_equals_last_row_of_rescan():
+    """A per-frame L = 1 update of carried state equals the last token of a full rescan."""
+    t = make(9, 8, 12, 32, 16, 1, "BLD", "f32")
+    y, hf = gpu_run(t, "f32", "BLD", want_final=True)
+    head = dict(t, u=t["u"][:, :11].copy(), delta=t["delta"][:, :11].copy(), z=t["z"][:, :11].copy(),
+                b=t["b"][:, :11].copy(), c=t["c"][:, :11].copy())
+    _, h11 = gpu_run(head, "f32", "BLD", want_final=True)
+    last = dict(t, u=t["u"][:, 11:].copy(), delta=t["delta"][:, 11:].copy(), z=t["z"][:, 11:].copy(),
+                b=t["b"][:, 11:].copy(), c=t["c"][:, 11:].copy())
+    y1, h12 = gpu_run(last, "f32", "BLD", h0=h11, want_final=True)
+    np.testing.assert_allclose(y1[:, 0], y[:, 11], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(h12, hf, rtol=1e-6, atol=1e-6)
+
+
+def test_layouts_agree():
+    t = make(11, 2, 40, 48, 16, 2, "BLD", "bf16")
+    y1, _ = gpu_run(t, "bf16", "BLD")
+    tr = lambda a: np.ascontiguousarray(np.moveaxis(a, 1, -1))
+    t2 = dict(t, u=tr(t["u"]), delta=tr(t["delta"]), z=tr(t["z"]), b=tr(t["b"]), c=tr(t["c"]))
+    y2, _ = gpu_run(t2, "bf16", "BDL")
+    ref, _, _ = oracle_run(t, "BLD", groups=2)
+    check_16bit("bld", y1, ref)
+    check_16bit("bdl", np.moveaxis(y2, -1, 1), ref)
+
+
+def test_rejections():
+    t = make(0, 1, 16, 64, 16)
+    u = torch.zeros(1, 64, 16, dtype=torch.bfloat16, device="cuda")
+    A = torch.zeros(64, 16, device="cuda")
+    B = torch.zeros(1, 1, 16, 16, dtype=torch.bfloat16, device="cuda")
+    s = torch.cuda.Stream()
+    with pytest.raises(sb.ScanInvalidArgument, match="non-default stream"):
+        sb.selective_scan_ex(u, u, A, B, B, stream=0)
+    with pytest.raises(sb.ScanInvalidArgument, match="power of two"):
+        sb.selective_scan_ex(u, u, torch.zeros(64, 3, device="cuda"),
+                             torch.zeros(1, 1, 3, 16, dtype=torch.bfloat16, device="cuda"),
+                             torch.zeros(1, 1, 3, 16, dtype=torch.bfloat16, device="cuda"), stream=s)
+    with pytest.raises(sb.ScanInvalidArgument, match="y overlaps u"):
+        sb.selective_scan_ex(u, u.clone(), A, B, B, out=u, stream=s)
+    del t

@@ -71,8 +71,75 @@ def committed_traffic():
     return None
 
 
+class NvmlClocks:
+    """Samples SM clock and throttle reasons through NVML every 10 ms while the timed region runs."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+
+    def __init__(self, device_index: int):
+        import pynvml
+        pynvml.nvmlInit()
+        self.nv = pynvml
+        uuid = None
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            pass
+        self.handle = None
+        if uuid:
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = None
+        if self.handle is None:
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+        self.samples: list[tuple[float, int]] = []
+        self.stop = threading.Event()
+
+    def _run(self):
+        nv, h = self.nv, self.handle
+        while not self.stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        self.thread.join(timeout=2)
+
+    def summary(self):
+        reasons = set()
+        for _, mask in self.samples:
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    reasons.add(name)
+        try:
+            mx = float(self.nv.nvmlDeviceGetMaxClockInfo(self.handle, self.nv.NVML_CLOCK_SM))
+        except Exception:
+            mx = None
+        sm = [c for c, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "source": "nvml"}
+
+
+def clock_sampler(device_index: int):
+    try:
+        return NvmlClocks(device_index)
+    except Exception:
+        return Clocks(device_index)
+
+
 class Clocks:
-    """Samples nvidia-smi every 200 ms while the timed region runs."""
+    """Samples nvidia-smi every 200 ms while the timed region runs (used when NVML is unavailable)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -158,7 +225,7 @@ def run_ours(args, rank, world, local_rank):
     sb.load_kernels()
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
-        t = make_inputs(torch, device, 1234 + rank)
+        t = make_inputs(torch, device, 1234 + rank, batch=args.batch)
         y = torch.empty_like(t["u"])
     stream.synchronize()
 
@@ -186,7 +253,7 @@ def run_ours(args, rank, world, local_rank):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(device)
-    with Clocks(local_rank) as clocks:
+    with clock_sampler(local_rank) as clocks:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -234,7 +301,7 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         return None
-    nbytes = algorithmic_bytes()
+    nbytes = algorithmic_bytes(batch=args.batch)
     per_step_s = total_ms / 1e3 / args.steps
     value = nbytes * world / per_step_s / 1e9
     peak, peak_kind = peaks()
@@ -244,11 +311,11 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config-0 distributions)",
-        "config": {"workload": "C2 bulk selective scan: B=64 D=1536 L=2048 N=16 bf16 (B,D,L), fp32 state, "
-                               "dt_bias+softplus+D fused, per GPU", "global_batch": B * world, "seq_len": L,
+        "config": {"workload": f"C2 bulk selective scan: B={args.batch} D=1536 L=2048 N=16 bf16 (B,D,L), fp32 state, "
+                               "dt_bias+softplus+D fused, per GPU", "global_batch": args.batch * world, "seq_len": L,
                    "d_inner": D, "d_state": N, "parallelism": f"batch-sharded x{world}",
                    "l2": "inputs 1.2 GB > 126 MB L2, no flush"},
-        "tracks_frames_per_s": round(B * world / per_step_s, 1),
+        "tracks_frames_per_s": round(args.batch * world / per_step_s, 1),
         "e2e": {"value": round(nbytes * world / (e2e_ms / 1e3 / e2e_steps) / 1e9, 3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -337,10 +404,11 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -113,6 +113,13 @@ const char* sacc_last_error(void);
 /* Build identity: nvcc version, flags, target architectures, one key=value per line. */
 const char* sacc_scan_identity(void);
 
+/* Diagnostics (no counterpart in the reference): every wait of a kernel on an
+ * asynchronous copy has an iteration limit; when one runs out, the kernel sets
+ * a bit in the library's device fault word and leaves.  Reads that word into
+ * *out (synchronous with the device), clearing it when `clear` is non-zero.
+ * 0 means no kernel has ever given up waiting. */
+int sacc_scan_fault(uint32_t* out, int clear);
+
 /* ------------------------------------------------------------------------
  * Extended scan (no counterpart in the reference, whose contract has zero
  * initial state, no final state and FP32 only): the Mamba selective-scan

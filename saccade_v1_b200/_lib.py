@@ -26,6 +26,7 @@ EXPORTS = (
     "sacc_last_error",
     "sacc_scan_identity",
     "sacc_selective_scan_ex",
+    "sacc_scan_fault",
 )
 
 
@@ -81,6 +82,8 @@ def load() -> ctypes.CDLL:
     L.sacc_scan_identity.restype = ctypes.c_char_p
     L.sacc_selective_scan_ex.argtypes = [ctypes.POINTER(ScanExArgs), vp]
     L.sacc_selective_scan_ex.restype = i
+    L.sacc_scan_fault.argtypes = [ctypes.POINTER(ctypes.c_uint32), i]
+    L.sacc_scan_fault.restype = i
     _lib = L
     return L
 

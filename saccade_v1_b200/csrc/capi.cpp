@@ -247,6 +247,15 @@ int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, f
     });
 }
 
+int sacc_scan_fault(uint32_t* out, int clear) {
+    return guarded([&] {
+        if (out == nullptr) reject("sacc_scan_fault", "out is required");
+        unsigned v = 0;
+        CK(read_bulk_fault(&v, clear != 0));
+        *out = v;
+    });
+}
+
 int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream) {
     return guarded([&] {
         constexpr const char* api = "selective_scan_ex";

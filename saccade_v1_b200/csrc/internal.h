@@ -54,6 +54,11 @@ cudaError_t launch_cross_merge(const CrossLaunch& p, const float* y, float* out,
 cudaError_t launch_scan_ex(const SaccScanExArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_scan_general(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_general_kernels(std::string& report);
+bool bulk_eligible(const SaccScanExArgs& a);
+cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream);
+cudaError_t load_scan_bulk_kernels(std::string& report);
+// Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
+cudaError_t read_bulk_fault(unsigned* out, bool clear);
 
 // Loads every kernel (cudaFuncGetAttributes) and sets shared-memory limits;
 // appends one report line per kernel.

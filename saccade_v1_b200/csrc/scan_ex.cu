@@ -170,9 +170,14 @@ namespace sacc {
 
 cudaError_t launch_scan_ex(const SaccScanExArgs& a, int sm_count, cudaStream_t stream) {
     (void)sm_count;
+    if (bulk_eligible(a)) return launch_scan_bulk(a, stream);
     return launch_scan_general(a, stream);
 }
 
-cudaError_t load_scan_ex_kernels(std::string& report) { return load_scan_general_kernels(report); }
+cudaError_t load_scan_ex_kernels(std::string& report) {
+    const cudaError_t e = load_scan_general_kernels(report);
+    if (e != cudaSuccess) return e;
+    return load_scan_bulk_kernels(report);
+}
 
 } // namespace sacc

@@ -192,3 +192,66 @@ def test_rejections():
     with pytest.raises(sb.ScanInvalidArgument, match="y overlaps u"):
         sb.selective_scan_ex(u, u.clone(), A, B, B, out=u, stream=s)
     del t
+
+
+# ---------------------------------------------------------------- bulk path
+# Shapes inside the bulk kernel's domain: 16-bit (B, D, L), N = 16,
+# D a multiple of 128 (per group), L a multiple of 8.
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("case", [
+    dict(B=2, L=96, D=256, G=1, c_full=True, use=("D", "z", "bias")),
+    dict(B=1, L=200, D=128, G=1, c_full=True, use=("D", "bias")),        # partial last chunk
+    dict(B=2, L=64, D=256, G=2, c_full=False, use=("D", "z", "bias")),   # groups, rank-1 C
+    dict(B=3, L=40, D=384, G=1, c_full=True, use=()),                    # no bias / D / gate
+])
+def test_bulk_path_matches_oracle(dt, case):
+    t = make(21, case["B"], case["L"], case["D"], 16, case["G"], "BDL", dt, c_full=case["c_full"])
+    y, _ = gpu_run(t, dt, "BDL", use=case["use"])
+    ref, _, _ = oracle_run(t, "BDL", use=case["use"], groups=case["G"])
+    check_16bit(f"bulk_{dt}_{case}", y, ref)
+
+
+def test_bulk_path_state_in_out():
+    t = make(22, 2, 72, 256, 16, 1, "BDL", "bf16")
+    h0 = (np.random.default_rng(3).standard_normal((2, 256, 16)) * 0.5).astype(np.float32)
+    y, hf = gpu_run(t, "bf16", "BDL", h0=h0, want_final=True)
+    ref, hr, _ = oracle_run(t, "BDL", h0=h0, want_final=True)
+    check_16bit("bulk_state_y", y, ref)
+    np.testing.assert_allclose(hf, hr, rtol=1e-3, atol=1e-3)
+
+
+def test_bulk_config2_full_size_sampled_lanes():
+    """BASELINE config 2 at full size (64 x 1536 x 2048, N = 16, bf16): 48 sampled
+    lanes against the oracle run on exactly those lanes."""
+    B, D, L, N = 64, 1536, 2048, 16
+    s = torch.cuda.Stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    with torch.cuda.stream(s):
+        u = torch.randn(B, D, L, device="cuda", generator=g).to(torch.bfloat16)
+        dl = torch.randn(B, D, L, device="cuda", generator=g).to(torch.bfloat16)
+        bm = torch.randn(B, 1, N, L, device="cuda", generator=g).to(torch.bfloat16)
+        cm = torch.randn(B, 1, N, L, device="cuda", generator=g).to(torch.bfloat16)
+        rng = np.random.default_rng(5)
+        bias = np.log(np.expm1(np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D)))).astype(np.float32)
+        A = -np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1))
+        y = sb.selective_scan_ex(u, dl, torch.from_numpy(A).cuda(), bm, cm, D=torch.ones(D, device="cuda"),
+                                 delta_bias=torch.from_numpy(bias).cuda(), layout="BDL", stream=s)
+    s.synchronize()
+    picks = [(int(b), int(d)) for b, d in zip(rng.integers(0, B, 48), rng.integers(0, D, 48))]
+    for b, d in picks:
+        f = lambda x: x.float().cpu().numpy()
+        ref, _ = oracle.scan_ex(f(u[b:b + 1, d:d + 1]), f(dl[b:b + 1, d:d + 1]), A[d:d + 1], f(bm[b:b + 1]),
+                                f(cm[b:b + 1]), layout="BDL", d=np.ones(1, np.float32), delta_bias=bias[d:d + 1])
+        check_16bit(f"c2_lane_{b}_{d}", f(y[b:b + 1, d:d + 1]), ref)
+    fault = ctypes_fault()
+    assert fault == 0
+
+
+def ctypes_fault():
+    import ctypes
+    from saccade_v1_b200 import _lib
+    v = ctypes.c_uint32(0)
+    assert _lib.load().sacc_scan_fault(ctypes.byref(v), 0) == 0
+    return v.value

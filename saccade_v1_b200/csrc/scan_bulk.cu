@@ -1,26 +1,27 @@
-// scan_bulk.cu -- high-throughput selective scan for 16-bit activations in
-// Mamba's (B, D, L) layout, N = 16 states, FP32 state.
+// scan_bulk.cu -- high-throughput selective scan for 16-bit activations with
+// FP32 state and N = 16 states, in Mamba's (B, D, L)
+// layout or the reference's (B, L, D) layout.
 //
 // Work split: one thread owns one (batch, channel) lane and its 16 states in
 // registers; a CTA of 128 threads owns 128 consecutive channels of one batch
 // row and walks the sequence in chunks of 32 tokens.
 //
 // Data movement: per chunk, one thread issues TMA loads of the u / delta / z
-// tiles (128 rows x 64 bytes, 64-byte swizzle so that every thread reads its
-// own row with conflict-free 16-byte shared loads) and of the B / C tiles
-// (16 x 32 tokens) into a two-stage ring completed by mbarriers; the outputs
-// are written into a swizzled shared tile and stored with a TMA store.  The
-// chunk after next is in flight while one chunk is computed.  Inputs are read
-// from HBM once; nothing is re-read.
+// tiles and of the B / C tiles into a two-stage ring completed by mbarriers,
+// and a TMA store of the y tile.  In (B, D, L) each thread's 32 tokens are one
+// 64-byte row of a 64-byte-swizzled tile, read with conflict-free 16-byte
+// shared loads; in (B, L, D) a warp reads 32 consecutive channels of one
+// token.  B and C are converted once per chunk to an FP32 token-major table
+// that all threads read with broadcast loads.  Every input byte crosses HBM
+// once, every output byte once.
 //
-// Arithmetic: the scan is bound by the FP32 and special-function pipes, not by
-// HBM (16 state updates per 6 bytes of bf16 traffic: one exp, one multiply for
-// Delta*A, one for Delta*u*B, one FMA for the state and one for C*h per
-// update).  The 16 decays of a token are split between the MUFU ex2 unit and
-// an FMA-pipe exp2 (Cody-Waite reduction 2^x = 2^j 2^f, degree-5 minimax
-// polynomial for 2^f, coefficients from gen_exp2_poly.py, max relative error
-// 2.4e-7), so both pipes work in parallel; state pairs use the packed
-// fma/mul.rn.f32x2 instructions to halve the issue slots.
+// Arithmetic: with N = 16 the scan is bound by the special-function unit, not
+// by HBM: every state update needs one 2^x (MUFU ex2, 16 per SM per clock) and
+// four FP32 operations (Delta*A, Delta*u*B, the state FMA and the C*h FMA),
+// against 6 bytes of bf16 traffic per 16 updates.  softplus runs on the FMA
+// pipe except for one ex2 (log1p(e) = e * P(e), a degree-7 fit with 3e-7
+// relative error, gen_exp2_poly.py), so the special-function unit spends its
+// cycles on the decays.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -46,51 +47,47 @@ constexpr int kLanes = 128; // threads (lanes) per CTA
 constexpr int kT = 32;      // tokens per chunk
 constexpr int kStages = 2;
 constexpr int kN = 16;
-constexpr int kPairs = kN / 2;
+constexpr int kMinBlocks = 4; // four CTAs per SM: 128 registers per thread
 
-template <typename T>
+template <typename T, bool kHasZ>
 struct Smem {
     alignas(1024) T u[kStages][kLanes * kT];
     alignas(1024) T dl[kStages][kLanes * kT];
-    alignas(1024) T z[kStages][kLanes * kT];
-    alignas(1024) T y[2][kLanes * kT];
+    alignas(1024) T z[kHasZ ? kStages : 1][kHasZ ? kLanes * kT : 8];
+    alignas(1024) T y[kLanes * kT];
     alignas(128) T braw[kStages][kN * kT];
     alignas(128) T craw[kStages][kN * kT];
     alignas(16) float bc[kT][2 * kN]; // per token: B[0..15], C[16..31] (C[16] only when rank 1)
     alignas(8) std::uint64_t full[kStages];
 };
 
+template <typename T, bool kHasZ>
+constexpr size_t smem_bytes() {
+    return sizeof(Smem<T, kHasZ>) + 1024; // + alignment slack for the 1024-byte swizzle atoms
+}
+
 struct BulkParams {
     const float *a, *d, *bias, *h0;
     float* h_final;
-    unsigned long long length, channels, lanes, per_group;
+    unsigned long long length, channels, per_group;
     unsigned groups;
-    int a_shared, c_full, has_d, softplus, has_z, nchunks;
+    int a_shared, c_full, has_d, softplus, nchunks;
 };
 
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-    unsigned long long r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return bits_f2(r);
-}
-
-// 2^x for a pair on the FMA pipe: j = rint(x) by the 1.5 * 2^23 addition,
-// f = x - j in [-1/2, 1/2], p(f) ~ 2^f, exponent j added to p's bits.
-// x is clamped to [-125, 126]; 2^-125 stands in for smaller decays.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    x.x = fminf(fmaxf(x.x, -125.0f), 126.0f);
-    x.y = fminf(fmaxf(x.y, -125.0f), 126.0f);
-    const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    const float2 t = add2(x, magic);
-    const float2 j = sub2(t, magic);
-    const float2 f = sub2(x, j);
-    float2 p = fma2(make_float2(1.3276472e-3f, 1.3276472e-3f), f, make_float2(9.675541e-3f, 9.675541e-3f));
-    p = fma2(p, f, make_float2(5.550713e-2f, 5.550713e-2f));
-    p = fma2(p, f, make_float2(2.4022120e-1f, 2.4022120e-1f));
-    p = fma2(p, f, make_float2(6.9314694e-1f, 6.9314694e-1f));
-    p = fma2(p, f, make_float2(1.0000001f, 1.0000001f));
-    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+// softplus(x) = max(x, 0) + log1p(e^-|x|), log1p(e) = e * P(e) on e in (0, 1]
+// (degree-7 least-squares fit, relative error 3.2e-7 in FP32); x > 20 passes
+// through as in the reference (src/selective_scan.cpp:123).
+__device__ __forceinline__ float softplus_bulk(float x) {
+    const float e = fast_exp2(-fabsf(x) * kLog2e);
+    float q = fmaf(-8.336497e-3f, e, 4.337085e-2f);
+    q = fmaf(q, e, -1.0667790e-1f);
+    q = fmaf(q, e, 1.7675494e-1f);
+    q = fmaf(q, e, -2.4470469e-1f);
+    q = fmaf(q, e, 3.3271188e-1f);
+    q = fmaf(q, e, -4.9997127e-1f);
+    q = fmaf(q, e, 9.9999976e-1f);
+    const float r = fmaf(e, q, fmaxf(x, 0.0f));
+    return x > 20.0f ? x : r;
 }
 
 template <typename T>
@@ -123,46 +120,109 @@ __device__ __forceinline__ std::uint32_t pack2<__half>(float lo, float hi) {
     return w;
 }
 
-template <typename T>
-__device__ __forceinline__ float scalar16(T v) {
-    return to_f32(v);
+// Eight tokens of one lane's u / raw delta / z.
+struct Block8 {
+    float u[8], x[8], z[8];
+};
+
+// (B, D, L): row `tid` of a 64-byte-swizzled [128][32] tile; chunk q of row r
+// sits at q ^ ((r >> 1) & 3) (TMA 64-byte swizzle: address bits [4:5] ^= [7:8]).
+template <typename T, bool kHasZ>
+__device__ __forceinline__ void load_block_bdl(const T* u, const T* dl, const T* z, int tid, int q, Block8& blk) {
+    const int off = tid * kT + ((q ^ ((tid >> 1) & 3)) << 3);
+    const uint4 uq = *reinterpret_cast<const uint4*>(u + off);
+    const uint4 xq = *reinterpret_cast<const uint4*>(dl + off);
+    const std::uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w}, xw[4] = {xq.x, xq.y, xq.z, xq.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 a = unpack2<T>(uw[j]), b = unpack2<T>(xw[j]);
+        blk.u[2 * j] = a.x; blk.u[2 * j + 1] = a.y;
+        blk.x[2 * j] = b.x; blk.x[2 * j + 1] = b.y;
+    }
+    if constexpr (kHasZ) {
+        const uint4 zq = *reinterpret_cast<const uint4*>(z + off);
+        const std::uint32_t zw[4] = {zq.x, zq.y, zq.z, zq.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 c = unpack2<T>(zw[j]);
+            blk.z[2 * j] = c.x; blk.z[2 * j + 1] = c.y;
+        }
+    }
 }
 
-// One chunk's issue: u, delta (and z) tiles of this CTA's 128 rows, B and C tiles.
 template <typename T>
-__device__ __forceinline__ void issue_chunk(Smem<T>& sm, int s, int chunk, int row0, int brow0, int crow0, int cw,
-                                            bool has_z, const CUtensorMap* tu, const CUtensorMap* td, const CUtensorMap* tz,
-                                            const CUtensorMap* tb, const CUtensorMap* tc) {
+__device__ __forceinline__ void store_block_bdl(T* y, int tid, int q, const float (&out)[8]) {
+    const int off = tid * kT + ((q ^ ((tid >> 1) & 3)) << 3);
+    *reinterpret_cast<uint4*>(y + off) = make_uint4(pack2<T>(out[0], out[1]), pack2<T>(out[2], out[3]),
+                                                    pack2<T>(out[4], out[5]), pack2<T>(out[6], out[7]));
+}
+
+// (B, L, D): token-major [32][128] tile; lane `tid` is column tid.
+template <typename T, bool kHasZ>
+__device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T* z, int tid, int q, Block8& blk) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int at = (q * 8 + j) * kLanes + tid;
+        blk.u[j] = to_f32(u[at]);
+        blk.x[j] = to_f32(dl[at]);
+        if constexpr (kHasZ) blk.z[j] = to_f32(z[at]);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const float (&out)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[(q * 8 + j) * kLanes + tid] = from_f32<T>(out[j]);
+}
+
+// Loads of one chunk into stage s.  (B, D, L): 2D maps, x = token, y = row
+// (b * D + d).  (B, L, D): 3D maps (channel, token, batch), so that a chunk
+// past the end of a sequence reads zeros instead of the next sequence.
+template <typename T, bool kBDL, bool kHasZ>
+__device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int chunk, int row0, int brow0, int crow0, int bb,
+                                            std::uint32_t c_bytes, const CUtensorMap* tu, const CUtensorMap* td,
+                                            const CUtensorMap* tz, const CUtensorMap* tb, const CUtensorMap* tc) {
     constexpr std::uint32_t tile = kLanes * kT * sizeof(T), btile = kN * kT * sizeof(T);
-    const std::uint32_t bytes = tile * (has_z ? 3u : 2u) + btile + static_cast<std::uint32_t>(cw) * kT * sizeof(T);
-    mbar_arrive_expect_tx(&sm.full[s], bytes);
-    const int x = chunk * kT;
-    tma_load_2d(sm.u[s], tu, &sm.full[s], x, row0);
-    tma_load_2d(sm.dl[s], td, &sm.full[s], x, row0);
-    if (has_z) tma_load_2d(sm.z[s], tz, &sm.full[s], x, row0);
-    tma_load_2d(sm.braw[s], tb, &sm.full[s], x, brow0);
-    tma_load_2d(sm.craw[s], tc, &sm.full[s], x, crow0);
+    mbar_arrive_expect_tx(&sm.full[s], tile * (kHasZ ? 3u : 2u) + btile + c_bytes);
+    const int t0 = chunk * kT;
+    if (kBDL) {
+        tma_load_2d(sm.u[s], tu, &sm.full[s], t0, row0);
+        tma_load_2d(sm.dl[s], td, &sm.full[s], t0, row0);
+        if constexpr (kHasZ) tma_load_2d(sm.z[s], tz, &sm.full[s], t0, row0);
+        tma_load_2d(sm.braw[s], tb, &sm.full[s], t0, brow0);
+        tma_load_2d(sm.craw[s], tc, &sm.full[s], t0, crow0);
+    } else {
+        tma_load_3d(sm.u[s], tu, &sm.full[s], row0, t0, bb);
+        tma_load_3d(sm.dl[s], td, &sm.full[s], row0, t0, bb);
+        if constexpr (kHasZ) tma_load_3d(sm.z[s], tz, &sm.full[s], row0, t0, bb);
+        tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
+        tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
+    }
 }
 
-template <typename T, int kPolyPairs>
-__global__ void __launch_bounds__(kLanes) bulk_bdl_kernel(const __grid_constant__ CUtensorMap tm_u,
-                                                          const __grid_constant__ CUtensorMap tm_d,
-                                                          const __grid_constant__ CUtensorMap tm_z,
-                                                          const __grid_constant__ CUtensorMap tm_b,
-                                                          const __grid_constant__ CUtensorMap tm_c,
-                                                          const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
+template <typename T, bool kBDL, bool kHasZ>
+__global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
+                                                                  const __grid_constant__ CUtensorMap tm_d,
+                                                                  const __grid_constant__ CUtensorMap tm_z,
+                                                                  const __grid_constant__ CUtensorMap tm_b,
+                                                                  const __grid_constant__ CUtensorMap tm_c,
+                                                                  const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
     extern __shared__ unsigned char smem_raw[];
-    Smem<T>& sm = *reinterpret_cast<Smem<T>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    auto& sm = *reinterpret_cast<Smem<T, kHasZ>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
     const int tid = threadIdx.x;
-    const unsigned long long D = p.channels;
-    const int row0 = blockIdx.x * kLanes; // first (batch * D + d) row of this CTA
-    const unsigned long long lane = static_cast<unsigned long long>(row0) + tid;
-    const unsigned long long b = static_cast<unsigned long long>(row0) / D, d = lane % D;
-    const unsigned long long g = (static_cast<unsigned long long>(row0) % D) / p.per_group;
+    const unsigned long long D = p.channels, L = p.length;
+    const unsigned long long tiles_per_row = D / kLanes;
+    const unsigned long long b = blockIdx.x / tiles_per_row;
+    const unsigned long long d0 = (blockIdx.x % tiles_per_row) * kLanes, d = d0 + tid;
+    const unsigned long long lane = b * D + d;
+    const unsigned long long g = d0 / p.per_group;
     const int cw = p.c_full ? kN : 1;
-    const int brow0 = static_cast<int>((b * p.groups + g) * kN);
-    const int crow0 = static_cast<int>((b * p.groups + g) * cw);
-    const bool has_z = p.has_z != 0;
+    // Tensor-map coordinates of this CTA.
+    const int row0 = kBDL ? static_cast<int>(b * D + d0) : static_cast<int>(d0);
+    const int bb = static_cast<int>(b);
+    const int brow0 = kBDL ? static_cast<int>((b * p.groups + g) * kN) : static_cast<int>(g * kN);
+    const int crow0 = kBDL ? static_cast<int>((b * p.groups + g) * cw) : static_cast<int>(g * cw);
+    const std::uint32_t c_bytes = static_cast<std::uint32_t>(cw) * kT * sizeof(T);
 
     if (tid == 0) {
         prefetch_tensor_map(&tm_u);
@@ -176,125 +236,109 @@ __global__ void __launch_bounds__(kLanes) bulk_bdl_kernel(const __grid_constant_
     __syncthreads();
     if (tid == 0)
         for (int s = 0; s < kStages && s < p.nchunks; ++s)
-            issue_chunk<T>(sm, s, s, row0, brow0, crow0, cw, has_z, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+            issue_chunk<T, kBDL, kHasZ>(sm, s, s, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
 
-    // Per-lane constants: A * log2(e) per state pair, D, dt bias, initial state.
-    float2 a2[kPairs], h[kPairs];
+    // Per-lane constants: A * log2(e), D, dt bias, initial state.
+    float a[kN], h[kN];
     const float* arow = p.a + (p.a_shared ? 0 : d * kN);
 #pragma unroll
-    for (int k = 0; k < kPairs; ++k) {
-        a2[k] = make_float2(arow[2 * k] * kLog2e, arow[2 * k + 1] * kLog2e);
-        h[k] = p.h0 ? make_float2(p.h0[lane * kN + 2 * k], p.h0[lane * kN + 2 * k + 1]) : make_float2(0.0f, 0.0f);
+    for (int n = 0; n < kN; ++n) {
+        a[n] = arow[n] * kLog2e;
+        h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
     }
     const float dskip = p.has_d ? p.d[d] : 0.0f;
     const float bias = p.bias ? p.bias[d] : 0.0f;
-    const int sw = (tid >> 1) & 3; // 64-byte swizzle: 16-byte chunk q of row r sits at q ^ ((r >> 1) & 3)
 
     bool fault = false;
     for (int chunk = 0; chunk < p.nchunks; ++chunk) {
         const int s = chunk % kStages;
         const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((chunk / kStages) & 1));
-        if (tid == 0) bulk_wait_read<1>(); // y tile (chunk & 1) no longer read by its previous store
+        if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
         if (!__syncthreads_and(ok)) {
             fault = true;
             break;
         }
-        // B / C tiles to FP32, token-major: 16 + (16 or 1) values per token.
-        {
-            const T* braw = sm.braw[s];
-            for (int i = tid; i < kN * kT; i += kLanes) {
-                const int n = i / kT, t = i % kT;
-                sm.bc[t][n] = scalar16(braw[i]);
+        // B / C tiles to an FP32 token-major table.
+        if (kBDL) {
+            // raw [state][token]: a thread takes 8 tokens of one state (16 bytes).
+            for (int i = tid; i < (kN + cw) * (kT / 8); i += kLanes) {
+                const int rowi = i / (kT / 8), t0 = (i % (kT / 8)) * 8;
+                const T* src = rowi < kN ? sm.braw[s] + rowi * kT + t0 : sm.craw[s] + (rowi - kN) * kT + t0;
+                const uint4 v = *reinterpret_cast<const uint4*>(src);
+                const std::uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = unpack2<T>(w[j]);
+                    sm.bc[t0 + 2 * j][rowi] = f.x;
+                    sm.bc[t0 + 2 * j + 1][rowi] = f.y;
+                }
             }
-            const T* craw = sm.craw[s];
-            for (int i = tid; i < cw * kT; i += kLanes) {
-                const int n = i / kT, t = i % kT;
-                sm.bc[t][kN + n] = scalar16(craw[i]);
-            }
+        } else {
+            // raw [token][state]: already token-major.
+            for (int i = tid; i < kN * kT; i += kLanes) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
+            for (int i = tid; i < cw * kT; i += kLanes) sm.bc[i / cw][kN + i % cw] = to_f32(sm.craw[s][i]);
         }
         __syncthreads();
 
         // Tokens past the end of the sequence (zero-filled by the TMA) are not
         // run through the recurrence; L is a multiple of 8.
-        const int valid = static_cast<int>(p.length - static_cast<unsigned long long>(chunk) * kT);
-        const int groups8 = (valid < kT ? valid : kT) / 8;
-        const T* urow = sm.u[s] + tid * kT;
-        const T* drow = sm.dl[s] + tid * kT;
-        const T* zrow = sm.z[s] + tid * kT;
-        T* yrow = sm.y[chunk & 1] + tid * kT;
+        const int valid = static_cast<int>(L - static_cast<unsigned long long>(chunk) * kT);
+        const int blocks8 = (valid < kT ? valid : kT) / 8;
 #pragma unroll 1
-        for (int q = 0; q < groups8; ++q) {
-            const int off = (q ^ sw) * 8;
-            const uint4 uq = *reinterpret_cast<const uint4*>(urow + off);
-            const uint4 xq = *reinterpret_cast<const uint4*>(drow + off);
-            uint4 zq = make_uint4(0, 0, 0, 0);
-            if (has_z) zq = *reinterpret_cast<const uint4*>(zrow + off);
-            const std::uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w}, xw[4] = {xq.x, xq.y, xq.z, xq.w},
-                                zw[4] = {zq.x, zq.y, zq.z, zq.w};
-            std::uint32_t yw[4];
+        for (int q = 0; q < blocks8; ++q) {
+            Block8 blk;
+            if (kBDL) load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+            else load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+            float out[8];
 #pragma unroll
-            for (int j2 = 0; j2 < 4; ++j2) {
-                const float2 u2 = unpack2<T>(uw[j2]), x2 = unpack2<T>(xw[j2]), z2 = unpack2<T>(zw[j2]);
-                float yv[2];
+            for (int j = 0; j < 8; ++j) {
+                const int t = q * 8 + j;
+                const float xv = blk.x[j] + bias;
+                const float dt = p.softplus ? softplus_bulk(xv) : xv;
+                const float du = dt * blk.u[j];
+                const float4* bcv = reinterpret_cast<const float4*>(sm.bc[t]);
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const float cr = sm.bc[t][kN];
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int t = q * 8 + j2 * 2 + e;
-                    const float uv = e ? u2.y : u2.x;
-                    const float xv = __fadd_rn(e ? x2.y : x2.x, bias);
-                    const float dt = p.softplus ? softplus_fast(xv) : xv;
-                    const float du = __fmul_rn(dt, uv);
-                    const float2 dt2 = make_float2(dt, dt), du2 = make_float2(du, du);
-                    const float4* bcv = reinterpret_cast<const float4*>(sm.bc[t]);
-                    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-                    const float cr = sm.bc[t][kN];
-#pragma unroll
-                    for (int k = 0; k < kPairs; ++k) {
-                        const float4 bq = bcv[k / 2];
-                        const float2 b2 = (k & 1) ? make_float2(bq.z, bq.w) : make_float2(bq.x, bq.y);
-                        float2 c2;
-                        if (p.c_full) {
-                            const float4 cq = bcv[4 + k / 2];
-                            c2 = (k & 1) ? make_float2(cq.z, cq.w) : make_float2(cq.x, cq.y);
-                        } else {
-                            c2 = make_float2(cr, cr);
-                        }
-                        const float2 arg = mul2(dt2, a2[k]);
-                        float2 dec;
-                        if (k >= kPairs - kPolyPairs) {
-                            dec = exp2_poly2(arg);
-                        } else {
-                            dec.x = fast_exp2(arg.x);
-                            dec.y = fast_exp2(arg.y);
-                        }
-                        const float2 drv = mul2(du2, b2);
-                        h[k] = fma2(dec, h[k], drv);
-                        if (k & 1) acc1 = fma2(c2, h[k], acc1);
-                        else acc0 = fma2(c2, h[k], acc0);
+                for (int k4 = 0; k4 < 4; ++k4) {
+                    const float4 bq = bcv[k4];
+                    const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
+                    float cc[4] = {cr, cr, cr, cr};
+                    if (p.c_full) {
+                        const float4 cq = bcv[4 + k4];
+                        cc[0] = cq.x; cc[1] = cq.y; cc[2] = cq.z; cc[3] = cq.w;
                     }
-                    const float2 accs = add2(acc0, acc1);
-                    float out = __fadd_rn(accs.x, accs.y);
-                    if (p.has_d) out = __fmaf_rn(dskip, uv, out);
-                    if (has_z) out = __fmul_rn(out, silu(e ? z2.y : z2.x));
-                    yv[e] = out;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int n = 4 * k4 + i;
+                        const float decay = fast_exp2(dt * a[n]);
+                        h[n] = fmaf(decay, h[n], du * bb[i]);
+                        acc[i] = fmaf(cc[i], h[n], acc[i]);
+                    }
                 }
-                yw[j2] = pack2<T>(yv[0], yv[1]);
+                float y = fmaf(dskip, blk.u[j], (acc[0] + acc[1]) + (acc[2] + acc[3]));
+                if constexpr (kHasZ) y *= silu(blk.z[j]);
+                out[j] = y;
             }
-            *reinterpret_cast<uint4*>(yrow + off) = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+            if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
+            else store_block_bld<T>(sm.y, tid, q, out);
         }
         fence_async_shared();
         __syncthreads();
         if (tid == 0) {
-            tma_store_2d(&tm_y, sm.y[chunk & 1], chunk * kT, row0);
+            if (kBDL) tma_store_2d(&tm_y, sm.y, chunk * kT, row0);
+            else tma_store_3d(&tm_y, sm.y, row0, chunk * kT, bb);
             bulk_commit();
             if (chunk + kStages < p.nchunks)
-                issue_chunk<T>(sm, s, chunk + kStages, row0, brow0, crow0, cw, has_z, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+                issue_chunk<T, kBDL, kHasZ>(sm, s, chunk + kStages, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z,
+                                            &tm_b, &tm_c);
         }
     }
     if (fault) {
         if (tid == 0) {
             atomicOr(&g_bulk_fault, 1u);
-            // Give copies still in flight a bounded chance to land before the CTA's
-            // shared memory is released.
+            // Give copies still in flight a bounded chance to land before the
+            // CTA's shared memory is released.
             for (int s = 0; s < kStages; ++s) (void)mbar_wait_bounded(&sm.full[s], 0u, 1u << 16);
         }
         return;
@@ -302,10 +346,7 @@ __global__ void __launch_bounds__(kLanes) bulk_bdl_kernel(const __grid_constant_
     if (tid == 0) bulk_wait<0>();
     if (p.h_final) {
 #pragma unroll
-        for (int k = 0; k < kPairs; ++k) {
-            p.h_final[lane * kN + 2 * k] = h[k].x;
-            p.h_final[lane * kN + 2 * k + 1] = h[k].y;
-        }
+        for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
     }
 }
 
@@ -324,6 +365,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// 3D map (inner, mid, outer) with a (box_inner, box_mid, 1) box, no swizzle.
+bool make_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, unsigned long long inner,
+                 unsigned long long mid, unsigned long long outer, unsigned box_inner, unsigned box_mid) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {inner, mid, outer};
+    const cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
+    const cuuint32_t box[3] = {box_inner, box_mid, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, unsigned long long inner,
                  unsigned long long rows, unsigned long long row_stride_bytes, unsigned box_inner, unsigned box_rows,
                  CUtensorMapSwizzle swizzle) {
@@ -337,84 +391,113 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr int kPoly = 2; // state pairs on the FMA-pipe exp2 (of 8)
+template <typename T, bool kBDL, bool kHasZ>
+struct Variant {
+    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ>); }
+    static cudaError_t prepare() {
+        static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                               static_cast<int>(smem_bytes<T, kHasZ>()));
+        return status;
+    }
+    static size_t smem() { return smem_bytes<T, kHasZ>(); }
+};
 
-template <typename T>
-const void* bulk_kernel_ptr() {
-    return reinterpret_cast<const void*>(bulk_bdl_kernel<T, kPoly>);
+struct Pick {
+    const void* fn;
+    size_t smem;
+    cudaError_t (*prepare)();
+};
+
+template <typename T, bool kBDL, bool kHasZ>
+Pick make_pick() {
+    return {Variant<T, kBDL, kHasZ>::fn(), Variant<T, kBDL, kHasZ>::smem(), &Variant<T, kBDL, kHasZ>::prepare};
 }
 
 template <typename T>
-cudaError_t ensure_smem_attr() {
-    static cudaError_t status = [] {
-        return cudaFuncSetAttribute(bulk_kernel_ptr<T>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(sizeof(Smem<T>) + 1024));
-    }();
-    return status;
+Pick pick_t(bool bdl, bool z) {
+    if (bdl) return z ? make_pick<T, true, true>() : make_pick<T, true, false>();
+    return z ? make_pick<T, false, true>() : make_pick<T, false, false>();
+}
+
+Pick pick(int dtype, bool bdl, bool z) {
+    return dtype == SACC_DTYPE_BF16 ? pick_t<__nv_bfloat16>(bdl, z) : pick_t<__half>(bdl, z);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
 } // namespace
 
-// The bulk kernel's domain: 16-bit (B, D, L) activations, N = 16, no varlen,
-// L a multiple of 8 (16-byte TMA row strides), 128-channel tiles inside one
-// group, 16-byte aligned tensors.  Other calls use the general kernel.
+// The bulk kernel's domain: 16-bit activations, N = 16, no varlen, channels
+// in 128-wide tiles inside one group, 16-byte aligned tensors and 16-byte row
+// strides for the TMA ((B, D, L): L % 8 == 0; (B, L, D): a full-width C, whose
+// rows are then 16 * groups * 2 bytes).  Other calls use the general kernel.
 bool bulk_eligible(const SaccScanExArgs& a) {
-    if (a.layout != SACC_LAYOUT_BDL || (a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) || a.state != kN ||
-        a.cu_seqlens != nullptr || a.length == 0 || a.length % 8 != 0 || a.channels % kLanes != 0 ||
-        (a.channels / a.groups) % kLanes != 0)
+    if ((a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) || a.state != kN || a.cu_seqlens != nullptr ||
+        a.length == 0 || a.groups == 0 || a.channels % kLanes != 0 || (a.channels / a.groups) % kLanes != 0)
         return false;
+    if (a.layout == SACC_LAYOUT_BDL) {
+        if (a.length % 8 != 0) return false;
+    } else if (a.layout == SACC_LAYOUT_BLD) {
+        if (a.c_width != kN || a.length % 8 != 0 || a.channels % 8 != 0) return false;
+    } else {
+        return false;
+    }
     for (const void* ptr : {a.u, a.delta, a.b, a.c, a.z, static_cast<const void*>(a.y)})
         if (ptr && !aligned16(ptr)) return false;
-    const unsigned long long rows = a.batch * a.channels;
-    return rows <= 0x7fffffffull && a.batch * a.groups * kN <= 0x7fffffffull && a.length <= 0x7fffffffull;
+    const unsigned long long rows = a.batch * a.channels, tokens = a.batch * a.length;
+    return rows <= 0x7fffffffull && tokens <= 0x7fffffffull && a.batch * a.groups * kN <= 0x7fffffffull;
 }
 
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream) {
-    const unsigned long long rows = a.batch * a.channels;
-    const unsigned long long cw = a.c_width;
+    const bool bdl = a.layout == SACC_LAYOUT_BDL;
+    const unsigned long long cw = a.c_width, B = a.batch, D = a.channels, L = a.length, G = a.groups;
     const CUtensorMapDataType dt = a.dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const unsigned long long stride = a.length * 2;
     CUtensorMap tu{}, td{}, tz{}, tb{}, tc{}, ty{};
-    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
-    if (!make_map_2d(&tu, dt, a.u, a.length, rows, stride, kT, kLanes, sw) ||
-        !make_map_2d(&td, dt, a.delta, a.length, rows, stride, kT, kLanes, sw) ||
-        !make_map_2d(&tz, dt, a.z ? a.z : a.u, a.length, rows, stride, kT, kLanes, sw) ||
-        !make_map_2d(&ty, dt, a.y, a.length, rows, stride, kT, kLanes, sw) ||
-        !make_map_2d(&tb, dt, a.b, a.length, a.batch * a.groups * kN, stride, kT, kN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&tc, dt, a.c, a.length, a.batch * a.groups * cw, stride, kT, static_cast<unsigned>(cw),
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue; // tensor-map encoding refused the (checked) layout
+    bool ok;
+    if (bdl) {
+        const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+        ok = make_map_2d(&tu, dt, a.u, L, B * D, L * 2, kT, kLanes, sw) &&
+             make_map_2d(&td, dt, a.delta, L, B * D, L * 2, kT, kLanes, sw) &&
+             make_map_2d(&tz, dt, a.z ? a.z : a.u, L, B * D, L * 2, kT, kLanes, sw) &&
+             make_map_2d(&ty, dt, a.y, L, B * D, L * 2, kT, kLanes, sw) &&
+             make_map_2d(&tb, dt, a.b, L, B * G * kN, L * 2, kT, kN, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             make_map_2d(&tc, dt, a.c, L, B * G * cw, L * 2, kT, static_cast<unsigned>(cw), CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        ok = make_map_3d(&tu, dt, a.u, D, L, B, kLanes, kT) && make_map_3d(&td, dt, a.delta, D, L, B, kLanes, kT) &&
+             make_map_3d(&tz, dt, a.z ? a.z : a.u, D, L, B, kLanes, kT) && make_map_3d(&ty, dt, a.y, D, L, B, kLanes, kT) &&
+             make_map_3d(&tb, dt, a.b, G * kN, L, B, kN, kT) &&
+             make_map_3d(&tc, dt, a.c, G * cw, L, B, static_cast<unsigned>(cw), kT);
+    }
+    if (!ok) return cudaErrorInvalidValue; // tensor-map encoding refused the (checked) layout
     BulkParams p{};
     p.a = a.a; p.d = a.d; p.bias = a.delta_bias; p.h0 = a.h0; p.h_final = a.h_final;
-    p.length = a.length; p.channels = a.channels; p.lanes = rows; p.per_group = a.channels / a.groups;
-    p.groups = static_cast<unsigned>(a.groups);
+    p.length = L; p.channels = D; p.per_group = D / G; p.groups = static_cast<unsigned>(G);
     p.a_shared = a.a_rows == 1; p.c_full = cw != 1; p.has_d = a.d != nullptr; p.softplus = a.delta_softplus != 0;
-    p.has_z = a.z != nullptr;
-    p.nchunks = static_cast<int>((a.length + kT - 1) / kT);
-    const bool bf16 = a.dtype == SACC_DTYPE_BF16;
-    const cudaError_t attr = bf16 ? ensure_smem_attr<__nv_bfloat16>() : ensure_smem_attr<__half>();
+    p.nchunks = static_cast<int>((L + kT - 1) / kT);
+    const Pick k = pick(a.dtype, bdl, a.z != nullptr);
+    const cudaError_t attr = k.prepare();
     if (attr != cudaSuccess) return attr;
-    const size_t smem = (bf16 ? sizeof(Smem<__nv_bfloat16>) : sizeof(Smem<__half>)) + 1024;
     void* args[] = {&tu, &td, &tz, &tb, &tc, &ty, &p};
-    return cudaLaunchKernel(bf16 ? bulk_kernel_ptr<__nv_bfloat16>() : bulk_kernel_ptr<__half>(),
-                            dim3(static_cast<unsigned>(rows / kLanes)), dim3(kLanes), args, smem, stream);
+    return cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(B * D / kLanes)), dim3(kLanes), args, k.smem, stream);
 }
 
 cudaError_t load_scan_bulk_kernels(std::string& report) {
-    for (const auto& k : {std::make_pair("scan_bulk_bdl_bf16", bulk_kernel_ptr<__nv_bfloat16>()),
-                          std::make_pair("scan_bulk_bdl_f16", bulk_kernel_ptr<__half>())}) {
-        cudaFuncAttributes attr{};
-        const cudaError_t e = cudaFuncGetAttributes(&attr, k.second);
-        if (e != cudaSuccess) return e;
-        report += std::string("kernel=") + k.first + " registers=" + std::to_string(attr.numRegs) +
-                  " local_bytes=" + std::to_string(attr.localSizeBytes) +
-                  " dynamic_shared_bytes=" + std::to_string(sizeof(Smem<__nv_bfloat16>) + 1024) + "\n";
-    }
-    cudaError_t e = ensure_smem_attr<__nv_bfloat16>();
-    if (e != cudaSuccess) return e;
-    return ensure_smem_attr<__half>();
+    const char* names[2] = {"bld", "bdl"};
+    for (int dtype : {SACC_DTYPE_BF16, SACC_DTYPE_F16})
+        for (int bdl = 0; bdl < 2; ++bdl)
+            for (int z = 0; z < 2; ++z) {
+                const Pick k = pick(dtype, bdl != 0, z != 0);
+                cudaFuncAttributes attr{};
+                cudaError_t e = cudaFuncGetAttributes(&attr, k.fn);
+                if (e != cudaSuccess) return e;
+                e = k.prepare();
+                if (e != cudaSuccess) return e;
+                report += std::string("kernel=scan_bulk_") + names[bdl] + (dtype == SACC_DTYPE_BF16 ? "_bf16" : "_f16") +
+                          (z ? "_gate" : "") + " registers=" + std::to_string(attr.numRegs) +
+                          " local_bytes=" + std::to_string(attr.localSizeBytes) +
+                          " dynamic_shared_bytes=" + std::to_string(k.smem) + "\n";
+            }
+    return cudaSuccess;
 }
 
 cudaError_t read_bulk_fault(unsigned* out, bool clear) {

@@ -55,6 +55,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, s
         : "memory");
 }
 
+// 3D tiled TMA load (x innermost, same alignment rule as the 2D form).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, std::uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 3D tiled TMA store from shared memory; elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 ::"l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(src))
+                 : "memory");
+}
+
 // 2D tiled TMA store from shared memory (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"

@@ -199,24 +199,26 @@ def test_rejections():
 # D a multiple of 128 (per group), L a multiple of 8.
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("layout", ["BDL", "BLD"])
 @pytest.mark.parametrize("case", [
     dict(B=2, L=96, D=256, G=1, c_full=True, use=("D", "z", "bias")),
-    dict(B=1, L=200, D=128, G=1, c_full=True, use=("D", "bias")),        # partial last chunk
+    dict(B=2, L=200, D=128, G=1, c_full=True, use=("D", "bias")),        # partial last chunk
     dict(B=2, L=64, D=256, G=2, c_full=False, use=("D", "z", "bias")),   # groups, rank-1 C
     dict(B=3, L=40, D=384, G=1, c_full=True, use=()),                    # no bias / D / gate
 ])
-def test_bulk_path_matches_oracle(dt, case):
-    t = make(21, case["B"], case["L"], case["D"], 16, case["G"], "BDL", dt, c_full=case["c_full"])
-    y, _ = gpu_run(t, dt, "BDL", use=case["use"])
-    ref, _, _ = oracle_run(t, "BDL", use=case["use"], groups=case["G"])
-    check_16bit(f"bulk_{dt}_{case}", y, ref)
+def test_bulk_path_matches_oracle(dt, layout, case):
+    t = make(21, case["B"], case["L"], case["D"], 16, case["G"], layout, dt, c_full=case["c_full"])
+    y, _ = gpu_run(t, dt, layout, use=case["use"])
+    ref, _, _ = oracle_run(t, layout, use=case["use"], groups=case["G"])
+    check_16bit(f"bulk_{dt}_{layout}_{case}", y, ref)
 
 
-def test_bulk_path_state_in_out():
-    t = make(22, 2, 72, 256, 16, 1, "BDL", "bf16")
+@pytest.mark.parametrize("layout", ["BDL", "BLD"])
+def test_bulk_path_state_in_out(layout):
+    t = make(22, 2, 72, 256, 16, 1, layout, "bf16")
     h0 = (np.random.default_rng(3).standard_normal((2, 256, 16)) * 0.5).astype(np.float32)
-    y, hf = gpu_run(t, "bf16", "BDL", h0=h0, want_final=True)
-    ref, hr, _ = oracle_run(t, "BDL", h0=h0, want_final=True)
+    y, hf = gpu_run(t, "bf16", layout, h0=h0, want_final=True)
+    ref, hr, _ = oracle_run(t, layout, h0=h0, want_final=True)
     check_16bit("bulk_state_y", y, ref)
     np.testing.assert_allclose(hf, hr, rtol=1e-3, atol=1e-3)
 

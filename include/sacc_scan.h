@@ -161,6 +161,31 @@ typedef struct SaccScanExArgs {
 
 int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Per-frame step (no counterpart in the reference): one token of every
+ * sequence advances carried FP32 state in place,
+ *   h[slot[i]] = exp(Delta_i A) h[slot[i]] + Delta_i B_i u_i,
+ *   y_i = (sum_n C_i,n h_n + D u_i) * silu(z_i).
+ * u, delta, z, y (nseq, channels); b (nseq, groups, state); c (nseq, groups,
+ * c_width); a (a_rows, state), d, delta_bias (channels) FP32.
+ * state: (slots, channels, state) FP32, 16-byte aligned, read and written.
+ * slot (optional, nseq int32): state row of sequence i (a tracker's slot);
+ * a negative slot skips the sequence and writes y_i = 0.  Without slot,
+ * sequence i uses row i and slots must equal nseq.  Two sequences must not
+ * name the same slot in one call.
+ * ------------------------------------------------------------------------ */
+typedef struct SaccScanStepArgs {
+    uint64_t nseq, channels, state, groups, a_rows, c_width, slots;
+    int32_t dtype, delta_softplus;
+    const void *u, *delta, *z, *b, *c; /* `dtype` */
+    const float *a, *d, *delta_bias;
+    float* state_io;
+    const int32_t* slot;
+    void* y;
+} SaccScanStepArgs;
+
+int sacc_selective_scan_step(const SaccScanStepArgs* args, cudaStream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -16,4 +16,5 @@ from .scan import (  # noqa: F401
     load_kernels,
     selective_scan_cuda,
     selective_scan_ex,
+    selective_scan_step,
 )

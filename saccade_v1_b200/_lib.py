@@ -27,6 +27,7 @@ EXPORTS = (
     "sacc_scan_identity",
     "sacc_selective_scan_ex",
     "sacc_scan_fault",
+    "sacc_selective_scan_step",
 )
 
 
@@ -53,6 +54,15 @@ class ScanExArgs(ctypes.Structure):
                 ("z", ctypes.c_void_p), ("a", ctypes.c_void_p), ("d", ctypes.c_void_p),
                 ("delta_bias", ctypes.c_void_p), ("h0", ctypes.c_void_p), ("h_final", ctypes.c_void_p),
                 ("cu_seqlens", ctypes.c_void_p), ("y", ctypes.c_void_p)]
+
+
+class ScanStepArgs(ctypes.Structure):
+    _fields_ = [("nseq", ctypes.c_uint64), ("channels", ctypes.c_uint64), ("state", ctypes.c_uint64),
+                ("groups", ctypes.c_uint64), ("a_rows", ctypes.c_uint64), ("c_width", ctypes.c_uint64),
+                ("slots", ctypes.c_uint64), ("dtype", ctypes.c_int32), ("delta_softplus", ctypes.c_int32),
+                ("u", ctypes.c_void_p), ("delta", ctypes.c_void_p), ("z", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("c", ctypes.c_void_p), ("a", ctypes.c_void_p), ("d", ctypes.c_void_p), ("delta_bias", ctypes.c_void_p),
+                ("state_io", ctypes.c_void_p), ("slot", ctypes.c_void_p), ("y", ctypes.c_void_p)]
 
 
 _lib = None
@@ -84,6 +94,8 @@ def load() -> ctypes.CDLL:
     L.sacc_selective_scan_ex.restype = i
     L.sacc_scan_fault.argtypes = [ctypes.POINTER(ctypes.c_uint32), i]
     L.sacc_scan_fault.restype = i
+    L.sacc_selective_scan_step.argtypes = [ctypes.POINTER(ScanStepArgs), vp]
+    L.sacc_selective_scan_step.restype = i
     _lib = L
     return L
 

@@ -151,6 +151,7 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
         CK(load_scan_f32_kernels(text));
         CK(load_cross_kernels(text));
         CK(load_scan_ex_kernels(text));
+        CK(load_scan_step_kernels(text));
         (void)sm_count();
         if (report && report_bytes) {
             std::snprintf(report, report_bytes, "%s", text.c_str());
@@ -305,6 +306,53 @@ int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream) {
             if (overlaps(hr, yr)) reject(api, "h_final overlaps y");
         }
         CK(launch_scan_ex(a, sm_count(), stream));
+    });
+}
+
+int sacc_selective_scan_step(const SaccScanStepArgs* args, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "selective_scan_step";
+        if (args == nullptr) reject(api, "args are required");
+        const SaccScanStepArgs& a = *args;
+        require_stream(api, stream);
+        if (a.dtype != SACC_DTYPE_F32 && a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16)
+            reject(api, "dtype must be f32, bf16 or f16");
+        if (a.channels == 0) reject(api, "channels must be positive");
+        if (a.state == 0 || a.state > 32 || (a.state & (a.state - 1)) != 0)
+            reject(api, "state " + std::to_string(a.state) + " must be a power of two in [1, 32]");
+        if (a.groups == 0 || a.channels % a.groups != 0) reject(api, "groups must divide channels");
+        if (a.a_rows != 1 && a.a_rows != a.channels) reject(api, "A rows must be 1 or channels");
+        if (a.c_width != 1 && a.c_width != a.state) reject(api, "C width must be 1 or state");
+        const std::uint64_t slots = a.slot ? a.slots : a.nseq;
+        if (!a.slot && a.slots != 0 && a.slots != a.nseq) reject(api, "slots must equal nseq without a slot map");
+        const auto ud = elements(api, {a.nseq, a.channels}, "u/delta/y");
+        const auto bn = elements(api, {a.nseq, a.groups, a.state}, "B");
+        const auto cn = elements(api, {a.nseq, a.groups, a.c_width}, "C");
+        const auto an = elements(api, {a.a_rows, a.state}, "A");
+        const auto sn = elements(api, {slots, a.channels, a.state}, "state");
+        const std::size_t e = dtype_bytes(a.dtype), f = sizeof(float), align = a.dtype == SACC_DTYPE_F32 ? 4 : 2;
+        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}, Region{a.y, ud * e, "y"}})
+            require_pointer(api, r, align);
+        for (const Region& r : {Region{a.a, an * f, "A"}, Region{a.d, a.d ? a.channels * f : 0, "D"},
+                                Region{a.delta_bias, a.delta_bias ? a.channels * f : 0, "delta_bias"},
+                                Region{a.slot, a.slot ? a.nseq * sizeof(std::int32_t) : 0, "slot"}})
+            require_pointer(api, r);
+        require_pointer(api, Region{a.state_io, sn * f, "state"}, a.state >= 4 ? 16 : 4);
+        if (ud == 0) return;
+        if (a.u == nullptr || a.delta == nullptr || a.a == nullptr || a.y == nullptr || a.b == nullptr ||
+            a.c == nullptr || a.state_io == nullptr)
+            reject(api, "u, delta, A, B, C, state and y are required");
+        const Region yr{a.y, ud * e, "y"}, sr{a.state_io, sn * f, "state"};
+        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}}) {
+            if (overlaps(yr, r)) reject(api, std::string("y overlaps ") + r.name);
+            if (overlaps(sr, r)) reject(api, std::string("state overlaps ") + r.name);
+        }
+        if (overlaps(sr, yr)) reject(api, "state overlaps y");
+        SaccScanStepArgs fixed = a;
+        fixed.slots = slots;
+        CK(launch_scan_step(fixed, stream));
     });
 }
 

@@ -55,6 +55,8 @@ cudaError_t launch_scan_ex(const SaccScanExArgs& a, int sm_count, cudaStream_t s
 cudaError_t launch_scan_general(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_general_kernels(std::string& report);
 bool bulk_eligible(const SaccScanExArgs& a);
+cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream);
+cudaError_t load_scan_step_kernels(std::string& report);
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).

@@ -200,7 +200,7 @@ __device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int chunk
     }
 }
 
-template <typename T, bool kBDL, bool kHasZ>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC>
 __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
                                                                   const __grid_constant__ CUtensorMap tm_d,
                                                                   const __grid_constant__ CUtensorMap tm_z,
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     const unsigned long long d0 = (blockIdx.x % tiles_per_row) * kLanes, d = d0 + tid;
     const unsigned long long lane = b * D + d;
     const unsigned long long g = d0 / p.per_group;
-    const int cw = p.c_full ? kN : 1;
+    const int cw = kFullC ? kN : 1;
     // Tensor-map coordinates of this CTA.
     const int row0 = kBDL ? static_cast<int>(b * D + d0) : static_cast<int>(d0);
     const int bb = static_cast<int>(b);
@@ -298,13 +298,13 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                 const float du = dt * blk.u[j];
                 const float4* bcv = reinterpret_cast<const float4*>(sm.bc[t]);
                 float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const float cr = sm.bc[t][kN];
+                const float cr = kFullC ? 0.0f : sm.bc[t][kN];
 #pragma unroll
                 for (int k4 = 0; k4 < 4; ++k4) {
                     const float4 bq = bcv[k4];
                     const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
                     float cc[4] = {cr, cr, cr, cr};
-                    if (p.c_full) {
+                    if constexpr (kFullC) {
                         const float4 cq = bcv[4 + k4];
                         cc[0] = cq.x; cc[1] = cq.y; cc[2] = cq.z; cc[3] = cq.w;
                     }
@@ -391,9 +391,9 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, bool kBDL, bool kHasZ>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC>
 struct Variant {
-    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ>); }
+    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC>); }
     static cudaError_t prepare() {
         static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                                static_cast<int>(smem_bytes<T, kHasZ>()));
@@ -408,19 +408,21 @@ struct Pick {
     cudaError_t (*prepare)();
 };
 
-template <typename T, bool kBDL, bool kHasZ>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC>
 Pick make_pick() {
-    return {Variant<T, kBDL, kHasZ>::fn(), Variant<T, kBDL, kHasZ>::smem(), &Variant<T, kBDL, kHasZ>::prepare};
+    using V = Variant<T, kBDL, kHasZ, kFullC>;
+    return {V::fn(), V::smem(), &V::prepare};
 }
 
-template <typename T>
-Pick pick_t(bool bdl, bool z) {
-    if (bdl) return z ? make_pick<T, true, true>() : make_pick<T, true, false>();
-    return z ? make_pick<T, false, true>() : make_pick<T, false, false>();
+template <typename T, bool kBDL>
+Pick pick_z(bool z, bool full_c) {
+    if (z) return full_c ? make_pick<T, kBDL, true, true>() : make_pick<T, kBDL, true, false>();
+    return full_c ? make_pick<T, kBDL, false, true>() : make_pick<T, kBDL, false, false>();
 }
 
-Pick pick(int dtype, bool bdl, bool z) {
-    return dtype == SACC_DTYPE_BF16 ? pick_t<__nv_bfloat16>(bdl, z) : pick_t<__half>(bdl, z);
+Pick pick(int dtype, bool bdl, bool z, bool full_c) {
+    if (dtype == SACC_DTYPE_BF16) return bdl ? pick_z<__nv_bfloat16, true>(z, full_c) : pick_z<__nv_bfloat16, false>(z, full_c);
+    return bdl ? pick_z<__half, true>(z, full_c) : pick_z<__half, false>(z, full_c);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
@@ -474,7 +476,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream) {
     p.length = L; p.channels = D; p.per_group = D / G; p.groups = static_cast<unsigned>(G);
     p.a_shared = a.a_rows == 1; p.c_full = cw != 1; p.has_d = a.d != nullptr; p.softplus = a.delta_softplus != 0;
     p.nchunks = static_cast<int>((L + kT - 1) / kT);
-    const Pick k = pick(a.dtype, bdl, a.z != nullptr);
+    const Pick k = pick(a.dtype, bdl, a.z != nullptr, cw != 1);
     const cudaError_t attr = k.prepare();
     if (attr != cudaSuccess) return attr;
     void* args[] = {&tu, &td, &tz, &tb, &tc, &ty, &p};
@@ -485,15 +487,16 @@ cudaError_t load_scan_bulk_kernels(std::string& report) {
     const char* names[2] = {"bld", "bdl"};
     for (int dtype : {SACC_DTYPE_BF16, SACC_DTYPE_F16})
         for (int bdl = 0; bdl < 2; ++bdl)
-            for (int z = 0; z < 2; ++z) {
-                const Pick k = pick(dtype, bdl != 0, z != 0);
+            for (int z = 0; z < 4; ++z) {
+                if (!bdl && (z & 2) == 0) continue; // (B, L, D) always has a full-width C
+                const Pick k = pick(dtype, bdl != 0, (z & 1) != 0, (z & 2) != 0);
                 cudaFuncAttributes attr{};
                 cudaError_t e = cudaFuncGetAttributes(&attr, k.fn);
                 if (e != cudaSuccess) return e;
                 e = k.prepare();
                 if (e != cudaSuccess) return e;
                 report += std::string("kernel=scan_bulk_") + names[bdl] + (dtype == SACC_DTYPE_BF16 ? "_bf16" : "_f16") +
-                          (z ? "_gate" : "") + " registers=" + std::to_string(attr.numRegs) +
+                          ((z & 1) ? "_gate" : "") + ((z & 2) ? "" : "_rank1c") + " registers=" + std::to_string(attr.numRegs) +
                           " local_bytes=" + std::to_string(attr.localSizeBytes) +
                           " dynamic_shared_bytes=" + std::to_string(k.smem) + "\n";
             }

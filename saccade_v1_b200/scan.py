@@ -166,3 +166,30 @@ def selective_scan_ex(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, del
                            _ptr(h0), _ptr(h_final), _ptr(cu_seqlens), _ptr(out))
     _check(_lib.load().sacc_selective_scan_ex(ctypes.byref(args), _stream_handle(stream)))
     return out
+
+
+def selective_scan_step(u, delta, A, B, C, state, D=None, z=None, delta_bias=None, *, slot=None,
+                        delta_softplus: bool = True, out=None, stream=None):
+    """One L = 1 update of carried state, in place; returns y.
+
+    u, delta, z: (nseq, D); B, C: (nseq, N|1) or (nseq, groups, N|1) in u's dtype;
+    state: (slots, D, N) float32, updated in place; slot: optional int32 (nseq)
+    mapping each sequence to its state row (negative = skip, y = 0).
+    """
+    if u.dtype not in _DTYPES:
+        raise ScanInvalidArgument("selective_scan_step: dtype must be f32, bf16 or f16")
+    nseq, dim = u.shape
+    if B.dim() == 2:
+        B, C = B.unsqueeze(1), C.unsqueeze(1)
+    groups, nstate, c_width = B.shape[1], B.shape[2], C.shape[2]
+    for name, t in (("u", u), ("delta", delta), ("B", B), ("C", C), ("z", z), ("state", state), ("slot", slot)):
+        if t is not None and not t.is_contiguous():
+            raise ScanInvalidArgument(f"selective_scan_step: {name} must be contiguous")
+    if out is None:
+        out = torch.empty_like(u)
+    args = _lib.ScanStepArgs(nseq, dim, nstate, groups, A.shape[0] if A.dim() == 2 else 1, c_width,
+                             state.shape[0], _DTYPES[u.dtype], int(delta_softplus),
+                             _ptr(u), _ptr(delta), _ptr(z), _ptr(B), _ptr(C), _ptr(A), _ptr(D), _ptr(delta_bias),
+                             _ptr(state), _ptr(slot), _ptr(out))
+    _check(_lib.load().sacc_selective_scan_step(ctypes.byref(args), _stream_handle(stream)))
+    return out

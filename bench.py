@@ -307,6 +307,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     achieved = nbytes / (kernel_ms / 1e3) / 1e9
     cpu = cpu_baseline(args) if world == 1 and not args.no_cpu_baseline else None
+    extra = secondary(torch, device, stream, peaks()[0]) if not args.no_secondary else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
@@ -324,8 +325,93 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clocks.summary(),
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
+        "secondary": extra,
     }
     return line
+
+
+def time_device(torch, stream, fn, iters: int, warmup: int = 3) -> float:
+    """Mean device time of fn() in microseconds, CUDA events on `stream`."""
+    for _ in range(warmup):
+        fn()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / iters
+
+
+def secondary(torch, device, stream, peak):
+    """Other rows of the hot path, device-timed on this GPU (not part of `value`)."""
+    import saccade_v1_b200 as sb
+    out = {}
+    g = torch.Generator(device=device)
+    g.manual_seed(77)
+    with torch.cuda.stream(stream):
+        # Config 3: one per-frame L = 1 step of 4096 tracks' carried state (256 x 16 FP32 each), fp16 activations.
+        T3, D3, N3 = 4096, 256, 16
+        f16 = torch.float16
+        u = torch.randn(T3, D3, device=device, generator=g).to(f16)
+        dl = torch.randn(T3, D3, device=device, generator=g).to(f16)
+        z = torch.randn(T3, D3, device=device, generator=g).to(f16)
+        bm = torch.randn(T3, N3, device=device, generator=g).to(f16)
+        cm = torch.randn(T3, N3, device=device, generator=g).to(f16)
+        A = -torch.arange(1, N3 + 1, dtype=torch.float32, device=device).repeat(D3, 1).contiguous()
+        Dv = torch.ones(D3, device=device)
+        bias = torch.full((D3,), -4.6, device=device)
+        state = torch.randn(T3, D3, N3, device=device, generator=g) * 0.5
+        y = torch.empty_like(u)
+        step = lambda: sb.selective_scan_step(u, dl, A, bm, cm, state, D=Dv, z=z, delta_bias=bias, out=y, stream=stream)
+        us = time_device(torch, stream, step, 50)
+        nbytes = 2 * state.numel() * 4 + 4 * u.numel() * 2 + 2 * bm.numel() * 2 + 4 * (A.numel() + 2 * D3)
+        out["c3_step"] = {"us": round(us, 2), "tracks_frames_per_s": round(T3 / (us * 1e-6), 1),
+                          "GB_per_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+                          "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4), "bytes": nbytes,
+                          "workload": "4096 tracks, D=256, N=16, fp16 acts, fp32 carried state, gate+bias+D"}
+        # Config 3: full packed re-scan of the histories (lengths U{1..64}) with cu_seqlens.
+        rng = np.random.default_rng(3)
+        lens = rng.integers(1, 65, T3)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=device)
+        tot = int(lens.sum())
+        ur = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
+        dr = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
+        zr = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
+        br = torch.randn(1, tot, 1, N3, device=device, generator=g).to(f16)
+        cr = torch.randn(1, tot, 1, N3, device=device, generator=g).to(f16)
+        yr = torch.empty_like(ur)
+        hr = torch.empty(T3, D3, N3, device=device)
+        rescan = lambda: sb.selective_scan_ex(ur, dr, A, br, cr, D=Dv, z=zr, delta_bias=bias, h0=state, h_final=hr,
+                                              cu_seqlens=cu, layout="BLD", out=yr, stream=stream)
+        us_r = time_device(torch, stream, rescan, 10)
+        out["c3_rescan"] = {"us": round(us_r, 2), "tokens": tot,
+                            "workload": "4096 packed histories, lengths U{1..64}, BLD fp16, h0 -> h_final"}
+        out["c3_frame_avg_us"] = round(us + us_r / 30.0, 2)
+        out["c3_tracks_frames_per_s"] = round(T3 / ((us + us_r / 30.0) * 1e-6), 1)
+        # Reference ABI at the HR deploy shapes (4 directions x L tokens x 256 channels, N = 16, FP32,
+        # shared A, rank-1 C, D): the reference's published 3-level total is 722.351 us (RTX 5070 Ti laptop).
+        levels = {}
+        st = torch.zeros(2, dtype=torch.int32, device=device)
+        calls = []
+        for L_ in (960, 240, 60):
+            shape = sb.SelectiveScanShape(4, L_, 256, 16, 1, 1, True)
+            uu = torch.randn(4 * L_ * 256, device=device, generator=g) * 2
+            dd = torch.rand(4 * L_ * 256, device=device, generator=g) * 9 - 6
+            aa = -torch.rand(16, device=device, generator=g) * 3.95 - 0.05
+            bb = torch.randn(4 * L_ * 16, device=device, generator=g)
+            cc = torch.randn(4 * L_, device=device, generator=g)
+            dv = torch.randn(256, device=device, generator=g)
+            yy = torch.empty_like(uu)
+            call = (lambda s_=shape, a_=(uu, dd, aa, bb, cc, dv, yy): sb.selective_scan_cuda(s_, *a_, st, stream=stream))
+            levels[f"HR_L{L_}"] = round(time_device(torch, stream, call, 50), 2)
+            calls.append(call)
+        total = time_device(torch, stream, lambda: [c() for c in calls], 50)
+        out["hr_deploy_f32_us"] = dict(levels, total=round(total, 2), reference_published_total_us=722.351,
+                                       note="reference figure is its own CUDA kernel on an RTX 5070 Ti laptop GPU")
+    stream.synchronize()
+    return out
 
 
 def reference_sample(threads: int):
@@ -408,6 +494,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -82,6 +82,8 @@ def test_steps_chain_into_a_scan():
     """T single-token steps from h0 == one T-token scan from h0 (carried state)."""
     T, nseq, D, N = 6, 16, 128, 16
     ts = [make(100 + k, nseq, D, N, "f16") for k in range(T)]
+    for t in ts[1:]:  # per-channel parameters are fixed across frames
+        t["bias"] = ts[0]["bias"]
     h0 = ts[0]["h0"]
     state = torch.from_numpy(h0.copy()).cuda()
     ys = [gpu_step(t, "f16", state) for t in ts]

@@ -269,6 +269,35 @@ def run_ours(args, rank, world, local_rank):
     kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
     kernel_ms = max_over_ranks(kernel_ms)
 
+    # Output assembly (N > 1): scan + NCCL all-gather of every rank's y into
+    # the full (N x 64)-sequence output on every rank; not part of `value`.
+    gather = None
+    if world > 1:
+        from saccade_v1_b200.shard import gather_batch, shard_rows
+        shard = shard_rows(args.batch * world, world, rank)
+        gsteps = 5
+
+        def gather_step():
+            step()
+            return gather_batch(y, shard, args.batch * world)
+
+        with torch.cuda.stream(stream):
+            gather_step()
+        torch.cuda.synchronize(device)
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            g0.record(stream)
+            for _ in range(gsteps):
+                gather_step()
+            g1.record(stream)
+        g1.synchronize()
+        barrier()
+        gms = max_over_ranks(g0.elapsed_time(g1)) / gsteps
+        gather = {"ms_per_step": round(gms, 4), "value": round(algorithmic_bytes(batch=args.batch) * world / (gms / 1e3) / 1e9, 2),
+                  "unit": UNIT, "collective": "NCCL all_gather_into_tensor of y (bf16) over NVLink",
+                  "gathered_bytes_per_rank": y.numel() * y.element_size() * world}
+
     # End to end through the public API: H2D of the step's inputs from pinned
     # host memory, the scan, D2H of y, all inside the timed region.
     host = {k: t[k].cpu().pin_memory() for k in ("u", "delta", "B", "C")}
@@ -326,6 +355,7 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
         "secondary": extra,
+        "with_allgather": gather,
     }
     return line
 

@@ -79,3 +79,29 @@ def test_pointer_rules_without_gpu():
     for ins, y, status, diag in cases:
         rc = L.sacc_selective_scan_f32(ctypes.byref(shape.c()), ctypes.byref(ins), y, status, FAKE_STREAM)
         assert rc == _lib.SACC_EINVAL and diag in _lib.last_error(), _lib.last_error()
+
+
+def test_cpp_adapter_compiles_and_links(tmp_path):
+    """include/sacc_scan.hpp gives reference-signature C++ (selective_scan_cuda etc.) over the C ABI."""
+    import shutil
+    import subprocess
+    src = tmp_path / "adapter.cpp"
+    src.write_text(
+        '#include "sacc_scan.hpp"\n'
+        "int main() {\n"
+        "  saccade::SelectiveScanShape s{4, 960, 256, 16, 1, 1, true};\n"
+        "  saccade::SelectiveScanDeviceInputs in{};\n"
+        "  try { saccade::selective_scan_cuda(s, in, nullptr, nullptr, nullptr); }\n"
+        "  catch (const std::invalid_argument& e) {\n"
+        "    return std::string(e.what()).find(\"explicit non-default stream\") == std::string::npos; }\n"
+        "  return 2;\n"
+        "}\n")
+    exe = tmp_path / "adapter"
+    cuda_inc = "/usr/local/cuda/include"
+    cxx = shutil.which("g++")
+    assert cxx
+    lib_dir = os.path.join(ROOT, "saccade_v1_b200")
+    subprocess.run([cxx, "-std=c++17", "-I", os.path.join(ROOT, "include"), "-I", cuda_inc, str(src), "-o", str(exe),
+                    "-L", lib_dir, "-lsacc_scan", "-Wl,-rpath," + lib_dir], check=True)
+    # Host rejection of the default stream happens before any CUDA call: runs without a GPU.
+    assert subprocess.run([str(exe)]).returncode == 0

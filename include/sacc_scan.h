@@ -186,6 +186,27 @@ typedef struct SaccScanStepArgs {
 
 int sacc_selective_scan_step(const SaccScanStepArgs* args, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Projection GEMM on the tensor cores (no counterpart in the reference, whose
+ * projections are TensorRT matrix-multiply layers, src/head_trt_network.cpp:
+ * 192-230): C[m, n] = sum_k A[m, k] B[n, k] (+ bias[n]) (+ R[m, n]).
+ * A (m x k, row stride lda) and B (n x k, row stride ldb) are bf16 or fp16
+ * (in_dtype), K contiguous, 16-byte aligned, lda and ldb multiples of 8;
+ * C and R are out_dtype (f32, bf16, f16) with row strides ldc / ldr; bias FP32.
+ * FP32 accumulation in tensor memory.
+ * ------------------------------------------------------------------------ */
+typedef struct SaccGemmArgs {
+    uint64_t m, n, k, lda, ldb, ldc, ldr;
+    int32_t in_dtype, out_dtype;
+    const void* a;
+    const void* b;
+    void* c;
+    const float* bias;    /* optional (n) */
+    const void* residual; /* optional (m x n, ldr) */
+} SaccGemmArgs;
+
+int sacc_gemm(const SaccGemmArgs* args, cudaStream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

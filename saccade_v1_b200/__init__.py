@@ -12,8 +12,10 @@ from .scan import (  # noqa: F401
     SCAN_DONE,
     cross_scan_expand_cuda,
     cross_scan_merge_cuda,
+    gemm,
     identity,
     load_kernels,
+    scan_fault,
     selective_scan_cuda,
     selective_scan_ex,
     selective_scan_step,

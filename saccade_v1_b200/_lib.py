@@ -28,6 +28,7 @@ EXPORTS = (
     "sacc_selective_scan_ex",
     "sacc_scan_fault",
     "sacc_selective_scan_step",
+    "sacc_gemm",
 )
 
 
@@ -65,6 +66,13 @@ class ScanStepArgs(ctypes.Structure):
                 ("state_io", ctypes.c_void_p), ("slot", ctypes.c_void_p), ("y", ctypes.c_void_p)]
 
 
+class GemmArgs(ctypes.Structure):
+    _fields_ = [("m", ctypes.c_uint64), ("n", ctypes.c_uint64), ("k", ctypes.c_uint64), ("lda", ctypes.c_uint64),
+                ("ldb", ctypes.c_uint64), ("ldc", ctypes.c_uint64), ("ldr", ctypes.c_uint64),
+                ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("a", ctypes.c_void_p),
+                ("b", ctypes.c_void_p), ("c", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p)]
+
+
 _lib = None
 
 
@@ -96,6 +104,8 @@ def load() -> ctypes.CDLL:
     L.sacc_scan_fault.restype = i
     L.sacc_selective_scan_step.argtypes = [ctypes.POINTER(ScanStepArgs), vp]
     L.sacc_selective_scan_step.restype = i
+    L.sacc_gemm.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    L.sacc_gemm.restype = i
     _lib = L
     return L
 

@@ -152,6 +152,7 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
         CK(load_cross_kernels(text));
         CK(load_scan_ex_kernels(text));
         CK(load_scan_step_kernels(text));
+        CK(load_gemm_kernels(text));
         (void)sm_count();
         if (report && report_bytes) {
             std::snprintf(report, report_bytes, "%s", text.c_str());
@@ -251,9 +252,10 @@ int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, f
 int sacc_scan_fault(uint32_t* out, int clear) {
     return guarded([&] {
         if (out == nullptr) reject("sacc_scan_fault", "out is required");
-        unsigned v = 0;
-        CK(read_bulk_fault(&v, clear != 0));
-        *out = v;
+        unsigned scan = 0, gemm = 0;
+        CK(read_bulk_fault(&scan, clear != 0));
+        CK(read_gemm_fault(&gemm, clear != 0));
+        *out = (scan ? 1u : 0u) | (gemm ? 2u : 0u);
     });
 }
 
@@ -353,6 +355,33 @@ int sacc_selective_scan_step(const SaccScanStepArgs* args, cudaStream_t stream) 
         SaccScanStepArgs fixed = a;
         fixed.slots = slots;
         CK(launch_scan_step(fixed, stream));
+    });
+}
+
+int sacc_gemm(const SaccGemmArgs* args, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "gemm";
+        if (args == nullptr) reject(api, "args are required");
+        const SaccGemmArgs& a = *args;
+        require_stream(api, stream);
+        if (a.in_dtype != SACC_DTYPE_BF16 && a.in_dtype != SACC_DTYPE_F16) reject(api, "in_dtype must be bf16 or f16");
+        if (a.out_dtype != SACC_DTYPE_F32 && a.out_dtype != SACC_DTYPE_BF16 && a.out_dtype != SACC_DTYPE_F16)
+            reject(api, "out_dtype must be f32, bf16 or f16");
+        if (a.m == 0 || a.n == 0 || a.k == 0) reject(api, "m, n and k must be positive");
+        if (a.lda < a.k || a.ldb < a.k || a.ldc < a.n || (a.residual && a.ldr < a.n)) reject(api, "leading dimensions too small");
+        if (a.lda % 8 != 0 || a.ldb % 8 != 0) reject(api, "lda and ldb must be multiples of 8 (16-byte rows)");
+        if (a.m > 0x7fffffffull || a.n > 0x7fffffffull || a.k > 0x7fffffffull) reject(api, "dimensions exceed int32");
+        const std::size_t eo = dtype_bytes(a.out_dtype);
+        const Region ar{a.a, ((a.m - 1) * a.lda + a.k) * 2, "A"}, br{a.b, ((a.n - 1) * a.ldb + a.k) * 2, "B"};
+        const Region cr{a.c, ((a.m - 1) * a.ldc + a.n) * eo, "C"};
+        require_pointer(api, ar, 16);
+        require_pointer(api, br, 16);
+        require_pointer(api, cr, eo);
+        require_pointer(api, Region{a.bias, a.bias ? a.n * sizeof(float) : 0, "bias"});
+        const Region rr{a.residual, a.residual ? ((a.m - 1) * a.ldr + a.n) * eo : 0, "residual"};
+        require_pointer(api, rr, eo);
+        if (overlaps(cr, ar) || overlaps(cr, br)) reject(api, "C overlaps an operand");
+        CK(launch_gemm(a, stream));
     });
 }
 

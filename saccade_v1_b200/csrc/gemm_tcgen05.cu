@@ -1,0 +1,312 @@
+// gemm_tcgen05.cu -- C = A B^T (+ bias, + residual) on the sm_100a tensor cores.
+//
+// The dense projections around the scan (in_proj, x_proj, out_proj of the
+// Mamba block, reference src/head_trt_network.cpp:192-230) are GEMMs of
+// token rows A (M x K, K contiguous) with weight rows B (N x K, K contiguous).
+//
+// One CTA computes a 128 x BN tile of C with a 128 x BN FP32 accumulator in
+// tensor memory (TMEM):
+//   warp 0      TMA producer: 128 x 64 A and BN x 64 B bf16/fp16 tiles with
+//               128-byte swizzle into a 4-stage ring (full / empty mbarriers);
+//   warp 1      allocates TMEM, and one elected thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN, K = 16)
+//               four times per stage from shared-memory descriptors, then
+//               tcgen05.commit to free the stage and, at the end, to signal
+//               the epilogue;
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, bias,
+//               residual, conversion, bounds-checked stores.
+// No multicast, no clusters.  Every mbarrier wait has an iteration limit and
+// sets the library fault word when it runs out.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+#include "scan_common.cuh"
+#include "tma.cuh"
+
+namespace sacc {
+
+__device__ unsigned int g_gemm_fault; // set when a bounded wait ran out; read by sacc_scan_fault()
+
+namespace {
+
+constexpr int kBM = 128, kBK = 64, kStages = 4;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmSmem {
+    alignas(1024) std::uint16_t a[kStages][kBM * kBK];
+    alignas(1024) std::uint16_t b[kStages][BN * kBK];
+    alignas(8) std::uint64_t full[kStages];
+    alignas(8) std::uint64_t empty[kStages];
+    alignas(8) std::uint64_t accum;
+    std::uint32_t tmem_base;
+};
+
+struct GemmParams {
+    void* c;
+    const void* residual;
+    const float* bias;
+    unsigned long long m, n, k, ldc, ldr;
+    int out_dtype, in_dtype, kblocks;
+};
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with the
+// 128-byte swizzle: rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart
+// (stride byte offset), leading byte offset unused for swizzled K-major (1),
+// descriptor version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ std::uint64_t sw128_desc(const void* tile) {
+    const std::uint64_t addr = smem_addr(tile);
+    return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: FP32 accumulate, A/B format (0 = f16, 1 = bf16),
+// both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr std::uint32_t instr_desc(int ab_format, int m, int n) {
+    return (1u << 4) | (static_cast<std::uint32_t>(ab_format) << 7) | (static_cast<std::uint32_t>(ab_format) << 10) |
+           (static_cast<std::uint32_t>(n >> 3) << 17) | (static_cast<std::uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(std::uint32_t tmem_d, std::uint64_t adesc, std::uint64_t bdesc, std::uint32_t idesc,
+                                        std::uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 TMEM lanes (one per thread of the warp) x 32 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld32(std::uint32_t taddr, float (&v)[32]) {
+    std::uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float load_elem(const void* p, unsigned long long i, int dtype) {
+    if (dtype == SACC_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    if (dtype == SACC_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);
+    return static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_elem(void* p, unsigned long long i, int dtype, float v) {
+    if (dtype == SACC_DTYPE_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+    else if (dtype == SACC_DTYPE_F16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else static_cast<float*>(p)[i] = v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                                                           const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    auto& sm = *reinterpret_cast<GemmSmem<BN>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+
+    if (threadIdx.x == 0) {
+        prefetch_tensor_map(&tm_a);
+        prefetch_tensor_map(&tm_b);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        mbar_init(&sm.accum, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const std::uint32_t tmem = sm.tmem_base;
+
+    bool fault = false;
+    if (warp == 0) {
+        if (lane == 0) {
+            constexpr std::uint32_t bytes = (kBM + BN) * kBK * 2;
+            for (int kb = 0; kb < p.kblocks; ++kb) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait_bounded(&sm.empty[s], static_cast<std::uint32_t>(((kb / kStages) - 1) & 1))) {
+                    fault = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(&sm.full[s], bytes);
+                tma_load_2d(sm.a[s], &tm_a, &sm.full[s], kb * kBK, m0);
+                tma_load_2d(sm.b[s], &tm_b, &sm.full[s], kb * kBK, n0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const std::uint32_t idesc = instr_desc(p.in_dtype == SACC_DTYPE_BF16 ? 1 : 0, kBM, BN);
+            for (int kb = 0; kb < p.kblocks; ++kb) {
+                const int s = kb % kStages;
+                if (!mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((kb / kStages) & 1))) {
+                    fault = true;
+                    break;
+                }
+                tmem_fence_after();
+                const std::uint64_t ad = sw128_desc(sm.a[s]), bd = sw128_desc(sm.b[s]);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                    mma_f16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                mma_commit(&sm.empty[s]);
+            }
+            mma_commit(&sm.accum);
+        }
+    } else {
+        // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
+        const int quarter = warp % 4;
+        const int row = m0 + quarter * 32 + lane;
+        if (!mbar_wait_bounded(&sm.accum, 0u)) {
+            fault = true;
+        } else {
+            tmem_fence_after();
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                tmem_ld32(tmem + (static_cast<std::uint32_t>(quarter * 32) << 16) + static_cast<std::uint32_t>(c * 32), v);
+                if (row < static_cast<int>(p.m)) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const unsigned long long col = static_cast<unsigned long long>(n0 + c * 32 + i);
+                        if (col < p.n) {
+                            float x = v[i];
+                            if (p.bias) x += p.bias[col];
+                            if (p.residual) x += load_elem(p.residual, row * p.ldr + col, p.out_dtype);
+                            store_elem(p.c, row * p.ldc + col, p.out_dtype, x);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (fault) atomicOr(&g_gemm_fault, 1u);
+    tmem_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tmem_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// K-major 2D map (K innermost) with a (64, rows) box and 128-byte swizzle.
+bool kmajor_map(CUtensorMap* map, int dtype, const void* base, unsigned long long k, unsigned long long rows,
+                unsigned long long ld, unsigned box_rows) {
+    auto fn = encode();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {k, rows};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <int BN>
+size_t gemm_smem() {
+    return sizeof(GemmSmem<BN>) + 1024;
+}
+
+template <int BN>
+cudaError_t prepare_gemm() {
+    static const cudaError_t st = cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_kernel<BN>),
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(gemm_smem<BN>()));
+    return st;
+}
+
+template <int BN>
+cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream) {
+    const cudaError_t e = prepare_gemm<BN>();
+    if (e != cudaSuccess) return e;
+    const dim3 grid(static_cast<unsigned>((p.n + BN - 1) / BN), static_cast<unsigned>((p.m + kBM - 1) / kBM));
+    void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), &p};
+    return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), grid, dim3(kThreads), args, gemm_smem<BN>(),
+                            stream);
+}
+
+} // namespace
+
+cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
+    const unsigned bn = a.n <= 64 ? 64u : a.n <= 128 ? 128u : 256u;
+    CUtensorMap ta{}, tb{};
+    if (!kmajor_map(&ta, a.in_dtype, a.a, a.k, a.m, a.lda, kBM) || !kmajor_map(&tb, a.in_dtype, a.b, a.k, a.n, a.ldb, bn))
+        return cudaErrorInvalidValue;
+    GemmParams p{};
+    p.c = a.c; p.residual = a.residual; p.bias = a.bias;
+    p.m = a.m; p.n = a.n; p.k = a.k; p.ldc = a.ldc; p.ldr = a.residual ? a.ldr : 0;
+    p.out_dtype = a.out_dtype; p.in_dtype = a.in_dtype;
+    p.kblocks = static_cast<int>((a.k + kBK - 1) / kBK);
+    if (bn == 64) return launch_bn<64>(ta, tb, p, stream);
+    if (bn == 128) return launch_bn<128>(ta, tb, p, stream);
+    return launch_bn<256>(ta, tb, p, stream);
+}
+
+cudaError_t load_gemm_kernels(std::string& report) {
+    const std::pair<const char*, const void*> ks[] = {{"gemm_tcgen05_bn64", reinterpret_cast<const void*>(gemm_kernel<64>)},
+                                                      {"gemm_tcgen05_bn128", reinterpret_cast<const void*>(gemm_kernel<128>)},
+                                                      {"gemm_tcgen05_bn256", reinterpret_cast<const void*>(gemm_kernel<256>)}};
+    for (const auto& k : ks) {
+        cudaFuncAttributes attr{};
+        const cudaError_t e = cudaFuncGetAttributes(&attr, k.second);
+        if (e != cudaSuccess) return e;
+        report += std::string("kernel=") + k.first + " registers=" + std::to_string(attr.numRegs) + "\n";
+    }
+    cudaError_t e = prepare_gemm<64>();
+    if (e == cudaSuccess) e = prepare_gemm<128>();
+    if (e == cudaSuccess) e = prepare_gemm<256>();
+    return e;
+}
+
+cudaError_t read_gemm_fault(unsigned* out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_gemm_fault, sizeof(unsigned));
+    if (e != cudaSuccess || !clear) return e;
+    const unsigned zero = 0;
+    return cudaMemcpyToSymbol(g_gemm_fault, &zero, sizeof(unsigned));
+}
+
+} // namespace sacc

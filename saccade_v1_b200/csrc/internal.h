@@ -56,6 +56,9 @@ cudaError_t launch_scan_general(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_general_kernels(std::string& report);
 bool bulk_eligible(const SaccScanExArgs& a);
 cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream);
+cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream);
+cudaError_t load_gemm_kernels(std::string& report);
+cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_bulk_kernels(std::string& report);

@@ -193,3 +193,29 @@ def selective_scan_step(u, delta, A, B, C, state, D=None, z=None, delta_bias=Non
                              _ptr(state), _ptr(slot), _ptr(out))
     _check(_lib.load().sacc_selective_scan_step(ctypes.byref(args), _stream_handle(stream)))
     return out
+
+
+def gemm(a, b, *, out=None, bias=None, residual=None, out_dtype=None, stream=None):
+    """C = a @ b.T (+ bias) (+ residual) on the tensor cores; a (m, k), b (n, k) bf16/fp16."""
+    if a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype:
+        raise ScanInvalidArgument("gemm: a and b must both be bf16 or both fp16")
+    m, k = a.shape
+    n = b.shape[0]
+    if b.shape[1] != k:
+        raise ScanInvalidArgument("gemm: a and b disagree on k")
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype or a.dtype, device=a.device)
+    for name, t in (("a", a), ("b", b), ("out", out), ("residual", residual)):
+        if t is not None and t.stride(-1) != 1:
+            raise ScanInvalidArgument(f"gemm: {name} must have unit inner stride")
+    args = _lib.GemmArgs(m, n, k, a.stride(0), b.stride(0), out.stride(0), residual.stride(0) if residual is not None else 0,
+                         _DTYPES[a.dtype], _DTYPES[out.dtype], _ptr(a), _ptr(b), _ptr(out), _ptr(bias), _ptr(residual))
+    _check(_lib.load().sacc_gemm(ctypes.byref(args), _stream_handle(stream)))
+    return out
+
+
+def scan_fault(clear: bool = False) -> int:
+    """The library's device fault word (0 = no kernel ever gave up a bounded wait); synchronous."""
+    v = ctypes.c_uint32(0)
+    _check(_lib.load().sacc_scan_fault(ctypes.byref(v), int(clear)))
+    return v.value

@@ -189,7 +189,7 @@ int sacc_selective_scan_step(const SaccScanStepArgs* args, cudaStream_t stream);
 /* ------------------------------------------------------------------------
  * Projection GEMM on the tensor cores (no counterpart in the reference, whose
  * projections are TensorRT matrix-multiply layers, src/head_trt_network.cpp:
- * 192-230): C[m, n] = sum_k A[m, k] B[n, k] (+ bias[n]) (+ R[m, n]).
+ * 192-230): C[m, n] = s[m] sum_k A[m, k] B[n, k] (+ bias[n]) (+ R[m, n]).
  * A (m x k, row stride lda) and B (n x k, row stride ldb) are bf16 or fp16
  * (in_dtype), K contiguous, 16-byte aligned, lda and ldb multiples of 8;
  * C and R are out_dtype (f32, bf16, f16) with row strides ldc / ldr; bias FP32.
@@ -201,11 +201,46 @@ typedef struct SaccGemmArgs {
     const void* a;
     const void* b;
     void* c;
-    const float* bias;    /* optional (n) */
-    const void* residual; /* optional (m x n, ldr) */
+    const float* bias;      /* optional (n) */
+    const void* residual;   /* optional (m x n, ldr) */
+    const float* row_scale; /* optional (m), s above; 1 when absent */
 } SaccGemmArgs;
 
 int sacc_gemm(const SaccGemmArgs* args, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
+ * One Mamba block forward (the reference builds it from TensorRT layers
+ * around its scan plugin, src/head_trt_network.cpp:181-233), with the
+ * optional RMSNorm prologue of BASELINE configs 1 and 4:
+ *   xn = rmsnorm(x) * norm_w; [x_in, z] = xn W_in^T; u = silu(conv1d(x_in) + conv_b);
+ *   [dt, B, C] = u W_x^T; delta = dt W_dt^T; y = scan(u, delta + dt_bias, A, B, C, D) * silu(z);
+ *   out = y W_out^T (+ x when residual).
+ * Activations and projection weights bf16 or fp16 (dtype); x, out
+ * (batch, length, d_model); w_in (2 d_inner, d_model); w_x (dt_rank + 2 d_state,
+ * d_inner); w_dt (d_inner, dt_rank); w_out (d_model, d_inner).  FP32: norm_w
+ * (d_model, optional), conv_w (d_inner, d_conv), conv_b, dt_bias, d (d_inner),
+ * a (d_inner, d_state) = -exp(A_log).  d_conv must be 4, d_state 16, d_inner
+ * and d_model multiples of 128, length a multiple of 8, dt_rank a multiple of 8.
+ * Intermediates go to `workspace` (at least sacc_mamba_block_workspace bytes,
+ * 256-byte aligned); the call allocates nothing.
+ * ------------------------------------------------------------------------ */
+typedef struct SaccMambaBlockArgs {
+    uint64_t batch, length, d_model, d_inner, d_state, d_conv, dt_rank;
+    int32_t dtype, residual;
+    float eps;
+    const void* x;
+    const float* norm_w;
+    const void* w_in;
+    const float *conv_w, *conv_b;
+    const void* w_x;
+    const void* w_dt;
+    const float *dt_bias, *a, *d;
+    const void* w_out;
+    void* out;
+} SaccMambaBlockArgs;
+
+int sacc_mamba_block_workspace(const SaccMambaBlockArgs* args, size_t* bytes);
+int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -15,6 +15,8 @@ from .scan import (  # noqa: F401
     gemm,
     identity,
     load_kernels,
+    mamba_block_forward,
+    mamba_block_workspace,
     scan_fault,
     selective_scan_cuda,
     selective_scan_ex,

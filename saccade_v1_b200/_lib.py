@@ -29,6 +29,8 @@ EXPORTS = (
     "sacc_scan_fault",
     "sacc_selective_scan_step",
     "sacc_gemm",
+    "sacc_mamba_block_workspace",
+    "sacc_mamba_block_forward",
 )
 
 
@@ -70,7 +72,15 @@ class GemmArgs(ctypes.Structure):
     _fields_ = [("m", ctypes.c_uint64), ("n", ctypes.c_uint64), ("k", ctypes.c_uint64), ("lda", ctypes.c_uint64),
                 ("ldb", ctypes.c_uint64), ("ldc", ctypes.c_uint64), ("ldr", ctypes.c_uint64),
                 ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("a", ctypes.c_void_p),
-                ("b", ctypes.c_void_p), ("c", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p)]
+                ("b", ctypes.c_void_p), ("c", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p),
+                ("row_scale", ctypes.c_void_p)]
+
+
+class MambaBlockArgs(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_uint64) for k in ("batch", "length", "d_model", "d_inner", "d_state", "d_conv", "dt_rank")] + [
+        ("dtype", ctypes.c_int32), ("residual", ctypes.c_int32), ("eps", ctypes.c_float)] + [
+        (k, ctypes.c_void_p) for k in ("x", "norm_w", "w_in", "conv_w", "conv_b", "w_x", "w_dt", "dt_bias", "a", "d",
+                                       "w_out", "out")]
 
 
 _lib = None
@@ -106,6 +116,10 @@ def load() -> ctypes.CDLL:
     L.sacc_selective_scan_step.restype = i
     L.sacc_gemm.argtypes = [ctypes.POINTER(GemmArgs), vp]
     L.sacc_gemm.restype = i
+    L.sacc_mamba_block_workspace.argtypes = [ctypes.POINTER(MambaBlockArgs), ctypes.POINTER(ctypes.c_size_t)]
+    L.sacc_mamba_block_workspace.restype = i
+    L.sacc_mamba_block_forward.argtypes = [ctypes.POINTER(MambaBlockArgs), vp, sz, vp]
+    L.sacc_mamba_block_forward.restype = i
     _lib = L
     return L
 

@@ -1,0 +1,140 @@
+// block_kernels.cu -- the elementwise stages of the Mamba block around the scan
+// (reference src/head_trt_network.cpp:192-230, binary64 twin
+// src/head_reference.cpp:471-495), and the RMSNorm prologue of BASELINE
+// configs 1 and 4 (not in the reference head).
+//
+// RMSNorm is folded into the in_proj GEMM: in_proj(rmsnorm(x)) =
+// diag(r) x (W diag(w))^T with r = 1 / sqrt(mean(x^2) + eps) per token, so the
+// prologue is one pass computing r (applied as a row scale in the GEMM
+// epilogue) and a once-per-call scaling of the weight columns by w.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "internal.h"
+#include "scan_common.cuh"
+
+namespace sacc {
+namespace {
+
+// One warp per token row: r[m] = 1 / sqrt(mean_k x[m,k]^2 + eps).
+template <typename T>
+__global__ void __launch_bounds__(256) rms_scale_kernel(const T* __restrict__ x, unsigned long long m, unsigned k,
+                                                        float eps, float* __restrict__ r) {
+    const unsigned long long row = (static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x) / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= m) return;
+    const T* xr = x + row * k;
+    float acc = 0.0f;
+    for (unsigned i = lane; i < k; i += 32) {
+        const float v = to_f32(xr[i]);
+        acc = fmaf(v, v, acc);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) r[row] = rsqrtf(acc / static_cast<float>(k) + eps);
+}
+
+// W'[n, k] = W[n, k] * w[k].
+template <typename T>
+__global__ void __launch_bounds__(256) scale_columns_kernel(const T* __restrict__ w_in, const float* __restrict__ w,
+                                                            unsigned long long n, unsigned k, T* __restrict__ out) {
+    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= n * k) return;
+    out[i] = from_f32<T>(to_f32(w_in[i]) * w[i % k]);
+}
+
+// u[b, t, d] = silu(bias[d] + sum_j w[d, j] x[b, t + j - (K - 1), d]), zero
+// outside the sequence (causal depthwise conv1d, reference
+// src/head_reference.cpp:190-216).  One thread per (sequence, channel)
+// walks the tokens keeping the last K - 1 inputs in registers; consecutive
+// threads take consecutive channels, so every load and store is coalesced.
+template <typename T, int K>
+__global__ void __launch_bounds__(256) conv_silu_kernel(const T* __restrict__ x, unsigned long long ldx,
+                                                        const float* __restrict__ w, const float* __restrict__ bias,
+                                                        unsigned long long batch, unsigned long long len,
+                                                        unsigned long long dim, T* __restrict__ u) {
+    const unsigned long long lane = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
+    if (lane >= batch * dim) return;
+    const unsigned long long b = lane / dim, d = lane % dim;
+    float wk[K], hist[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        wk[j] = w[d * K + j];
+        hist[j] = 0.0f;
+    }
+    const float bv = bias ? bias[d] : 0.0f;
+    const T* xr = x + b * len * ldx + d;
+    T* ur = u + b * len * dim + d;
+    for (unsigned long long t = 0; t < len; ++t) {
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) hist[j] = hist[j + 1];
+        hist[K - 1] = to_f32(xr[t * ldx]);
+        float acc = bv;
+#pragma unroll
+        for (int j = 0; j < K; ++j) acc = fmaf(wk[j], hist[j], acc);
+        ur[t * dim] = from_f32<T>(acc / (1.0f + expf(-acc)));
+    }
+}
+
+} // namespace
+
+cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
+                             cudaStream_t stream) {
+    const unsigned long long blocks = (m * 32 + 255) / 256;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    if (dtype == SACC_DTYPE_BF16)
+        rms_scale_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), m, k, eps, r);
+    else
+        rms_scale_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __half*>(x), m, k, eps, r);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
+                                 cudaStream_t stream) {
+    const unsigned long long blocks = (n * k + 255) / 256;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    if (dtype == SACC_DTYPE_BF16)
+        scale_columns_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(w_in), w, n, k, static_cast<__nv_bfloat16*>(out));
+    else
+        scale_columns_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __half*>(w_in), w, n,
+                                                                                        k, static_cast<__half*>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
+                             unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
+                             cudaStream_t stream) {
+    const unsigned long long blocks = (batch * dim + 255) / 256;
+    if (blocks > 0x7fffffffull || kwidth != 4) return cudaErrorInvalidConfiguration;
+    if (dtype == SACC_DTYPE_BF16)
+        conv_silu_kernel<__nv_bfloat16, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u));
+    else
+        conv_silu_kernel<__half, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
+    return cudaGetLastError();
+}
+
+cudaError_t load_block_kernels(std::string& report) {
+    const void* ks[] = {reinterpret_cast<const void*>(rms_scale_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(rms_scale_kernel<__half>),
+                        reinterpret_cast<const void*>(scale_columns_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(scale_columns_kernel<__half>),
+                        reinterpret_cast<const void*>(conv_silu_kernel<__nv_bfloat16, 4>),
+                        reinterpret_cast<const void*>(conv_silu_kernel<__half, 4>)};
+    for (const void* k : ks) {
+        cudaFuncAttributes attr{};
+        const cudaError_t e = cudaFuncGetAttributes(&attr, k);
+        if (e != cudaSuccess) return e;
+    }
+    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x6\n";
+    return cudaSuccess;
+}
+
+} // namespace sacc

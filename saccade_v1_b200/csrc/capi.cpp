@@ -153,6 +153,7 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
         CK(load_scan_ex_kernels(text));
         CK(load_scan_step_kernels(text));
         CK(load_gemm_kernels(text));
+        CK(load_block_kernels(text));
         (void)sm_count();
         if (report && report_bytes) {
             std::snprintf(report, report_bytes, "%s", text.c_str());
@@ -378,10 +379,64 @@ int sacc_gemm(const SaccGemmArgs* args, cudaStream_t stream) {
         require_pointer(api, br, 16);
         require_pointer(api, cr, eo);
         require_pointer(api, Region{a.bias, a.bias ? a.n * sizeof(float) : 0, "bias"});
+        require_pointer(api, Region{a.row_scale, a.row_scale ? a.m * sizeof(float) : 0, "row_scale"});
         const Region rr{a.residual, a.residual ? ((a.m - 1) * a.ldr + a.n) * eo : 0, "residual"};
         require_pointer(api, rr, eo);
         if (overlaps(cr, ar) || overlaps(cr, br)) reject(api, "C overlaps an operand");
         CK(launch_gemm(a, stream));
+    });
+}
+
+static void check_block_shape(const char* api, const SaccMambaBlockArgs& a) {
+    if (a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) reject(api, "dtype must be bf16 or f16");
+    if (a.batch == 0 || a.length == 0) reject(api, "batch and length must be positive");
+    if (a.d_conv != 4) reject(api, "d_conv must be 4");
+    if (a.d_state != 16) reject(api, "d_state must be 16");
+    if (a.d_inner == 0 || a.d_inner % 128 != 0 || a.d_model == 0 || a.d_model % 128 != 0)
+        reject(api, "d_inner and d_model must be positive multiples of 128");
+    if (a.length % 8 != 0) reject(api, "length must be a multiple of 8");
+    if (a.dt_rank == 0 || a.dt_rank % 8 != 0) reject(api, "dt_rank must be a positive multiple of 8");
+    if (!(a.eps > 0.0f) && a.norm_w) reject(api, "eps must be positive");
+    const std::uint64_t M = a.batch * a.length;
+    if (M > 0x7fffffffull) reject(api, "batch * length exceeds int32");
+    if (a.length * a.d_inner > kMaxElements) reject(api, "length * d_inner exceeds int32 capacity");
+}
+
+static void check_block(const char* api, const SaccMambaBlockArgs& a) {
+    check_block_shape(api, a);
+    const std::uint64_t M = a.batch * a.length;
+    const std::uint64_t D = a.d_inner, dm = a.d_model, R = a.dt_rank, N = a.d_state;
+    for (const Region& r : {Region{a.x, M * dm * 2, "x"}, Region{a.w_in, 2 * D * dm * 2, "w_in"},
+                            Region{a.w_x, (R + 2 * N) * D * 2, "w_x"}, Region{a.w_dt, D * R * 2, "w_dt"},
+                            Region{a.w_out, dm * D * 2, "w_out"}, Region{a.out, M * dm * 2, "out"}})
+        require_pointer(api, r, 16);
+    for (const Region& r : {Region{a.conv_w, D * 4 * 4, "conv_w"}, Region{a.a, D * N * 4, "A"}})
+        require_pointer(api, r);
+    for (const Region& r : {Region{a.norm_w, a.norm_w ? dm * 4 : 0, "norm_w"}, Region{a.conv_b, a.conv_b ? D * 4 : 0, "conv_b"},
+                            Region{a.dt_bias, a.dt_bias ? D * 4 : 0, "dt_bias"}, Region{a.d, a.d ? D * 4 : 0, "D"}})
+        require_pointer(api, r);
+    if (overlaps(Region{a.out, M * dm * 2, "out"}, Region{a.x, M * dm * 2, "x"})) reject(api, "out overlaps x");
+}
+
+int sacc_mamba_block_workspace(const SaccMambaBlockArgs* args, size_t* bytes) {
+    return guarded([&] {
+        if (args == nullptr || bytes == nullptr) reject("mamba_block", "args and bytes are required");
+        check_block_shape("mamba_block", *args);
+        *bytes = mamba_block_workspace(*args);
+    });
+}
+
+int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "mamba_block";
+        if (args == nullptr) reject(api, "args are required");
+        require_stream(api, stream);
+        check_block(api, *args);
+        const std::size_t need = mamba_block_workspace(*args);
+        if (workspace_bytes < need) reject(api, "workspace holds " + std::to_string(workspace_bytes) + " bytes, needs " +
+                                                    std::to_string(need));
+        require_pointer(api, Region{workspace, need, "workspace"}, 256);
+        CK(launch_mamba_block(*args, workspace, stream));
     });
 }
 

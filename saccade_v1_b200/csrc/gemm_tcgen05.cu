@@ -13,8 +13,8 @@
 //               four times per stage from shared-memory descriptors, then
 //               tcgen05.commit to free the stage and, at the end, to signal
 //               the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, bias,
-//               residual, conversion, bounds-checked stores.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, row
+//               scale, bias, residual, conversion, bounds-checked stores.
 // No multicast, no clusters.  Every mbarrier wait has an iteration limit and
 // sets the library fault word when it runs out.
 #include <cuda.h>
@@ -54,6 +54,7 @@ struct GemmParams {
     void* c;
     const void* residual;
     const float* bias;
+    const float* row_scale;
     unsigned long long m, n, k, ldc, ldr;
     int out_dtype, in_dtype, kblocks;
 };
@@ -195,11 +196,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 float v[32];
                 tmem_ld32(tmem + (static_cast<std::uint32_t>(quarter * 32) << 16) + static_cast<std::uint32_t>(c * 32), v);
                 if (row < static_cast<int>(p.m)) {
+                    const float rs = p.row_scale ? p.row_scale[row] : 1.0f;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const unsigned long long col = static_cast<unsigned long long>(n0 + c * 32 + i);
                         if (col < p.n) {
-                            float x = v[i];
+                            float x = v[i] * rs;
                             if (p.bias) x += p.bias[col];
                             if (p.residual) x += load_elem(p.residual, row * p.ldr + col, p.out_dtype);
                             store_elem(p.c, row * p.ldc + col, p.out_dtype, x);
@@ -277,7 +279,7 @@ cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     if (!kmajor_map(&ta, a.in_dtype, a.a, a.k, a.m, a.lda, kBM) || !kmajor_map(&tb, a.in_dtype, a.b, a.k, a.n, a.ldb, bn))
         return cudaErrorInvalidValue;
     GemmParams p{};
-    p.c = a.c; p.residual = a.residual; p.bias = a.bias;
+    p.c = a.c; p.residual = a.residual; p.bias = a.bias; p.row_scale = a.row_scale;
     p.m = a.m; p.n = a.n; p.k = a.k; p.ldc = a.ldc; p.ldr = a.residual ? a.ldr : 0;
     p.out_dtype = a.out_dtype; p.in_dtype = a.in_dtype;
     p.kblocks = static_cast<int>((a.k + kBK - 1) / kBK);

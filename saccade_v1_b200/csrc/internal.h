@@ -57,6 +57,16 @@ cudaError_t load_scan_general_kernels(std::string& report);
 bool bulk_eligible(const SaccScanExArgs& a);
 cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream);
+cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
+                             cudaStream_t stream);
+cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
+                                 cudaStream_t stream);
+cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
+                             unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
+                             cudaStream_t stream);
+cudaError_t load_block_kernels(std::string& report);
+std::size_t mamba_block_workspace(const SaccMambaBlockArgs& a);
+cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cudaStream_t stream);
 cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);

@@ -195,8 +195,8 @@ def selective_scan_step(u, delta, A, B, C, state, D=None, z=None, delta_bias=Non
     return out
 
 
-def gemm(a, b, *, out=None, bias=None, residual=None, out_dtype=None, stream=None):
-    """C = a @ b.T (+ bias) (+ residual) on the tensor cores; a (m, k), b (n, k) bf16/fp16."""
+def gemm(a, b, *, out=None, bias=None, residual=None, row_scale=None, out_dtype=None, stream=None):
+    """C = diag(row_scale) a @ b.T (+ bias) (+ residual) on the tensor cores; a (m, k), b (n, k) bf16/fp16."""
     if a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype:
         raise ScanInvalidArgument("gemm: a and b must both be bf16 or both fp16")
     m, k = a.shape
@@ -209,7 +209,8 @@ def gemm(a, b, *, out=None, bias=None, residual=None, out_dtype=None, stream=Non
         if t is not None and t.stride(-1) != 1:
             raise ScanInvalidArgument(f"gemm: {name} must have unit inner stride")
     args = _lib.GemmArgs(m, n, k, a.stride(0), b.stride(0), out.stride(0), residual.stride(0) if residual is not None else 0,
-                         _DTYPES[a.dtype], _DTYPES[out.dtype], _ptr(a), _ptr(b), _ptr(out), _ptr(bias), _ptr(residual))
+                         _DTYPES[a.dtype], _DTYPES[out.dtype], _ptr(a), _ptr(b), _ptr(out), _ptr(bias), _ptr(residual),
+                         _ptr(row_scale))
     _check(_lib.load().sacc_gemm(ctypes.byref(args), _stream_handle(stream)))
     return out
 
@@ -219,3 +220,49 @@ def scan_fault(clear: bool = False) -> int:
     v = ctypes.c_uint32(0)
     _check(_lib.load().sacc_scan_fault(ctypes.byref(v), int(clear)))
     return v.value
+
+
+BLOCK_KEYS = ("norm_w", "w_in", "conv_w", "conv_b", "w_x", "w_dt", "dt_bias", "A", "D", "w_out")
+
+
+def _block_args(x, p, eps, residual, out):
+    batch, length, d_model = x.shape
+    d_inner = p["w_in"].shape[0] // 2
+    d_conv = p["conv_w"].shape[-1]
+    dt_rank = p["w_dt"].shape[1]
+    d_state = p["A"].shape[1]
+    for k in BLOCK_KEYS:
+        t = p.get(k)
+        if t is not None and not t.is_contiguous():
+            raise ScanInvalidArgument(f"mamba_block: {k} must be contiguous")
+    return _lib.MambaBlockArgs(batch, length, d_model, d_inner, d_state, d_conv, dt_rank, _DTYPES[x.dtype], int(residual),
+                               float(eps), _ptr(x), _ptr(p.get("norm_w")), _ptr(p["w_in"]), _ptr(p["conv_w"]),
+                               _ptr(p.get("conv_b")), _ptr(p["w_x"]), _ptr(p["w_dt"]), _ptr(p.get("dt_bias")),
+                               _ptr(p["A"]), _ptr(p.get("D")), _ptr(p["w_out"]), _ptr(out))
+
+
+def mamba_block_workspace(x, params, eps=1e-5, residual=True) -> int:
+    n = ctypes.c_size_t(0)
+    _check(_lib.load().sacc_mamba_block_workspace(ctypes.byref(_block_args(x, params, eps, residual, None)), ctypes.byref(n)))
+    return n.value
+
+
+def mamba_block_forward(x, params, *, eps=1e-5, residual=True, out=None, workspace=None, stream=None):
+    """One Mamba block forward (RMSNorm when params["norm_w"] is given, in_proj, conv1d + SiLU,
+    x_proj, dt_proj, selective scan with D skip and SiLU(z) gate, out_proj, + x).
+
+    x (batch, length, d_model) bf16/fp16; weights as in include/sacc_scan.h
+    (SaccMambaBlockArgs).  workspace: optional uint8 device tensor of at least
+    mamba_block_workspace(...) bytes (allocated here when omitted).
+    """
+    if out is None:
+        out = torch.empty_like(x)
+    args = _block_args(x, params, eps, residual, out)
+    need = mamba_block_workspace(x, params, eps, residual)
+    if workspace is None:
+        workspace = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+    base = workspace.data_ptr()
+    off = (-base) % 256
+    _check(_lib.load().sacc_mamba_block_forward(ctypes.byref(args), base + off, workspace.numel() - off,
+                                                _stream_handle(stream)))
+    return out

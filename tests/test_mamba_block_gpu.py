@@ -1,0 +1,88 @@
+"""GPU parity of the fused Mamba block forward (sacc_mamba_block_forward).
+
+The device pipeline (RMSNorm folded into the tcgen05 in_proj, conv1d + SiLU,
+tcgen05 x_proj / dt_proj, bulk scan with D skip and SiLU(z) gate, tcgen05
+out_proj with the residual) is compared with the binary64 block oracle
+(oracle/mamba_oracle.py), which rounds to the activation dtype where the
+device stores activations.  Tolerance (BASELINE, 16-bit activations against
+an FP32-or-better reference): |gpu - ref| <= 1e-3 + 1e-2 |ref|.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import mamba_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import saccade_v1_b200 as sb  # noqa: E402
+
+TORCH = {"bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def to_dev(p, dt):
+    out = {}
+    for k, v in p.items():
+        if k in ("w_in", "w_x", "w_dt", "w_out"):
+            out[k] = torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device="cuda", dtype=TORCH[dt])
+        else:
+            out[k] = torch.from_numpy(np.ascontiguousarray(v, np.float32)).cuda()
+    return out
+
+
+def run_block(x_np, p, dt, residual=True):
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        x = torch.from_numpy(np.ascontiguousarray(x_np, np.float32)).to(device="cuda", dtype=TORCH[dt])
+        y = sb.mamba_block_forward(x, to_dev(p, dt), residual=residual, stream=s)
+    s.synchronize()
+    return y.float().cpu().numpy()
+
+
+def check(name, got, ref):
+    err = np.abs(got.astype(np.float64) - ref)
+    bad = ~(err <= 1e-3 + 1e-2 * np.abs(ref))
+    assert not bad.any(), f"{name}: {int(bad.sum())}/{got.size} beyond 1e-3 + 1e-2|ref|, max err {err.max():.3g}"
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("norm", [True, False])
+def test_block_matches_oracle_small(dt, norm):
+    B, L, dm, D, N, R = 4, 32, 128, 256, 16, 8
+    p = mo.random_block(10, dm, D, N, R, 4, dt, norm=norm)
+    x = mo.rnd(np.random.default_rng(2).standard_normal((B, L, dm)) * 0.1, dt)
+    got = run_block(x, p, dt)
+    check(f"block_{dt}_{norm}", got, mo.block_forward(x, p, dt))
+    assert sb.scan_fault() == 0
+
+
+def test_block_without_residual_and_wide_dt_rank():
+    B, L, dm, D, N, R = 2, 40, 256, 384, 16, 64
+    p = mo.random_block(11, dm, D, N, R, 4, "bf16")
+    x = mo.rnd(np.random.default_rng(3).standard_normal((B, L, dm)) * 0.1, "bf16")
+    check("block_wide", run_block(x, p, "bf16", residual=False), mo.block_forward(x, p, "bf16", residual=False))
+
+
+def test_config1_full_size_sampled_tracks():
+    """256 tracks x 32 frames, d_model 128, D 256, N 16, dt_rank 8, fp16."""
+    B, L, dm, D, N, R = 256, 32, 128, 256, 16, 8
+    p = mo.random_block(12, dm, D, N, R, 4, "f16")
+    x = mo.rnd(np.random.default_rng(4).standard_normal((B, L, dm)) * 0.1, "f16")
+    got = run_block(x, p, "f16")
+    pick = np.random.default_rng(5).integers(0, B, 12)
+    check("config1_tracks", got[pick], mo.block_forward(x[pick], p, "f16"))
+
+
+def test_block_rejections():
+    x = torch.zeros(2, 8, 128, dtype=torch.float16, device="cuda")
+    p = to_dev(mo.random_block(1, 128, 256, 16, 8, 4, "f16"), "f16")
+    with pytest.raises(sb.ScanInvalidArgument, match="non-default stream"):
+        sb.mamba_block_forward(x, p, stream=0)
+    with pytest.raises(sb.ScanInvalidArgument, match="length must be a multiple of 8"):
+        sb.mamba_block_forward(torch.zeros(2, 6, 128, dtype=torch.float16, device="cuda"), p, stream=torch.cuda.Stream())
+    bad = dict(p, conv_w=torch.zeros(256, 3, device="cuda"))
+    with pytest.raises(sb.ScanInvalidArgument, match="d_conv must be 4"):
+        sb.mamba_block_forward(x, bad, stream=torch.cuda.Stream())

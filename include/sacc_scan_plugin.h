@@ -1,0 +1,96 @@
+/*
+ * sacc_scan_plugin.h -- the scan's TensorRT plugin surface as a C ABI.
+ *
+ * The reference exposes its scan to TensorRT as three IPluginV3 plugins
+ * (include/saccade/scan_trt_plugin.hpp:26-49, src/scan_trt_plugin.cpp):
+ *   saccade::SelectiveScan   v2  fields: has_d (INT32)
+ *   saccade::CrossScanExpand v1  fields: none
+ *   saccade::CrossScanMerge  v1  fields: height, width (INT32)
+ * Each entry point below implements one IPluginV3 / IPluginCreatorV3One method
+ * with the reference's semantics and messages, on plain structs; a TensorRT
+ * adapter only translates TensorRT's descriptors and fields into these
+ * (INTEGRATION.md).  Errors: SACC_EINVAL (nothing enqueued) or SACC_ECUDA,
+ * message from sacc_plugin_last_error().
+ */
+#ifndef SACC_SCAN_PLUGIN_H
+#define SACC_SCAN_PLUGIN_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#include "sacc_scan.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SACC_PLUGIN_NAMESPACE "saccade"
+#define SACC_PLUGIN_SCAN_NAME "SelectiveScan"
+#define SACC_PLUGIN_SCAN_VERSION "2"
+#define SACC_PLUGIN_EXPAND_NAME "CrossScanExpand"
+#define SACC_PLUGIN_EXPAND_VERSION "1"
+#define SACC_PLUGIN_MERGE_NAME "CrossScanMerge"
+#define SACC_PLUGIN_MERGE_VERSION "1"
+
+/* Field and tensor type tags (the adapter maps TensorRT's PluginFieldType,
+ * DataType and TensorFormat values onto these). */
+#define SACC_FIELD_INT32 1
+#define SACC_FIELD_OTHER 0
+#define SACC_TENSOR_FLOAT 0
+#define SACC_TENSOR_INT32 3
+#define SACC_TENSOR_OTHER 99
+#define SACC_FORMAT_LINEAR 0
+#define SACC_FORMAT_OTHER 99
+
+typedef struct SaccPluginField {
+    const char* name;
+    const void* data;
+    int32_t type;   /* SACC_FIELD_* */
+    int32_t length; /* number of values */
+} SaccPluginField;
+
+typedef struct SaccTensorDesc {
+    int32_t nb_dims;
+    int64_t dims[8];
+    int32_t type;   /* SACC_TENSOR_* */
+    int32_t format; /* SACC_FORMAT_* */
+} SaccTensorDesc;
+
+typedef struct SaccScanPlugin SaccScanPlugin;
+
+/* IPluginCreatorV3One::createPlugin (src/scan_trt_plugin.cpp:365-393): exactly
+ * the advertised fields, each one INT32 value; unknown, duplicate, missing,
+ * wrong-typed or null fields are rejected. */
+int sacc_plugin_create(const char* name, const char* version, const SaccPluginField* fields, int32_t nb_fields,
+                       SaccScanPlugin** out);
+void sacc_plugin_destroy(SaccScanPlugin* plugin);
+/* IPluginV3::clone (:83-89): semantic fields and the context binding. */
+int sacc_plugin_clone(const SaccScanPlugin* plugin, SaccScanPlugin** out);
+/* getFieldsToSerialize (:244): -1 for a field the plugin does not have. */
+int sacc_plugin_fields(const SaccScanPlugin* plugin, int32_t* has_d, int32_t* height, int32_t* width);
+/* getOutputDataTypes (:102-109). */
+int sacc_plugin_output_types(const SaccScanPlugin* plugin, const int32_t* in_types, int32_t nb_in, int32_t* out_types,
+                             int32_t nb_out);
+/* getOutputShapes (:111-160) for concrete input dims. */
+int sacc_plugin_output_shapes(const SaccScanPlugin* plugin, const SaccTensorDesc* in, int32_t nb_in, SaccTensorDesc* out,
+                              int32_t nb_out);
+/* supportsFormatCombination (:163-167): 1 when supported. */
+int sacc_plugin_supports_format(const SaccScanPlugin* plugin, int32_t pos, const SaccTensorDesc* io, int32_t nb_in,
+                                int32_t nb_out);
+/* getWorkspaceSize (:184-186): always 0. */
+size_t sacc_plugin_workspace_size(const SaccScanPlugin* plugin);
+/* configurePlugin / attachToContext (:171-180, 233-242): load every kernel in
+ * the current CUDA context and bind the plugin to that context. */
+int sacc_plugin_bind(SaccScanPlugin* plugin);
+/* enqueue (:201-229): explicit non-default stream of the bound context,
+ * descriptor checks (:299-341), then the operator on `stream`. */
+int sacc_plugin_enqueue(const SaccScanPlugin* plugin, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
+                        const void* const* inputs, void* const* outputs, cudaStream_t stream);
+const char* sacc_plugin_last_error(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SACC_SCAN_PLUGIN_H */

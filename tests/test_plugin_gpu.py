@@ -1,0 +1,98 @@
+"""The plugin surface on the GPU: after bind(), enqueue must produce the same
+bits and status words as the direct API (the reference's scan_trt_tests
+compare every plugin call bit for bit with the direct S02 API,
+docs/SCAN_TRT.md:46), including a failing call, and the three plugins chain
+expand -> scan -> merge."""
+import numpy as np
+import pytest
+import torch
+
+from oracle.oracle import Shape, random_case
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import gpu_util as gu  # noqa: E402
+import saccade_v1_b200 as sb  # noqa: E402
+from saccade_v1_b200.plugin import EXPAND, MERGE, SCAN, TENSOR_INT32, PluginError, ScanPlugin, TensorDesc  # noqa: E402
+
+
+def descs_for(k):
+    s = k.shape
+    dims = [(s.batch, s.length, s.channels), (s.batch, s.length, s.channels), (s.a_rows, s.state),
+            (s.batch, s.length, s.state), (s.batch, s.length, s.c_width)] + ([(s.channels,)] if s.has_d else [])
+    return [TensorDesc.of(d) for d in dims], [TensorDesc.of((s.batch, s.length, s.channels)),
+                                              TensorDesc.of((2,), TENSOR_INT32)]
+
+
+@pytest.mark.parametrize("bad", [False, True])
+def test_plugin_enqueue_is_bitwise_the_direct_api(bad):
+    k = random_case(Shape(4, 240, 256, 16, 1, 1, True), 0x5eed0600)
+    if bad:
+        k.delta[17] = np.inf
+    p = ScanPlugin.create(*SCAN, [("has_d", 1)])
+    p.bind()
+    s = gu.stream()
+    with torch.cuda.stream(s):
+        ins = [gu.dev(x) for x in k.inputs()]
+        y = torch.empty(k.u.size, device="cuda")
+        st = gu.new_status()
+        ind, outd = descs_for(k)
+        p.enqueue(ind, outd, [t.data_ptr() for t in ins], [y.data_ptr(), st.data_ptr()], s)
+    s.synchronize()
+    direct_y, direct_st = gu.run_f32(k)
+    assert gu.status_words(st) == direct_st
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), direct_y.view(np.uint32))
+
+
+def test_plugin_descriptor_rejection_leaves_status():
+    k = random_case(Shape(2, 8, 128, 16, 1, 1, True), 0x5eed0601)
+    p = ScanPlugin.create(*SCAN, [("has_d", 1)])
+    p.bind()
+    s = gu.stream()
+    with torch.cuda.stream(s):
+        ins = [gu.dev(x) for x in k.inputs()]
+        y = torch.empty(k.u.size, device="cuda")
+        st = gu.new_status()
+    s.synchronize()
+    ind, outd = descs_for(k)
+    ind[1] = TensorDesc.of((2, 9, 128))
+    with pytest.raises(PluginError, match=r"saccade::SelectiveScan: delta \(2,9,128\) differs from u \(2,8,128\)"):
+        p.enqueue(ind, outd, [t.data_ptr() for t in ins], [y.data_ptr(), st.data_ptr()], s)
+    assert gu.status_words(st) == gu.STATUS_SENTINEL
+
+
+def test_plugins_chain_expand_scan_merge():
+    C, H, W = 8, 5, 5
+    L = H * W
+    x = np.random.default_rng(1).standard_normal(C * L).astype(np.float32)
+    k = random_case(Shape(4, L, C, 4, 1, 1, True), 0x5eed0602)
+    e = ScanPlugin.create(*EXPAND, [])
+    sc = ScanPlugin.create(*SCAN, [("has_d", 1)])
+    m = ScanPlugin.create(*MERGE, [("height", H), ("width", W)])
+    for p in (e, sc, m):
+        p.bind()
+    s = gu.stream()
+    with torch.cuda.stream(s):
+        dx = gu.dev(x)
+        tokens = torch.empty(4 * C * L, device="cuda")
+        ins = [gu.dev(v) for v in k.inputs()]
+        y = torch.empty(4 * L * C, device="cuda")
+        out = torch.empty(C * L, device="cuda")
+        sts = [gu.new_status() for _ in range(3)]
+        e.enqueue([TensorDesc.of((1, C, H, W))], [TensorDesc.of((4, L, C)), TensorDesc.of((2,), TENSOR_INT32)],
+                  [dx.data_ptr()], [tokens.data_ptr(), sts[0].data_ptr()], s)
+        ind, outd = descs_for(k)
+        sc.enqueue(ind, outd, [tokens.data_ptr()] + [t.data_ptr() for t in ins[1:]], [y.data_ptr(), sts[1].data_ptr()], s)
+        m.enqueue([TensorDesc.of((4, L, C))], [TensorDesc.of((1, C, H, W)), TensorDesc.of((2,), TENSOR_INT32)],
+                  [y.data_ptr()], [out.data_ptr(), sts[2].data_ptr()], s)
+    s.synchronize()
+    assert all(gu.status_words(t) == (0, sb.SCAN_DONE) for t in sts)
+    # Same calls through the direct API give the same bits.
+    k2 = k.copy()
+    from oracle import oracle
+    k2.u = oracle.cross_scan_expand(x, 1, C, H, W)
+    y2, _ = gu.run_f32(k2)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), y2.view(np.uint32))

@@ -441,7 +441,76 @@ def secondary(torch, device, stream, peak):
         out["hr_deploy_f32_us"] = dict(levels, total=round(total, 2), reference_published_total_us=722.351,
                                        note="reference figure is its own CUDA kernel on an RTX 5070 Ti laptop GPU")
     stream.synchronize()
+    out["c1_block"] = c1_block(torch, device, stream)
+    out["gemm"] = gemm_probe(torch, device, stream)
     return out
+
+
+def synthetic_block(seed, d_model, d_inner, d_state, dt_rank, d_conv=4):
+    """Seeded block weights: uniform +-1/sqrt(fan_in), A = -(1..N), D = 1,
+    dt_bias = softplus^-1(logU[1e-3, 1e-1]), RMSNorm weight ~ 1 + N(0, 0.01)."""
+    r = np.random.default_rng(seed)
+    u = lambda shape, fan: (r.uniform(-1, 1, shape) / np.sqrt(fan)).astype(np.float32)
+    return {"w_in": u((2 * d_inner, d_model), d_model), "conv_w": u((d_inner, d_conv), d_conv),
+            "conv_b": u((d_inner,), d_conv), "w_x": u((dt_rank + 2 * d_state, d_inner), d_inner),
+            "w_dt": u((d_inner, dt_rank), dt_rank),
+            "dt_bias": np.log(np.expm1(np.exp(r.uniform(np.log(1e-3), np.log(1e-1), d_inner)))).astype(np.float32),
+            "A": -np.tile(np.arange(1, d_state + 1, dtype=np.float32), (d_inner, 1)),
+            "D": np.ones(d_inner, np.float32), "w_out": u((d_model, d_inner), d_inner),
+            "norm_w": (1.0 + 0.1 * r.standard_normal(d_model)).astype(np.float32)}
+
+
+def c1_block(torch, device, stream):
+    """one Mamba block forward over 256 tracks x 32 frames (fp16), graph-captured."""
+    import saccade_v1_b200 as sb
+    B1, L1, dm, D1, N1, R1 = 256, 32, 128, 256, 16, 8
+    p = synthetic_block(12, dm, D1, N1, R1)
+    with torch.cuda.stream(stream):
+        dev = {k: (torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device=device, dtype=torch.float16)
+                   if k in ("w_in", "w_x", "w_dt", "w_out") else torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device))
+               for k, v in p.items()}
+        x = (torch.randn(B1, L1, dm, device=device) * 0.1).to(torch.float16)
+        y = torch.empty_like(x)
+        ws = torch.empty(sb.mamba_block_workspace(x, dev) + 256, dtype=torch.uint8, device=device)
+        fwd = lambda: sb.mamba_block_forward(x, dev, out=y, workspace=ws, stream=stream)
+        fwd()
+    stream.synchronize()
+    eager_us = time_device(torch, stream, fwd, 50)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fwd()
+
+    def replay():
+        with torch.cuda.stream(stream):  # CUDAGraph.replay launches on the current stream
+            g.replay()
+
+    graph_us = time_device(torch, stream, replay, 200)
+    flops = 2 * B1 * L1 * (dm * 2 * D1 + D1 * (R1 + 2 * N1) + R1 * D1 + D1 * dm)
+    return {"us_graph": round(graph_us, 2), "us_eager": round(eager_us, 2),
+            "tracks_frames_per_s": round(B1 / (graph_us * 1e-6), 1), "gflop": round(flops / 1e9, 3),
+            "kernels_per_forward": 11,
+            "workload": "256 tracks x 32 frames, d_model 128, D 256, N 16, dt_rank 8, fp16, RMSNorm + residual"}
+
+
+def gemm_probe(torch, device, stream):
+    """The tcgen05 projection GEMM at the config-4 in_proj shape of one 8-GPU shard (bf16 in, bf16 out)."""
+    import saccade_v1_b200 as sb
+    m, n, k = 64 * 4096, 4096, 1024
+    with torch.cuda.stream(stream):
+        a = torch.randn(m, k, device=device).to(torch.bfloat16)
+        b = (torch.randn(n, k, device=device) / 32).to(torch.bfloat16)
+        c = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        run = lambda: sb.gemm(a, b, out=c, stream=stream)
+    us = time_device(torch, stream, run, 5, warmup=2)
+    tflops = 2 * m * n * k / (us * 1e-6) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak = 1590.0
+    del a, b, c
+    return {"shape_mnk": [m, n, k], "us": round(us, 1), "tflops": round(tflops, 1), "peak_tflops": peak,
+            "frac": round(tflops / peak, 4), "bound": "tensor"}
 
 
 def reference_sample(threads: int):

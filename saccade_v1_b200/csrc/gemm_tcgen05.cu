@@ -4,17 +4,19 @@
 // Mamba block, reference src/head_trt_network.cpp:192-230) are GEMMs of
 // token rows A (M x K, K contiguous) with weight rows B (N x K, K contiguous).
 //
-// One CTA computes a 128 x BN tile of C with a 128 x BN FP32 accumulator in
-// tensor memory (TMEM):
+// A persistent CTA (one per SM) walks 128 x BN tiles of C, accumulating each in
+// one of two 128 x BN FP32 tensor-memory (TMEM) buffers so that the epilogue of
+// a tile overlaps the MMAs of the next:
 //   warp 0      TMA producer: 128 x 64 A and BN x 64 B bf16/fp16 tiles with
 //               128-byte swizzle into a 4-stage ring (full / empty mbarriers);
 //   warp 1      allocates TMEM, and one elected thread issues
 //               tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN, K = 16)
 //               four times per stage from shared-memory descriptors, then
-//               tcgen05.commit to free the stage and, at the end, to signal
+//               tcgen05.commit to free the stage and, per tile, to signal
 //               the epilogue;
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, row
-//               scale, bias, residual, conversion, bounds-checked stores.
+//               scale, bias, residual, conversion, 16-byte stores, then
+//               release the accumulator buffer.
 // No multicast, no clusters.  Every mbarrier wait has an iteration limit and
 // sets the library fault word when it runs out.
 #include <cuda.h>
@@ -46,7 +48,8 @@ struct GemmSmem {
     alignas(1024) std::uint16_t b[kStages][BN * kBK];
     alignas(8) std::uint64_t full[kStages];
     alignas(8) std::uint64_t empty[kStages];
-    alignas(8) std::uint64_t accum;
+    alignas(8) std::uint64_t acc_full[2];
+    alignas(8) std::uint64_t acc_empty[2];
     std::uint32_t tmem_base;
 };
 
@@ -56,7 +59,7 @@ struct GemmParams {
     const float* bias;
     const float* row_scale;
     unsigned long long m, n, k, ldc, ldr;
-    int out_dtype, in_dtype, kblocks;
+    int out_dtype, in_dtype, kblocks, tiles_m, tiles_n, vec_store;
 };
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with the
@@ -88,6 +91,10 @@ __device__ __forceinline__ void mma_f16(std::uint32_t tmem_d, std::uint64_t ades
 __device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                  : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -122,13 +129,60 @@ __device__ __forceinline__ void store_elem(void* p, unsigned long long i, int dt
     else static_cast<float*>(p)[i] = v;
 }
 
+__device__ __forceinline__ std::uint32_t pack_out(float lo, float hi, int dtype) {
+    if (dtype == SACC_DTYPE_BF16) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const std::uint32_t*>(&v);
+    }
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const std::uint32_t*>(&v);
+}
+
+// Epilogue of 32 consecutive columns of one row: row scale, bias, residual,
+// conversion; 16-byte stores when the row segment is aligned and complete.
+__device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long long row, unsigned long long col0, float (&v)[32]) {
+    const float rs = p.row_scale ? p.row_scale[row] : 1.0f;
+    const bool full = col0 + 32 <= p.n;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float x = v[i] * rs;
+        if (p.bias && (full || col0 + i < p.n)) x += p.bias[col0 + i];
+        v[i] = x;
+    }
+    if (p.residual) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (full || col0 + i < p.n) v[i] += load_elem(p.residual, row * p.ldr + col0 + i, p.out_dtype);
+    }
+    if (full && p.vec_store) {
+        if (p.out_dtype == SACC_DTYPE_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.c) + row * p.ldc + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<std::uint16_t*>(p.c) + row * p.ldc + col0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                dst[q] = make_uint4(pack_out(v[8 * q], v[8 * q + 1], p.out_dtype), pack_out(v[8 * q + 2], v[8 * q + 3], p.out_dtype),
+                                    pack_out(v[8 * q + 4], v[8 * q + 5], p.out_dtype),
+                                    pack_out(v[8 * q + 6], v[8 * q + 7], p.out_dtype));
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.n) store_elem(p.c, row * p.ldc + col0 + i, p.out_dtype, v[i]);
+}
+
+// Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...;
+// two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                                                            const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
     extern __shared__ unsigned char smem_raw[];
     auto& sm = *reinterpret_cast<GemmSmem<BN>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int tiles = p.tiles_m * p.tiles_n;
 
     if (threadIdx.x == 0) {
         prefetch_tensor_map(&tm_a);
@@ -137,12 +191,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        mbar_init(&sm.accum, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm.acc_full[b], 1);
+            mbar_init(&sm.acc_empty[b], 4); // one arrival per epilogue warp
+        }
         fence_barrier_init();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
-                     "r"(BN)
+                     "r"(2 * BN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -155,60 +212,73 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 0) {
         if (lane == 0) {
             constexpr std::uint32_t bytes = (kBM + BN) * kBK * 2;
-            for (int kb = 0; kb < p.kblocks; ++kb) {
-                const int s = kb % kStages;
-                if (kb >= kStages && !mbar_wait_bounded(&sm.empty[s], static_cast<std::uint32_t>(((kb / kStages) - 1) & 1))) {
-                    fault = true;
-                    break;
+            unsigned g = 0; // k-blocks issued by this CTA
+            for (int tile = blockIdx.x; tile < tiles && !fault; tile += gridDim.x) {
+                const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
+                for (int kb = 0; kb < p.kblocks; ++kb, ++g) {
+                    const unsigned s = g % kStages;
+                    if (g >= kStages && !mbar_wait_bounded(&sm.empty[s], ((g / kStages) - 1) & 1u)) {
+                        fault = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sm.full[s], bytes);
+                    tma_load_2d(sm.a[s], &tm_a, &sm.full[s], kb * kBK, m0);
+                    tma_load_2d(sm.b[s], &tm_b, &sm.full[s], kb * kBK, n0);
                 }
-                mbar_arrive_expect_tx(&sm.full[s], bytes);
-                tma_load_2d(sm.a[s], &tm_a, &sm.full[s], kb * kBK, m0);
-                tma_load_2d(sm.b[s], &tm_b, &sm.full[s], kb * kBK, n0);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const std::uint32_t idesc = instr_desc(p.in_dtype == SACC_DTYPE_BF16 ? 1 : 0, kBM, BN);
-            for (int kb = 0; kb < p.kblocks; ++kb) {
-                const int s = kb % kStages;
-                if (!mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((kb / kStages) & 1))) {
+            unsigned g = 0, it = 0;
+            for (int tile = blockIdx.x; tile < tiles && !fault; tile += gridDim.x, ++it) {
+                const unsigned ab = it & 1u;
+                if (it >= 2 && !mbar_wait_bounded(&sm.acc_empty[ab], ((it / 2) - 1) & 1u)) {
                     fault = true;
                     break;
                 }
                 tmem_fence_after();
-                const std::uint64_t ad = sw128_desc(sm.a[s]), bd = sw128_desc(sm.b[s]);
+                const std::uint32_t acc = tmem + ab * BN;
+                for (int kb = 0; kb < p.kblocks; ++kb, ++g) {
+                    const unsigned s = g % kStages;
+                    if (!mbar_wait_bounded(&sm.full[s], (g / kStages) & 1u)) {
+                        fault = true;
+                        break;
+                    }
+                    tmem_fence_after();
+                    const std::uint64_t ad = sw128_desc(sm.a[s]), bd = sw128_desc(sm.b[s]);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                    mma_f16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
-                mma_commit(&sm.empty[s]);
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_f16(acc, ad + 2ull * kk, bd + 2ull * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit(&sm.empty[s]);
+                }
+                if (fault) break;
+                mma_commit(&sm.acc_full[ab]);
             }
-            mma_commit(&sm.accum);
         }
     } else {
         // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
         const int quarter = warp % 4;
-        const int row = m0 + quarter * 32 + lane;
-        if (!mbar_wait_bounded(&sm.accum, 0u)) {
-            fault = true;
-        } else {
+        unsigned it = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+            const unsigned ab = it & 1u;
+            if (!mbar_wait_bounded(&sm.acc_full[ab], (it / 2) & 1u)) {
+                fault = true;
+                break;
+            }
             tmem_fence_after();
+            const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
+            const unsigned long long row = static_cast<unsigned long long>(m0 + quarter * 32 + lane);
             for (int c = 0; c < BN / 32; ++c) {
                 float v[32];
-                tmem_ld32(tmem + (static_cast<std::uint32_t>(quarter * 32) << 16) + static_cast<std::uint32_t>(c * 32), v);
-                if (row < static_cast<int>(p.m)) {
-                    const float rs = p.row_scale ? p.row_scale[row] : 1.0f;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const unsigned long long col = static_cast<unsigned long long>(n0 + c * 32 + i);
-                        if (col < p.n) {
-                            float x = v[i] * rs;
-                            if (p.bias) x += p.bias[col];
-                            if (p.residual) x += load_elem(p.residual, row * p.ldr + col, p.out_dtype);
-                            store_elem(p.c, row * p.ldc + col, p.out_dtype, x);
-                        }
-                    }
-                }
+                tmem_ld32(tmem + ab * BN + (static_cast<std::uint32_t>(quarter * 32) << 16) + static_cast<std::uint32_t>(c * 32),
+                          v);
+                const unsigned long long col0 = static_cast<unsigned long long>(n0 + c * 32);
+                if (row < p.m && col0 < p.n) store_chunk(p, row, col0, v);
             }
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
         }
     }
     if (fault) atomicOr(&g_gemm_fault, 1u);
@@ -216,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     if (warp == 1) {
         tmem_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
     }
 }
 
@@ -262,18 +332,23 @@ cudaError_t prepare_gemm() {
 }
 
 template <int BN>
-cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream) {
+cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, int sm_count, cudaStream_t stream) {
     const cudaError_t e = prepare_gemm<BN>();
     if (e != cudaSuccess) return e;
-    const dim3 grid(static_cast<unsigned>((p.n + BN - 1) / BN), static_cast<unsigned>((p.m + kBM - 1) / kBM));
+    p.tiles_m = static_cast<int>((p.m + kBM - 1) / kBM);
+    p.tiles_n = static_cast<int>((p.n + BN - 1) / BN);
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+    const unsigned grid = static_cast<unsigned>(tiles < sm_count ? tiles : sm_count); // one CTA per SM (TMEM: 2 x BN columns)
     void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), &p};
-    return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), grid, dim3(kThreads), args, gemm_smem<BN>(),
-                            stream);
+    return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), args,
+                            gemm_smem<BN>(), stream);
 }
 
 } // namespace
 
 cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const unsigned bn = a.n <= 64 ? 64u : a.n <= 128 ? 128u : 256u;
     CUtensorMap ta{}, tb{};
     if (!kmajor_map(&ta, a.in_dtype, a.a, a.k, a.m, a.lda, kBM) || !kmajor_map(&tb, a.in_dtype, a.b, a.k, a.n, a.ldb, bn))
@@ -283,9 +358,11 @@ cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     p.m = a.m; p.n = a.n; p.k = a.k; p.ldc = a.ldc; p.ldr = a.residual ? a.ldr : 0;
     p.out_dtype = a.out_dtype; p.in_dtype = a.in_dtype;
     p.kblocks = static_cast<int>((a.k + kBK - 1) / kBK);
-    if (bn == 64) return launch_bn<64>(ta, tb, p, stream);
-    if (bn == 128) return launch_bn<128>(ta, tb, p, stream);
-    return launch_bn<256>(ta, tb, p, stream);
+    const std::size_t eo = a.out_dtype == SACC_DTYPE_F32 ? 4 : 2;
+    p.vec_store = (reinterpret_cast<std::uintptr_t>(a.c) % 16 == 0) && ((a.ldc * eo) % 16 == 0);
+    if (bn == 64) return launch_bn<64>(ta, tb, p, sms, stream);
+    if (bn == 128) return launch_bn<128>(ta, tb, p, sms, stream);
+    return launch_bn<256>(ta, tb, p, sms, stream);
 }
 
 cudaError_t load_gemm_kernels(std::string& report) {

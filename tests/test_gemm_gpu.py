@@ -25,7 +25,7 @@ def check(c, ref, mag, out_dtype):
 
 
 @pytest.mark.parametrize("shape", [(256, 512, 128), (200, 40, 256), (300, 1000, 520), (8192, 512, 128), (128, 64, 64),
-                                   (1000, 256, 2048)])
+                                   (1000, 256, 2048), (16384, 2048, 320), (5000, 700, 72)])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_gemm_matches_fp32_reference(shape, dt):
     m, n, k = shape

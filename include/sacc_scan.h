@@ -242,6 +242,23 @@ typedef struct SaccMambaBlockArgs {
 int sacc_mamba_block_workspace(const SaccMambaBlockArgs* args, size_t* bytes);
 int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * sacc_mamba_block_forward_noalloc -- no counterpart in the reference.
+ *
+ * The same block forward for callers that cannot allocate a workspace (a
+ * plugin that the engine gives no workspace and that may not allocate inside
+ * enqueue; a per-frame loop under a fixed memory budget).  The intermediates
+ * go to one static device array of SACC_NOALLOC_SCRATCH_BYTES per device,
+ * reserved when CUDA loads the library's module; the call allocates nothing.
+ * Blocks whose sacc_mamba_block_workspace exceeds that size are rejected with
+ * SACC_EINVAL.  The first call on a device looks up the array's address:
+ * make it before any stream capture.  All calls on a device share the array
+ * (it keeps the last call's contents; nothing needs to start at zero), so
+ * calls that overlap on the GPU race: order them on one stream.
+ * ------------------------------------------------------------------------ */
+#define SACC_NOALLOC_SCRATCH_BYTES ((size_t)24 << 20)
+int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

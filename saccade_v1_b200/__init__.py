@@ -16,6 +16,7 @@ from .scan import (  # noqa: F401
     identity,
     load_kernels,
     mamba_block_forward,
+    mamba_block_forward_noalloc,
     mamba_block_workspace,
     scan_fault,
     selective_scan_cuda,

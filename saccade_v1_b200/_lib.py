@@ -31,6 +31,7 @@ EXPORTS = (
     "sacc_gemm",
     "sacc_mamba_block_workspace",
     "sacc_mamba_block_forward",
+    "sacc_mamba_block_forward_noalloc",
 )
 
 
@@ -120,6 +121,8 @@ def load() -> ctypes.CDLL:
     L.sacc_mamba_block_workspace.restype = i
     L.sacc_mamba_block_forward.argtypes = [ctypes.POINTER(MambaBlockArgs), vp, sz, vp]
     L.sacc_mamba_block_forward.restype = i
+    L.sacc_mamba_block_forward_noalloc.argtypes = [ctypes.POINTER(MambaBlockArgs), vp]
+    L.sacc_mamba_block_forward_noalloc.restype = i
     _lib = L
     return L
 

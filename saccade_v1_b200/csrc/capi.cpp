@@ -440,4 +440,18 @@ int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, si
     });
 }
 
+int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "mamba_block_noalloc";
+        if (args == nullptr) reject(api, "args are required");
+        require_stream(api, stream);
+        check_block(api, *args);
+        const std::size_t need = mamba_block_workspace(*args);
+        if (need > kNoAllocScratchBytes)
+            reject(api, "needs " + std::to_string(need) + " bytes of scratch, more than the static maximum of " +
+                            std::to_string(kNoAllocScratchBytes) + "; use sacc_mamba_block_forward with a workspace");
+        CK(launch_mamba_block_noalloc(*args, stream));
+    });
+}
+
 } // extern "C"

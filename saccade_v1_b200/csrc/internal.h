@@ -67,6 +67,11 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
 cudaError_t load_block_kernels(std::string& report);
 std::size_t mamba_block_workspace(const SaccMambaBlockArgs& a);
 cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cudaStream_t stream);
+// Same forward with the intermediates in a static device array of
+// kNoAllocScratchBytes (block_noalloc.cu); cudaErrorInvalidValue when the
+// block needs more.
+constexpr std::size_t kNoAllocScratchBytes = SACC_NOALLOC_SCRATCH_BYTES;
+cudaError_t launch_mamba_block_noalloc(const SaccMambaBlockArgs& a, cudaStream_t stream);
 cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);

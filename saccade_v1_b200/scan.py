@@ -266,3 +266,17 @@ def mamba_block_forward(x, params, *, eps=1e-5, residual=True, out=None, workspa
     _check(_lib.load().sacc_mamba_block_forward(ctypes.byref(args), base + off, workspace.numel() - off,
                                                 _stream_handle(stream)))
     return out
+
+
+def mamba_block_forward_noalloc(x, params, *, eps=1e-5, residual=True, out=None, stream=None):
+    """mamba_block_forward with the intermediates in the library's static
+    device scratch (SACC_NOALLOC_SCRATCH_BYTES per device) instead of a
+    workspace: the call allocates nothing on the device when `out` is given.
+    All calls on a device share that scratch, so calls that overlap on the
+    GPU race; order them on one stream.  The first call on a device does the
+    scratch set-up and should come before any stream capture."""
+    if out is None:
+        out = torch.empty_like(x)
+    args = _block_args(x, params, eps, residual, out)
+    _check(_lib.load().sacc_mamba_block_forward_noalloc(ctypes.byref(args), _stream_handle(stream)))
+    return out

@@ -75,6 +75,7 @@ cudaError_t launch_mamba_block_noalloc(const SaccMambaBlockArgs& a, cudaStream_t
 cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);
+cudaError_t read_step_fault(unsigned* out, bool clear);
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).

@@ -74,22 +74,6 @@ struct BulkParams {
     int a_shared, c_full, has_d, softplus, nchunks;
 };
 
-// softplus(x) = max(x, 0) + log1p(e^-|x|), log1p(e) = e * P(e) on e in (0, 1]
-// (degree-7 least-squares fit, relative error 3.2e-7 in FP32); x > 20 passes
-// through as in the reference (src/selective_scan.cpp:123).
-__device__ __forceinline__ float softplus_bulk(float x) {
-    const float e = fast_exp2(-fabsf(x) * kLog2e);
-    float q = fmaf(-8.336497e-3f, e, 4.337085e-2f);
-    q = fmaf(q, e, -1.0667790e-1f);
-    q = fmaf(q, e, 1.7675494e-1f);
-    q = fmaf(q, e, -2.4470469e-1f);
-    q = fmaf(q, e, 3.3271188e-1f);
-    q = fmaf(q, e, -4.9997127e-1f);
-    q = fmaf(q, e, 9.9999976e-1f);
-    const float r = fmaf(e, q, fmaxf(x, 0.0f));
-    return x > 20.0f ? x : r;
-}
-
 template <typename T>
 __device__ __forceinline__ float2 unpack2(std::uint32_t w);
 template <>
@@ -294,7 +278,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             for (int j = 0; j < 8; ++j) {
                 const int t = q * 8 + j;
                 const float xv = blk.x[j] + bias;
-                const float dt = p.softplus ? softplus_bulk(xv) : xv;
+                const float dt = p.softplus ? softplus_poly(xv) : xv;
                 const float du = dt * blk.u[j];
                 const float4* bcv = reinterpret_cast<const float4*>(sm.bc[t]);
                 float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};

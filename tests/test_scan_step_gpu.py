@@ -116,6 +116,97 @@ def test_slot_map_updates_only_named_rows():
     assert np.array_equal(got[untouched], table[untouched])
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_step16_rank1_c_groups_shared_a_ragged(dt):
+    """The 16-bit N = 16 path with rank-1 C, 3 groups, one shared A row and a
+    lane count that fills no whole grid."""
+    nseq, D, N, G = 37, 384, 16, 3
+    t = make(41, nseq, D, N, dt, G=G, c_full=False)
+    t["A"] = t["A"][:1].copy() * 0.37
+    state = torch.from_numpy(t["h0"].copy()).cuda()
+    y = gpu_step(t, dt, state)
+    u = t["u"][:, None, :]
+    ry, rh = oracle.scan_ex(u, t["delta"][:, None, :], t["A"], t["b"][:, None], t["c"][:, None], layout="BLD", d=t["D"],
+                            z=t["z"][:, None, :], delta_bias=t["bias"], h0=t["h0"], want_final=True, groups=G,
+                            c_width=1)
+    assert np.all(np.abs(y - ry[:, 0, :]) <= 1e-3 + 1e-2 * np.abs(ry[:, 0, :]))
+    np.testing.assert_allclose(state.cpu().numpy(), rh, rtol=1e-4, atol=1e-5)
+
+
+def offset_view(t):
+    """The same values at an address 2 bytes past a 16-byte boundary."""
+    wide = torch.zeros(t.numel() + 1, dtype=t.dtype, device=t.device)
+    wide[1:] = t.reshape(-1)
+    return wide[1:].view(t.shape)
+
+
+def step_variants(t, dt, table, slot, G=1):
+    """The same step through the three kernels: TMA-pipelined (all operands
+    16-byte aligned), one-thread-per-lane (z 2 bytes off a 16-byte boundary,
+    which the pipelined kernel's bulk copies cannot take) and the generic
+    four-threads-per-lane kernel (B 2 bytes off, which rules out both)."""
+    s = torch.cuda.Stream()
+    outs = []
+    with torch.cuda.stream(s):
+        g = lambda k: torch.from_numpy(np.ascontiguousarray(t[k])).to(device="cuda", dtype=TORCH[dt])
+        f = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+        slot = None if slot is None else torch.from_numpy(slot).cuda()
+        b, z = g("b"), g("z")
+        for bb, zz in ((b, z), (b, offset_view(z)), (offset_view(b), z)):
+            st = torch.from_numpy(table.copy()).cuda()
+            y = sb.selective_scan_step(g("u"), g("delta"), f(t["A"]), bb, g("c"), st, D=f(t["D"]), z=zz,
+                                       delta_bias=f(t["bias"]), slot=slot, stream=s)
+            outs.append((y, st))
+    s.synchronize()
+    return outs
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_step_kernels_agree_bitwise(dt):
+    """All three step kernels apply the same operations in the same order, so
+    outputs and states agree bit for bit.  Slot map with an arbitrary negative
+    entry and an out-of-table one (both skipped, y = 0)."""
+    nseq, D, N, slots = 300, 256, 16, 310
+    t = make(43, nseq, D, N, dt)
+    rng = np.random.default_rng(44)
+    rows = rng.permutation(slots)[:nseq].astype(np.int32)
+    rows[5], rows[9] = -7, slots + 3
+    table = (rng.standard_normal((slots, D, N)) * 0.5).astype(np.float32)
+    outs = step_variants(t, dt, table, rows)
+    y0, s0 = outs[0]
+    for y1, s1 in outs[1:]:
+        assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+        assert torch.equal(s0.view(torch.int32), s1.view(torch.int32))
+    assert bool((y0[5] == 0).all()) and bool((y0[9] == 0).all())
+    untouched = sorted(set(range(slots)) - set(int(r) for r in rows if 0 <= r < slots))
+    assert np.array_equal(s0.cpu().numpy()[untouched], table[untouched])
+    ry, rh = oracle_step(t, table[np.clip(rows, 0, slots - 1)])
+    live = [i for i, r in enumerate(rows) if 0 <= r < slots]
+    yv = y0.float().cpu().numpy()
+    assert np.all(np.abs(yv[live] - ry[live]) <= 1e-3 + 1e-2 * np.abs(ry[live]))
+    np.testing.assert_allclose(s0.cpu().numpy()[rows[live]], rh[live], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_step_pipe_partial_channel_block_and_groups(dt):
+    """384 channels = one full and one half 256-channel tile (rows past the
+    table's channels are zero-filled on load and not stored), 3 groups."""
+    nseq, D, N, G = 260, 384, 16, 3
+    t = make(47, nseq, D, N, dt, G=G)
+    outs = step_variants(t, dt, t["h0"], None, G)
+    y0, s0 = outs[0]
+    for y1, s1 in outs[1:]:
+        assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+        assert torch.equal(s0.view(torch.int32), s1.view(torch.int32))
+    u = t["u"][:, None, :]
+    ry, rh = oracle.scan_ex(u, t["delta"][:, None, :], t["A"], t["b"][:, None], t["c"][:, None], layout="BLD", d=t["D"],
+                            z=t["z"][:, None, :], delta_bias=t["bias"], h0=t["h0"], want_final=True, groups=G)
+    yv = y0.float().cpu().numpy()
+    assert np.all(np.abs(yv - ry[:, 0, :]) <= 1e-3 + 1e-2 * np.abs(ry[:, 0, :]))
+    np.testing.assert_allclose(s0.cpu().numpy(), rh, rtol=1e-4, atol=1e-5)
+    assert sb.scan_fault() == 0
+
+
 def test_config3_scale_property():
     """Config 3 size (4096 tracks x 256 x 16, fp16): sampled tracks against the oracle."""
     nseq, D, N = 4096, 256, 16

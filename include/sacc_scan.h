@@ -137,7 +137,9 @@ int sacc_scan_fault(uint32_t* out, int clear);
  * h0 / h_final (nseq, channels, state) FP32, each optional.
  * cu_seqlens (nseq + 1 int32, batch must be 1): sequence k is tokens
  * [cu_seqlens[k], cu_seqlens[k+1]) of the length axis and starts from h0[k]
- * (or zero); without cu_seqlens nseq = batch.
+ * (or zero); without cu_seqlens nseq = batch.  The entries are device data and
+ * are not checked on the host: each is clamped to [0, length], and a
+ * sequence whose end precedes its start is empty.
  * No status words: non-finite values propagate into y as IEEE arithmetic does.
  * Pointers of 16-bit tensors must be 16-byte aligned and channels * 2 bytes
  * (BLD) or length * 2 bytes (BDL) a multiple of 16, for the TMA staging.

@@ -69,6 +69,8 @@ constexpr size_t smem_bytes() {
 struct BulkParams {
     const float *a, *d, *bias, *h0;
     float* h_final;
+    const int32_t* cu; // packed varlen sequences ((B, L, D) with batch 1), else null
+    void* y;           // plain stores of a varlen sequence's last, partial chunk
     unsigned long long length, channels, per_group;
     unsigned groups;
     int a_shared, c_full, has_d, softplus, nchunks;
@@ -159,16 +161,16 @@ __device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const floa
     for (int j = 0; j < 8; ++j) y[(q * 8 + j) * kLanes + tid] = from_f32<T>(out[j]);
 }
 
-// Loads of one chunk into stage s.  (B, D, L): 2D maps, x = token, y = row
-// (b * D + d).  (B, L, D): 3D maps (channel, token, batch), so that a chunk
-// past the end of a sequence reads zeros instead of the next sequence.
+// Loads of the chunk starting at token t0 into stage s.  (B, D, L): 2D maps,
+// x = token, y = row (b * D + d).  (B, L, D): 3D maps (channel, token, batch),
+// so that a chunk past the end of a sequence reads zeros instead of the next
+// sequence; a packed varlen sequence reads whatever follows it, unused.
 template <typename T, bool kBDL, bool kHasZ>
-__device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int chunk, int row0, int brow0, int crow0, int bb,
+__device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
                                             std::uint32_t c_bytes, const CUtensorMap* tu, const CUtensorMap* td,
                                             const CUtensorMap* tz, const CUtensorMap* tb, const CUtensorMap* tc) {
     constexpr std::uint32_t tile = kLanes * kT * sizeof(T), btile = kN * kT * sizeof(T);
     mbar_arrive_expect_tx(&sm.full[s], tile * (kHasZ ? 3u : 2u) + btile + c_bytes);
-    const int t0 = chunk * kT;
     if (kBDL) {
         tma_load_2d(sm.u[s], tu, &sm.full[s], t0, row0);
         tma_load_2d(sm.dl[s], td, &sm.full[s], t0, row0);
@@ -181,6 +183,46 @@ __device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int chunk
         if constexpr (kHasZ) tma_load_3d(sm.z[s], tz, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
         tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
+    }
+}
+
+// Eight tokens of one lane through the recurrence; with kGuard only the first
+// `count` (fewer in a sequence's last, partial block; the others are left out
+// of the state).
+template <bool kFullC, bool kHasZ, bool kGuard>
+__device__ __forceinline__ void scan_block8(const float (*bc)[2 * kN], int q, int count, const Block8& blk, const float (&a)[kN],
+                                            float (&h)[kN], float bias, float dskip, int softplus, float (&out)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        out[j] = 0.0f;
+        if (kGuard && j >= count) continue;
+        const int t = q * 8 + j;
+        const float xv = blk.x[j] + bias;
+        const float dt = softplus ? softplus_poly(xv) : xv;
+        const float du = dt * blk.u[j];
+        const float4* bcv = reinterpret_cast<const float4*>(bc[t]);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float cr = kFullC ? 0.0f : bc[t][kN];
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 bq = bcv[k4];
+            const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
+            float cc[4] = {cr, cr, cr, cr};
+            if constexpr (kFullC) {
+                const float4 cq = bcv[4 + k4];
+                cc[0] = cq.x; cc[1] = cq.y; cc[2] = cq.z; cc[3] = cq.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int n = 4 * k4 + i;
+                const float decay = fast_exp2(dt * a[n]);
+                h[n] = fmaf(decay, h[n], du * bb[i]);
+                acc[i] = fmaf(cc[i], h[n], acc[i]);
+            }
+        }
+        float y = fmaf(dskip, blk.u[j], (acc[0] + acc[1]) + (acc[2] + acc[3]));
+        if constexpr (kHasZ) y *= silu(blk.z[j]);
+        out[j] = y;
     }
 }
 
@@ -201,9 +243,19 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     const unsigned long long lane = b * D + d;
     const unsigned long long g = d0 / p.per_group;
     const int cw = kFullC ? kN : 1;
+    // Token range: the whole row, or packed sequence b ((B, L, D), batch 1),
+    // its cu_seqlens entries clamped to [0, L] so no access leaves the tensors.
+    unsigned long long tok0 = 0, len = L;
+    if (!kBDL && p.cu) {
+        const long long lo = p.cu[b], hi = p.cu[b + 1];
+        tok0 = lo < 0 ? 0 : (static_cast<unsigned long long>(lo) > L ? L : static_cast<unsigned long long>(lo));
+        const unsigned long long end = hi < 0 ? 0 : (static_cast<unsigned long long>(hi) > L ? L : static_cast<unsigned long long>(hi));
+        len = end > tok0 ? end - tok0 : 0;
+    }
+    const int nchunks = (!kBDL && p.cu) ? static_cast<int>((len + kT - 1) / kT) : p.nchunks;
     // Tensor-map coordinates of this CTA.
     const int row0 = kBDL ? static_cast<int>(b * D + d0) : static_cast<int>(d0);
-    const int bb = static_cast<int>(b);
+    const int bb = (!kBDL && p.cu) ? 0 : static_cast<int>(b);
     const int brow0 = kBDL ? static_cast<int>((b * p.groups + g) * kN) : static_cast<int>(g * kN);
     const int crow0 = kBDL ? static_cast<int>((b * p.groups + g) * cw) : static_cast<int>(g * cw);
     const std::uint32_t c_bytes = static_cast<std::uint32_t>(cw) * kT * sizeof(T);
@@ -219,8 +271,9 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     }
     __syncthreads();
     if (tid == 0)
-        for (int s = 0; s < kStages && s < p.nchunks; ++s)
-            issue_chunk<T, kBDL, kHasZ>(sm, s, s, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+        for (int s = 0; s < kStages && s < nchunks; ++s)
+            issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(tok0) + s * kT, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d,
+                                        &tm_z, &tm_b, &tm_c);
 
     // Per-lane constants: A * log2(e), D, dt bias, initial state.
     float a[kN], h[kN];
@@ -234,7 +287,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     const float bias = p.bias ? p.bias[d] : 0.0f;
 
     bool fault = false;
-    for (int chunk = 0; chunk < p.nchunks; ++chunk) {
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
         const int s = chunk % kStages;
         const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((chunk / kStages) & 1));
         if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
@@ -264,57 +317,39 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         }
         __syncthreads();
 
-        // Tokens past the end of the sequence (zero-filled by the TMA) are not
-        // run through the recurrence; L is a multiple of 8.
-        const int valid = static_cast<int>(L - static_cast<unsigned long long>(chunk) * kT);
-        const int blocks8 = (valid < kT ? valid : kT) / 8;
+        // Tokens past the end of the sequence (zero-filled by the TMA, or the
+        // next packed sequence) are not run through the recurrence.
+        const unsigned long long left = len - static_cast<unsigned long long>(chunk) * kT;
+        const int valid = static_cast<int>(left < kT ? left : kT);
+        const int blocks8 = (valid + 7) / 8;
 #pragma unroll 1
         for (int q = 0; q < blocks8; ++q) {
             Block8 blk;
             if (kBDL) load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
             else load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
             float out[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int t = q * 8 + j;
-                const float xv = blk.x[j] + bias;
-                const float dt = p.softplus ? softplus_poly(xv) : xv;
-                const float du = dt * blk.u[j];
-                const float4* bcv = reinterpret_cast<const float4*>(sm.bc[t]);
-                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const float cr = kFullC ? 0.0f : sm.bc[t][kN];
-#pragma unroll
-                for (int k4 = 0; k4 < 4; ++k4) {
-                    const float4 bq = bcv[k4];
-                    const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
-                    float cc[4] = {cr, cr, cr, cr};
-                    if constexpr (kFullC) {
-                        const float4 cq = bcv[4 + k4];
-                        cc[0] = cq.x; cc[1] = cq.y; cc[2] = cq.z; cc[3] = cq.w;
-                    }
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int n = 4 * k4 + i;
-                        const float decay = fast_exp2(dt * a[n]);
-                        h[n] = fmaf(decay, h[n], du * bb[i]);
-                        acc[i] = fmaf(cc[i], h[n], acc[i]);
-                    }
-                }
-                float y = fmaf(dskip, blk.u[j], (acc[0] + acc[1]) + (acc[2] + acc[3]));
-                if constexpr (kHasZ) y *= silu(blk.z[j]);
-                out[j] = y;
-            }
+            scan_block8<kFullC, kHasZ, true>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out);
             if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
             else store_block_bld<T>(sm.y, tid, q, out);
         }
         fence_async_shared();
         __syncthreads();
+        const int tc0 = static_cast<int>(tok0) + chunk * kT;
+        const bool tail = !kBDL && p.cu && valid < kT;
+        if (tail) {
+            // A packed sequence's partial last chunk: a tile store would also
+            // write the next sequence's rows, so store the valid rows only.
+            T* yg = static_cast<T*>(p.y);
+            for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
+        }
         if (tid == 0) {
-            if (kBDL) tma_store_2d(&tm_y, sm.y, chunk * kT, row0);
-            else tma_store_3d(&tm_y, sm.y, row0, chunk * kT, bb);
+            if (!tail) {
+                if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, row0);
+                else tma_store_3d(&tm_y, sm.y, row0, tc0, bb);
+            }
             bulk_commit();
-            if (chunk + kStages < p.nchunks)
-                issue_chunk<T, kBDL, kHasZ>(sm, s, chunk + kStages, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z,
+            if (chunk + kStages < nchunks)
+                issue_chunk<T, kBDL, kHasZ>(sm, s, tc0 + kStages * kT, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z,
                                             &tm_b, &tm_c);
         }
     }
@@ -418,10 +453,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15
 // strides for the TMA ((B, D, L): L % 8 == 0; (B, L, D): a full-width C, whose
 // rows are then 16 * groups * 2 bytes).  Other calls use the general kernel.
 bool bulk_eligible(const SaccScanExArgs& a) {
-    if ((a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) || a.state != kN || a.cu_seqlens != nullptr ||
-        a.length == 0 || a.groups == 0 || a.channels % kLanes != 0 || (a.channels / a.groups) % kLanes != 0)
+    if ((a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) || a.state != kN || a.length == 0 || a.groups == 0 ||
+        a.channels % kLanes != 0 || (a.channels / a.groups) % kLanes != 0)
         return false;
-    if (a.layout == SACC_LAYOUT_BDL) {
+    if (a.cu_seqlens != nullptr) {
+        // Packed varlen: (B, L, D) with batch 1, any sequence lengths.
+        if (a.layout != SACC_LAYOUT_BLD || a.batch != 1 || a.c_width != kN || a.channels % 8 != 0 || a.nseq <= 0 ||
+            static_cast<unsigned long long>(a.nseq) * (a.channels / kLanes) > 0x7fffffffull)
+            return false;
+    } else if (a.layout == SACC_LAYOUT_BDL) {
         if (a.length % 8 != 0) return false;
     } else if (a.layout == SACC_LAYOUT_BLD) {
         if (a.c_width != kN || a.length % 8 != 0 || a.channels % 8 != 0) return false;
@@ -460,11 +500,14 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream) {
     p.length = L; p.channels = D; p.per_group = D / G; p.groups = static_cast<unsigned>(G);
     p.a_shared = a.a_rows == 1; p.c_full = cw != 1; p.has_d = a.d != nullptr; p.softplus = a.delta_softplus != 0;
     p.nchunks = static_cast<int>((L + kT - 1) / kT);
+    p.cu = bdl ? nullptr : a.cu_seqlens;
+    p.y = a.y;
+    const unsigned long long rows = a.cu_seqlens ? static_cast<unsigned long long>(a.nseq) : B; // sequences
     const Pick k = pick(a.dtype, bdl, a.z != nullptr, cw != 1);
     const cudaError_t attr = k.prepare();
     if (attr != cudaSuccess) return attr;
     void* args[] = {&tu, &td, &tz, &tb, &tc, &ty, &p};
-    return cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(B * D / kLanes)), dim3(kLanes), args, k.smem, stream);
+    return cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(rows * D / kLanes)), dim3(kLanes), args, k.smem, stream);
 }
 
 cudaError_t load_scan_bulk_kernels(std::string& report) {

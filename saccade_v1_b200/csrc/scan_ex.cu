@@ -38,8 +38,11 @@ __global__ void __launch_bounds__(kThreads) scan_ex_kernel(ExParams p) {
     const unsigned long long D = p.channels, L = p.length, G = p.groups;
     const unsigned long long seq = lane / D, d = lane % D, g = d / p.per_group;
     const unsigned long long bb = p.cu ? 0 : seq;
-    const unsigned long long t0 = p.cu ? static_cast<unsigned long long>(p.cu[seq]) : 0;
-    const unsigned long long t1 = p.cu ? static_cast<unsigned long long>(p.cu[seq + 1]) : L;
+    // cu_seqlens entries clamped to [0, L] (and t1 >= t0) so no access leaves the tensors.
+    auto clamp_tok = [L](long long v) { return v < 0 ? 0ull : (static_cast<unsigned long long>(v) > L ? L : static_cast<unsigned long long>(v)); };
+    const unsigned long long t0 = p.cu ? clamp_tok(p.cu[seq]) : 0;
+    const unsigned long long t1r = p.cu ? clamp_tok(p.cu[seq + 1]) : L;
+    const unsigned long long t1 = t1r < t0 ? t0 : t1r;
     const T* u = static_cast<const T*>(p.u);
     const T* dl = static_cast<const T*>(p.delta);
     const T* z = static_cast<const T*>(p.z);

@@ -257,3 +257,62 @@ def ctypes_fault():
     v = ctypes.c_uint32(0)
     assert _lib.load().sacc_scan_fault(ctypes.byref(v), 0) == 0
     return v.value
+
+
+# ---------------------------------------------------------------- bulk varlen
+# Packed sequences ((1, total, D) with cu_seqlens, 16-bit, N = 16, D a multiple
+# of 128): the bulk kernel with one CTA per (sequence, 128 channels).
+
+def packed(seed, lens, D, dt, G=1):
+    t = make(seed, 1, int(sum(lens)), D, 16, G, "BLD", dt)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    return t, cu
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_bulk_varlen_matches_oracle(dt):
+    lens = [1, 7, 8, 9, 31, 32, 33, 64, 65, 100, 3, 17, 40, 2, 56, 71]
+    D = 256
+    t, cu = packed(31, lens, D, dt)
+    h0 = (np.random.default_rng(32).standard_normal((len(lens), D, 16)) * 0.5).astype(np.float32)
+    y, hf = gpu_run(t, dt, "BLD", h0=h0, want_final=True, cu=list(cu))
+    ref, hr, _ = oracle_run(t, "BLD", h0=h0, want_final=True, cu=cu)
+    check_16bit(f"bulk_varlen_{dt}", y, ref)
+    np.testing.assert_allclose(hf, hr, rtol=1e-3, atol=1e-3)
+    assert ctypes_fault() == 0
+
+
+def test_bulk_varlen_bitwise_equals_separate_calls():
+    """Sequences of multiple-of-8 lengths through one packed call and through
+    one unpacked bulk call each: the same kernel arithmetic, the same bits."""
+    lens, D = [8, 16, 40, 64, 72], 384
+    t, cu = packed(33, lens, D, "bf16", G=3)
+    h0 = (np.random.default_rng(34).standard_normal((len(lens), D, 16)) * 0.5).astype(np.float32)
+    y, hf = gpu_run(t, "bf16", "BLD", h0=h0, want_final=True, cu=list(cu))
+    for k, (a, b) in enumerate(zip(cu[:-1], cu[1:])):
+        part = dict(t, u=t["u"][:, a:b].copy(), delta=t["delta"][:, a:b].copy(), z=t["z"][:, a:b].copy(),
+                    b=t["b"][:, a:b].copy(), c=t["c"][:, a:b].copy())
+        y1, h1 = gpu_run(part, "bf16", "BLD", h0=h0[k:k + 1], want_final=True)
+        assert np.array_equal(y[:, a:b].view(np.uint32), y1.view(np.uint32)), k
+        assert np.array_equal(hf[k:k + 1].view(np.uint32), h1.view(np.uint32)), k
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_varlen_entries_are_clamped(dt):
+    """cu_seqlens past the end or below zero are clamped to [0, length]; a
+    sequence whose end precedes its start is empty (its final state is h0).
+    f32 takes the general kernel, bf16 with D = 256 the bulk kernel."""
+    D, L = 256, 100
+    t = make(35, 1, L, D, 16, 1, "BLD", dt)
+    h0 = (np.random.default_rng(36).standard_normal((4, D, 16)) * 0.5).astype(np.float32)
+    y, hf = gpu_run(t, dt, "BLD", h0=h0, want_final=True, cu=[0, 30, 30, 500, -5])
+    ref, hr, scale = oracle_run(t, "BLD", h0=h0, want_final=True, cu=np.array([0, 30, 30, 100, 100], np.int32))
+    if dt == "f32":
+        check_f32("clamped", y, ref, scale)
+        np.testing.assert_allclose(hf, hr, rtol=1e-5, atol=1e-5)
+    else:
+        check_16bit("clamped", y, ref)
+        np.testing.assert_allclose(hf, hr, rtol=1e-3, atol=1e-3)
+    np.testing.assert_array_equal(hf[1], h0[1])
+    np.testing.assert_array_equal(hf[3], h0[3])
+    assert ctypes_fault() == 0

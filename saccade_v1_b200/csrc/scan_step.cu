@@ -449,9 +449,13 @@ bool state_map(CUtensorMap* map, float* state, unsigned long long channels, unsi
 
 template <typename T>
 cudaError_t prepare_pipe() {
-    static const cudaError_t status = cudaFuncSetAttribute(reinterpret_cast<const void*>(step16_pipe_kernel<T>),
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                           static_cast<int>(pipe_smem_bytes<T>()));
+    static const cudaError_t status = [] {
+        const void* fn = reinterpret_cast<const void*>(step16_pipe_kernel<T>);
+        const cudaError_t e =
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pipe_smem_bytes<T>()));
+        if (e != cudaSuccess) return e;
+        return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    }();
     return status;
 }
 

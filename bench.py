@@ -374,57 +374,73 @@ def time_device(torch, stream, fn, iters: int, warmup: int = 3) -> float:
     return e0.elapsed_time(e1) * 1e3 / iters
 
 
-def secondary(torch, device, stream, peak):
-    """Other rows of the hot path, device-timed on this GPU (not part of `value`)."""
-    import saccade_v1_b200 as sb
-    out = {}
+def c3_inputs(torch, device, stream):
+    """Config 3 tensors: 4096 tracks' activations (fp16) and carried state (256 x 16 FP32 each), plus the
+    packed histories (lengths U{1..64}) of a full re-scan."""
     g = torch.Generator(device=device)
     g.manual_seed(77)
+    T3, D3, N3 = 4096, 256, 16
+    f16 = torch.float16
     with torch.cuda.stream(stream):
-        # Config 3: one per-frame L = 1 step of 4096 tracks' carried state (256 x 16 FP32 each), fp16 activations.
-        T3, D3, N3 = 4096, 256, 16
-        f16 = torch.float16
-        u = torch.randn(T3, D3, device=device, generator=g).to(f16)
-        dl = torch.randn(T3, D3, device=device, generator=g).to(f16)
-        z = torch.randn(T3, D3, device=device, generator=g).to(f16)
-        bm = torch.randn(T3, N3, device=device, generator=g).to(f16)
-        cm = torch.randn(T3, N3, device=device, generator=g).to(f16)
-        A = -torch.arange(1, N3 + 1, dtype=torch.float32, device=device).repeat(D3, 1).contiguous()
-        Dv = torch.ones(D3, device=device)
-        bias = torch.full((D3,), -4.6, device=device)
-        state = torch.randn(T3, D3, N3, device=device, generator=g) * 0.5
-        y = torch.empty_like(u)
-        step = lambda: sb.selective_scan_step(u, dl, A, bm, cm, state, D=Dv, z=z, delta_bias=bias, out=y, stream=stream)
-        us = time_device(torch, stream, step, 50)
-        nbytes = 2 * state.numel() * 4 + 4 * u.numel() * 2 + 2 * bm.numel() * 2 + 4 * (A.numel() + 2 * D3)
-        out["c3_step"] = {"us": round(us, 2), "tracks_frames_per_s": round(T3 / (us * 1e-6), 1),
-                          "GB_per_s": round(nbytes / (us * 1e-6) / 1e9, 1),
-                          "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4), "bytes": nbytes,
-                          "workload": "4096 tracks, D=256, N=16, fp16 acts, fp32 carried state, gate+bias+D"}
-        # Config 3: full packed re-scan of the histories (lengths U{1..64}) with cu_seqlens.
-        rng = np.random.default_rng(3)
-        lens = rng.integers(1, 65, T3)
-        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=device)
+        t = {"u": torch.randn(T3, D3, device=device, generator=g).to(f16),
+             "dl": torch.randn(T3, D3, device=device, generator=g).to(f16),
+             "z": torch.randn(T3, D3, device=device, generator=g).to(f16),
+             "bm": torch.randn(T3, N3, device=device, generator=g).to(f16),
+             "cm": torch.randn(T3, N3, device=device, generator=g).to(f16),
+             "A": -torch.arange(1, N3 + 1, dtype=torch.float32, device=device).repeat(D3, 1).contiguous(),
+             "Dv": torch.ones(D3, device=device), "bias": torch.full((D3,), -4.6, device=device),
+             "state": torch.randn(T3, D3, N3, device=device, generator=g) * 0.5}
+        t["y"] = torch.empty_like(t["u"])
+        lens = np.random.default_rng(3).integers(1, 65, T3)
+        t["cu"] = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=device)
         tot = int(lens.sum())
-        ur = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
-        dr = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
-        zr = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
-        br = torch.randn(1, tot, 1, N3, device=device, generator=g).to(f16)
-        cr = torch.randn(1, tot, 1, N3, device=device, generator=g).to(f16)
-        yr = torch.empty_like(ur)
-        hr = torch.empty(T3, D3, N3, device=device)
-        rescan = lambda: sb.selective_scan_ex(ur, dr, A, br, cr, D=Dv, z=zr, delta_bias=bias, h0=state, h_final=hr,
-                                              cu_seqlens=cu, layout="BLD", out=yr, stream=stream)
-        us_r = time_device(torch, stream, rescan, 10)
-        out["c3_rescan"] = {"us": round(us_r, 2), "tokens": tot,
-                            "workload": "4096 packed histories, lengths U{1..64}, BLD fp16, h0 -> h_final"}
-        out["c3_frame_avg_us"] = round(us + us_r / 30.0, 2)
-        out["c3_tracks_frames_per_s"] = round(T3 / ((us + us_r / 30.0) * 1e-6), 1)
-        # Reference ABI at the HR deploy shapes (4 directions x L tokens x 256 channels, N = 16, FP32,
-        # shared A, rank-1 C, D): the reference's published 3-level total is 722.351 us (RTX 5070 Ti laptop).
-        levels = {}
+        for k in ("ur", "dr", "zr"):
+            t[k] = torch.randn(1, tot, D3, device=device, generator=g).to(f16)
+        for k in ("br", "cr"):
+            t[k] = torch.randn(1, tot, 1, N3, device=device, generator=g).to(f16)
+        t["yr"] = torch.empty_like(t["ur"])
+        t["hr"] = torch.empty(T3, D3, N3, device=device)
+    stream.synchronize()
+    return t
+
+
+def c3_step(torch, device, stream, peak):
+    """Config 3: one per-frame L = 1 step of 4096 tracks' carried state."""
+    import saccade_v1_b200 as sb
+    t = c3_inputs(torch, device, stream)
+    step = lambda: sb.selective_scan_step(t["u"], t["dl"], t["A"], t["bm"], t["cm"], t["state"], D=t["Dv"], z=t["z"],
+                                          delta_bias=t["bias"], out=t["y"], stream=stream)
+    us = time_device(torch, stream, step, 50)
+    nbytes = 2 * t["state"].numel() * 4 + 4 * t["u"].numel() * 2 + 2 * t["bm"].numel() * 2 + 4 * (t["A"].numel() + 2 * 256)
+    return {"us": round(us, 2), "tracks_frames_per_s": round(4096 / (us * 1e-6), 1),
+            "GB_per_s": round(nbytes / (us * 1e-6) / 1e9, 1), "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4),
+            "bytes": nbytes, "workload": "4096 tracks, D=256, N=16, fp16 acts, fp32 carried state, gate+bias+D"}
+
+
+def c3_rescan(torch, device, stream, peak):
+    """Config 3: full packed re-scan of the 4096 histories with cu_seqlens, h0 -> h_final."""
+    import saccade_v1_b200 as sb
+    t = c3_inputs(torch, device, stream)
+    rescan = lambda: sb.selective_scan_ex(t["ur"], t["dr"], t["A"], t["br"], t["cr"], D=t["Dv"], z=t["zr"],
+                                          delta_bias=t["bias"], h0=t["state"], h_final=t["hr"], cu_seqlens=t["cu"],
+                                          layout="BLD", out=t["yr"], stream=stream)
+    us = time_device(torch, stream, rescan, 10)
+    tok = t["ur"].shape[1]
+    nbytes = 4 * tok * 256 * 2 + 2 * tok * 16 * 2 + 2 * t["state"].numel() * 4
+    return {"us": round(us, 2), "tokens": tok, "GB_per_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "updates_per_s": round(tok * 256 * 16 / (us * 1e-6), 1),
+            "workload": "4096 packed histories, lengths U{1..64}, BLD fp16, h0 -> h_final"}
+
+
+def hr_deploy(torch, device, stream, peak):
+    """Reference ABI at the HR deploy shapes (4 directions x L tokens x 256 channels, N = 16, FP32, shared A,
+    rank-1 C, D): the reference's published 3-level total is 722.351 us (RTX 5070 Ti laptop GPU)."""
+    import saccade_v1_b200 as sb
+    g = torch.Generator(device=device)
+    g.manual_seed(78)
+    levels, calls = {}, []
+    with torch.cuda.stream(stream):
         st = torch.zeros(2, dtype=torch.int32, device=device)
-        calls = []
         for L_ in (960, 240, 60):
             shape = sb.SelectiveScanShape(4, L_, 256, 16, 1, 1, True)
             uu = torch.randn(4 * L_ * 256, device=device, generator=g) * 2
@@ -437,12 +453,24 @@ def secondary(torch, device, stream, peak):
             call = (lambda s_=shape, a_=(uu, dd, aa, bb, cc, dv, yy): sb.selective_scan_cuda(s_, *a_, st, stream=stream))
             levels[f"HR_L{L_}"] = round(time_device(torch, stream, call, 50), 2)
             calls.append(call)
-        total = time_device(torch, stream, lambda: [c() for c in calls], 50)
-        out["hr_deploy_f32_us"] = dict(levels, total=round(total, 2), reference_published_total_us=722.351,
-                                       note="reference figure is its own CUDA kernel on an RTX 5070 Ti laptop GPU")
-    stream.synchronize()
-    out["c1_block"] = c1_block(torch, device, stream)
-    out["gemm"] = gemm_probe(torch, device, stream)
+    total = time_device(torch, stream, lambda: [c() for c in calls], 50)
+    return dict(levels, total=round(total, 2), reference_published_total_us=722.351,
+                note="reference figure is its own CUDA kernel on an RTX 5070 Ti laptop GPU")
+
+
+def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
+    """Other rows of the hot path, device-timed on this GPU (not part of `value`); `only` runs one of them."""
+    runs = {"c3_step": c3_step, "c3_rescan": c3_rescan, "hr_deploy_f32_us": hr_deploy,
+            "c1_block": lambda *a: c1_block(*a[:3]), "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m)}
+    out = {}
+    for name, fn in runs.items():
+        if only is None or name == only:
+            out[name] = fn(torch, device, stream, peak)
+            stream.synchronize()
+    if "c3_step" in out and "c3_rescan" in out:
+        us, us_r = out["c3_step"]["us"], out["c3_rescan"]["us"]
+        out["c3_frame_avg_us"] = round(us + us_r / 30.0, 2)
+        out["c3_tracks_frames_per_s"] = round(4096 / ((us + us_r / 30.0) * 1e-6), 1)
     return out
 
 
@@ -492,10 +520,11 @@ def c1_block(torch, device, stream):
             "workload": "256 tracks x 32 frames, d_model 128, D 256, N 16, dt_rank 8, fp16, RMSNorm + residual"}
 
 
-def gemm_probe(torch, device, stream):
-    """The tcgen05 projection GEMM at the config-4 in_proj shape of one 8-GPU shard (bf16 in, bf16 out)."""
+def gemm_probe(torch, device, stream, m=64 * 4096):
+    """The tcgen05 projection GEMM at the config-4 in_proj shape of one 8-GPU shard (bf16 in, bf16 out;
+    m = 64 tracks x 4096 tokens, n = 2 x d_inner, k = d_model)."""
     import saccade_v1_b200 as sb
-    m, n, k = 64 * 4096, 4096, 1024
+    n, k = 4096, 1024
     with torch.cuda.stream(stream):
         a = torch.randn(m, k, device=device).to(torch.bfloat16)
         b = (torch.randn(n, k, device=device) / 32).to(torch.bfloat16)
@@ -595,6 +624,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
+    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "gemm"],
+                    help="run one secondary measurement alone on cuda:0 and print it (for profiling)")
+    ap.add_argument("--gemm-m", type=int, default=64 * 4096, help="rows of the GEMM probe (smaller only for profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -607,6 +639,11 @@ def main():
 
     import torch
     import torch.distributed as dist
+    if args.only:
+        device = torch.device("cuda", 0)
+        stream = torch.cuda.Stream(device)
+        print(json.dumps(secondary(torch, device, stream, peaks()[0], only=args.only, gemm_m=args.gemm_m)), flush=True)
+        return
     if world > 1:
         import datetime
         torch.cuda.set_device(local_rank)

@@ -13,6 +13,7 @@
 
 #include <cstdint>
 #include <string>
+#include <type_traits>
 
 #include "internal.h"
 #include "scan_common.cuh"
@@ -80,6 +81,63 @@ __global__ void __launch_bounds__(256) conv_silu_kernel(const T* __restrict__ x,
     }
 }
 
+// Same conv + SiLU with one thread per (token row, 8 consecutive channels):
+// the four taps of a row are independent 16-byte loads of rows t-3..t of the
+// same sequence (zero before its start), so no thread walks a sequence and
+// every load is in flight at once; identical arithmetic (and bits) to the
+// per-lane walk above.  Needs dim and ldx multiples of 8 and 16-byte aligned
+// tensors.
+template <typename T>
+__global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restrict__ x, unsigned long long ldx,
+                                                              const float* __restrict__ w, const float* __restrict__ bias,
+                                                              unsigned long long rows, unsigned long long len,
+                                                              unsigned long long dim, T* __restrict__ u) {
+    constexpr int K = 4;
+    const unsigned long long groups = dim / 8;
+    const unsigned long long gid = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
+    if (gid >= rows * groups) return;
+    const unsigned long long row = gid / groups, d0 = (gid % groups) * 8;
+    const unsigned long long t = row % len;
+    float hist[K][8];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const unsigned long long back = K - 1 - j; // tokens before t
+        if (back <= t) {
+            const uint4 v = *reinterpret_cast<const uint4*>(x + (row - back) * ldx + d0);
+            const std::uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if constexpr (std::is_same_v<T, __half>) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[c]));
+                    hist[j][2 * c] = f.x;
+                    hist[j][2 * c + 1] = f.y;
+                } else {
+                    hist[j][2 * c] = __uint_as_float(wv[c] << 16);
+                    hist[j][2 * c + 1] = __uint_as_float(wv[c] & 0xffff0000u);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) hist[j][c] = 0.0f;
+        }
+    }
+    std::uint32_t out[4];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + (d0 + c) * K);
+        const float wk[K] = {wv.x, wv.y, wv.z, wv.w};
+        float acc = bias ? bias[d0 + c] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < K; ++j) acc = fmaf(wk[j], hist[j][c], acc);
+        const T v = from_f32<T>(acc / (1.0f + expf(-acc)));
+        std::uint32_t bits;
+        if constexpr (std::is_same_v<T, __half>) bits = __half_as_ushort(v);
+        else bits = __bfloat16_as_ushort(v);
+        out[c / 2] = (c % 2 == 0) ? bits : (out[c / 2] | (bits << 16));
+    }
+    *reinterpret_cast<uint4*>(u + row * dim + d0) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 } // namespace
 
 cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
@@ -110,8 +168,21 @@ cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, un
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
                              unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
                              cudaStream_t stream) {
+    if (kwidth != 4) return cudaErrorInvalidConfiguration;
+    const auto al16 = [](const void* ptr) { return reinterpret_cast<std::uintptr_t>(ptr) % 16 == 0; };
+    const unsigned long long rows = batch * len, row_blocks = (rows * (dim / 8) + 255) / 256;
+    if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks <= 0x7fffffffull && len > 0) {
+        if (row_blocks == 0) return cudaSuccess;
+        if (dtype == SACC_DTYPE_BF16)
+            conv4_silu_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
+                static_cast<const __nv_bfloat16*>(x), ldx, w, bias, rows, len, dim, static_cast<__nv_bfloat16*>(u));
+        else
+            conv4_silu_rows_kernel<__half><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
+                static_cast<const __half*>(x), ldx, w, bias, rows, len, dim, static_cast<__half*>(u));
+        return cudaGetLastError();
+    }
     const unsigned long long blocks = (batch * dim + 255) / 256;
-    if (blocks > 0x7fffffffull || kwidth != 4) return cudaErrorInvalidConfiguration;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
     if (dtype == SACC_DTYPE_BF16)
         conv_silu_kernel<__nv_bfloat16, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
             static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u));
@@ -127,13 +198,15 @@ cudaError_t load_block_kernels(std::string& report) {
                         reinterpret_cast<const void*>(scale_columns_kernel<__nv_bfloat16>),
                         reinterpret_cast<const void*>(scale_columns_kernel<__half>),
                         reinterpret_cast<const void*>(conv_silu_kernel<__nv_bfloat16, 4>),
-                        reinterpret_cast<const void*>(conv_silu_kernel<__half, 4>)};
+                        reinterpret_cast<const void*>(conv_silu_kernel<__half, 4>),
+                        reinterpret_cast<const void*>(conv4_silu_rows_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(conv4_silu_rows_kernel<__half>)};
     for (const void* k : ks) {
         cudaFuncAttributes attr{};
         const cudaError_t e = cudaFuncGetAttributes(&attr, k);
         if (e != cudaSuccess) return e;
     }
-    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x6\n";
+    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x8\n";
     return cudaSuccess;
 }
 

@@ -338,7 +338,9 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p
     p.tiles_m = static_cast<int>((p.m + kBM - 1) / kBM);
     p.tiles_n = static_cast<int>((p.n + BN - 1) / BN);
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-    const unsigned grid = static_cast<unsigned>(tiles < sm_count ? tiles : sm_count); // one CTA per SM (TMEM: 2 x BN columns)
+    // One CTA per SM; two at BN = 64 (2 x 97 KB of shared memory, 2 x 128 TMEM columns).
+    const long long slots = static_cast<long long>(sm_count) * (BN == 64 ? 2 : 1);
+    const unsigned grid = static_cast<unsigned>(tiles < slots ? tiles : slots);
     void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), &p};
     return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), args,
                             gemm_smem<BN>(), stream);
@@ -349,7 +351,11 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p
 cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const unsigned bn = a.n <= 64 ? 64u : a.n <= 128 ? 128u : 256u;
+    // Widest tile that covers n, narrowed while the tile count leaves SMs idle
+    // (the block's projections at config 1 have only 64 row tiles).
+    unsigned bn = a.n <= 64 ? 64u : a.n <= 128 ? 128u : 256u;
+    const unsigned long long mt = (a.m + kBM - 1) / kBM;
+    while (bn > 64 && mt * ((a.n + bn - 1) / bn) < static_cast<unsigned long long>(sms)) bn /= 2;
     CUtensorMap ta{}, tb{};
     if (!kmajor_map(&ta, a.in_dtype, a.a, a.k, a.m, a.lda, kBM) || !kmajor_map(&tb, a.in_dtype, a.b, a.k, a.n, a.ldb, bn))
         return cudaErrorInvalidValue;

@@ -50,7 +50,8 @@ __global__ void __launch_bounds__(256) scale_columns_kernel(const T* __restrict_
 
 // u[b, t, d] = silu(bias[d] + sum_j w[d, j] x[b, t + j - (K - 1), d]), zero
 // outside the sequence (causal depthwise conv1d, reference
-// src/head_reference.cpp:190-216).  One thread per (sequence, channel)
+// src/head_reference.cpp:190-216); SiLU as x / (1 + 2^(-x log2 e)) with the
+// special-function exp and a fast divide.  One thread per (sequence, channel)
 // walks the tokens keeping the last K - 1 inputs in registers; consecutive
 // threads take consecutive channels, so every load and store is coalesced.
 template <typename T, int K>
@@ -77,65 +78,75 @@ __global__ void __launch_bounds__(256) conv_silu_kernel(const T* __restrict__ x,
         float acc = bv;
 #pragma unroll
         for (int j = 0; j < K; ++j) acc = fmaf(wk[j], hist[j], acc);
-        ur[t * dim] = from_f32<T>(acc / (1.0f + expf(-acc)));
+        ur[t * dim] = from_f32<T>(silu(acc));
     }
 }
 
-// Same conv + SiLU with one thread per (token row, 8 consecutive channels):
-// the four taps of a row are independent 16-byte loads of rows t-3..t of the
-// same sequence (zero before its start), so no thread walks a sequence and
-// every load is in flight at once; identical arithmetic (and bits) to the
-// per-lane walk above.  Needs dim and ldx multiples of 8 and 16-byte aligned
-// tensors.
+// Same conv + SiLU with one thread per (4 consecutive token rows of one
+// sequence, 8 consecutive channels): rows t-3 .. t+3 are seven independent
+// 16-byte loads (zero before the sequence start, none past its end), the
+// weights and bias of the 8 channels load once for the 4 rows, and nothing
+// walks a sequence; same arithmetic, in the same order, as the per-lane walk
+// above.  Needs dim and ldx multiples of 8 and 16-byte aligned tensors.
 template <typename T>
 __global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restrict__ x, unsigned long long ldx,
                                                               const float* __restrict__ w, const float* __restrict__ bias,
-                                                              unsigned long long rows, unsigned long long len,
+                                                              unsigned long long batch, unsigned long long len,
                                                               unsigned long long dim, T* __restrict__ u) {
-    constexpr int K = 4;
-    const unsigned long long groups = dim / 8;
+    constexpr int K = 4, R = 4; // taps, rows per thread
+    const unsigned long long groups = dim / 8, quads = (len + R - 1) / R;
     const unsigned long long gid = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
-    if (gid >= rows * groups) return;
-    const unsigned long long row = gid / groups, d0 = (gid % groups) * 8;
-    const unsigned long long t = row % len;
-    float hist[K][8];
+    if (gid >= batch * quads * groups) return;
+    const unsigned long long g = gid % groups, bq = gid / groups;
+    const unsigned long long b = bq / quads, t0 = (bq % quads) * R, d0 = g * 8;
+    float wk[8][K], bv[8];
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-        const unsigned long long back = K - 1 - j; // tokens before t
-        if (back <= t) {
-            const uint4 v = *reinterpret_cast<const uint4*>(x + (row - back) * ldx + d0);
+    for (int c = 0; c < 8; ++c) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (d0 + c) * K));
+        wk[c][0] = wv.x; wk[c][1] = wv.y; wk[c][2] = wv.z; wk[c][3] = wv.w;
+        bv[c] = bias ? __ldg(bias + d0 + c) : 0.0f;
+    }
+    // rows t0 - 3 .. t0 + 3 of sequence b (index i = row - t0 + 3)
+    float xr[K - 1 + R][8];
+#pragma unroll
+    for (int i = 0; i < K - 1 + R; ++i) {
+        const long long t = static_cast<long long>(t0) + i - (K - 1);
+        if (t >= 0 && t < static_cast<long long>(len)) {
+            const uint4 v = *reinterpret_cast<const uint4*>(x + (b * len + static_cast<unsigned long long>(t)) * ldx + d0);
             const std::uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 if constexpr (std::is_same_v<T, __half>) {
                     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[c]));
-                    hist[j][2 * c] = f.x;
-                    hist[j][2 * c + 1] = f.y;
+                    xr[i][2 * c] = f.x;
+                    xr[i][2 * c + 1] = f.y;
                 } else {
-                    hist[j][2 * c] = __uint_as_float(wv[c] << 16);
-                    hist[j][2 * c + 1] = __uint_as_float(wv[c] & 0xffff0000u);
+                    xr[i][2 * c] = __uint_as_float(wv[c] << 16);
+                    xr[i][2 * c + 1] = __uint_as_float(wv[c] & 0xffff0000u);
                 }
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) hist[j][c] = 0.0f;
+            for (int c = 0; c < 8; ++c) xr[i][c] = 0.0f;
         }
     }
-    std::uint32_t out[4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + (d0 + c) * K);
-        const float wk[K] = {wv.x, wv.y, wv.z, wv.w};
-        float acc = bias ? bias[d0 + c] : 0.0f;
+    for (int r = 0; r < R; ++r) {
+        if (t0 + r >= len) break;
+        std::uint32_t out[4];
 #pragma unroll
-        for (int j = 0; j < K; ++j) acc = fmaf(wk[j], hist[j][c], acc);
-        const T v = from_f32<T>(acc / (1.0f + expf(-acc)));
-        std::uint32_t bits;
-        if constexpr (std::is_same_v<T, __half>) bits = __half_as_ushort(v);
-        else bits = __bfloat16_as_ushort(v);
-        out[c / 2] = (c % 2 == 0) ? bits : (out[c / 2] | (bits << 16));
+        for (int c = 0; c < 8; ++c) {
+            float acc = bv[c];
+#pragma unroll
+            for (int j = 0; j < K; ++j) acc = fmaf(wk[c][j], xr[r + j][c], acc);
+            const T v = from_f32<T>(silu(acc));
+            std::uint32_t bits;
+            if constexpr (std::is_same_v<T, __half>) bits = __half_as_ushort(v);
+            else bits = __bfloat16_as_ushort(v);
+            out[c / 2] = (c % 2 == 0) ? bits : (out[c / 2] | (bits << 16));
+        }
+        *reinterpret_cast<uint4*>(u + (b * len + t0 + r) * dim + d0) = make_uint4(out[0], out[1], out[2], out[3]);
     }
-    *reinterpret_cast<uint4*>(u + row * dim + d0) = make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 } // namespace
@@ -170,15 +181,15 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
                              cudaStream_t stream) {
     if (kwidth != 4) return cudaErrorInvalidConfiguration;
     const auto al16 = [](const void* ptr) { return reinterpret_cast<std::uintptr_t>(ptr) % 16 == 0; };
-    const unsigned long long rows = batch * len, row_blocks = (rows * (dim / 8) + 255) / 256;
+    const unsigned long long row_blocks = (batch * ((len + 3) / 4) * (dim / 8) + 255) / 256;
     if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks <= 0x7fffffffull && len > 0) {
         if (row_blocks == 0) return cudaSuccess;
         if (dtype == SACC_DTYPE_BF16)
             conv4_silu_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
-                static_cast<const __nv_bfloat16*>(x), ldx, w, bias, rows, len, dim, static_cast<__nv_bfloat16*>(u));
+                static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u));
         else
             conv4_silu_rows_kernel<__half><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
-                static_cast<const __half*>(x), ldx, w, bias, rows, len, dim, static_cast<__half*>(u));
+                static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
         return cudaGetLastError();
     }
     const unsigned long long blocks = (batch * dim + 255) / 256;

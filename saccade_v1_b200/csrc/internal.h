@@ -54,7 +54,12 @@ cudaError_t launch_cross_merge(const CrossLaunch& p, const float* y, float* out,
 cudaError_t launch_scan_ex(const SaccScanExArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_scan_general(const SaccScanExArgs& a, cudaStream_t stream);
 cudaError_t load_scan_general_kernels(std::string& report);
-bool bulk_eligible(const SaccScanExArgs& a);
+// Row pitches (elements between consecutive tokens) of z, B and C in the
+// (B, L, .) layout when they are column slices of wider matrices; 0 = dense.
+struct RowStrides {
+    unsigned long long z, b, c;
+};
+bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs = nullptr);
 cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream);
 cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
@@ -76,7 +81,7 @@ cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);
 cudaError_t read_step_fault(unsigned* out, bool clear);
-cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream);
+cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs = nullptr);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
 cudaError_t read_bulk_fault(unsigned* out, bool clear);

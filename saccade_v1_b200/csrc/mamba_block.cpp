@@ -4,12 +4,12 @@
 // src/head_reference.cpp:471-495), plus BASELINE's RMSNorm prologue:
 //
 //   r      = 1 / sqrt(mean(x^2) + eps)                    rms_scale            (x once)
-//   x_in   = diag(r) x (W_in[:D]  diag(w))^T              tcgen05 GEMM, row scale epilogue
-//   z      = diag(r) x (W_in[D:]  diag(w))^T              tcgen05 GEMM
-//   u      = silu(causal_conv1d(x_in) + conv_b)           conv_silu
-//   dt,B,C = u W_x[rows]^T                                three tcgen05 GEMMs (row slices of W_x)
-//   delta  = dt W_dt^T                                    tcgen05 GEMM (K = dt_rank)
-//   y      = scan(u, delta + dt_bias, A, B, C, D) * silu(z)   bulk scan, (B, L, D) layout
+//   xz     = diag(r) x (W_in diag(w))^T                   one tcgen05 GEMM, row scale epilogue
+//   u      = silu(causal_conv1d(x_in) + conv_b)           conv_silu on the x_in half of xz
+//   dbc    = u W_x^T = [dt | B | C]                       one tcgen05 GEMM (N = dt_rank + 2 d_state)
+//   delta  = dt W_dt^T                                    tcgen05 GEMM on the dt columns of dbc
+//   y      = scan(u, delta + dt_bias, A, B, C, D) * silu(z)   bulk scan, (B, L, D), z / B / C read
+//                                                          in place from xz and dbc (row pitches)
 //   out    = y W_out^T + x                                tcgen05 GEMM, residual epilogue
 //
 // Intermediates live in a caller-provided workspace (sacc_mamba_block_workspace
@@ -27,7 +27,7 @@ namespace sacc {
 namespace {
 
 struct Layout {
-    std::size_t r, wn, xin, z, u, dt, bm, cm, delta, y, total;
+    std::size_t r, wn, xz, u, dbc, delta, y, total;
 };
 
 std::size_t align256(std::size_t v) { return (v + 255) & ~std::size_t(255); }
@@ -44,12 +44,9 @@ Layout plan(const SaccMambaBlockArgs& a) {
     };
     l.r = take(M * sizeof(float));
     l.wn = take(2 * D * dm * e);
-    l.xin = take(M * D * e);
-    l.z = take(M * D * e);
+    l.xz = take(M * 2 * D * e);
     l.u = take(M * D * e);
-    l.dt = take(M * R * e);
-    l.bm = take(M * N * e);
-    l.cm = take(M * N * e);
+    l.dbc = take(M * (R + 2 * N) * e);
     l.delta = take(M * D * e);
     l.y = take(M * D * e);
     l.total = off;
@@ -74,9 +71,9 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
     auto* ws = static_cast<unsigned char*>(workspace);
     float* r = reinterpret_cast<float*>(ws + l.r);
     void* wn = ws + l.wn;
-    void *xin = ws + l.xin, *z = ws + l.z, *u = ws + l.u, *dt = ws + l.dt, *bm = ws + l.bm, *cm = ws + l.cm,
-         *delta = ws + l.delta, *y = ws + l.y;
+    void *xz = ws + l.xz, *u = ws + l.u, *dbc = ws + l.dbc, *delta = ws + l.delta, *y = ws + l.y;
     const std::uint64_t M = a.batch * a.length, D = a.d_inner, N = a.d_state, R = a.dt_rank, dm = a.d_model;
+    const std::uint64_t W = R + 2 * N; // dbc row: dt | B | C
     const int dt_ = a.dtype;
     const std::size_t e = 2;
     auto at = [&](const void* p, std::size_t elems) { return static_cast<const unsigned char*>(p) + elems * e; };
@@ -91,42 +88,41 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
             return err;
         w_in = wn;
     }
-    SaccGemmArgs g = gemm_args(dt_, M, D, dm, a.x, dm, w_in, dm, xin, D);
-    g.row_scale = norm ? r : nullptr;
-    if ((err = launch_gemm(g, stream)) != cudaSuccess) return err;
-    g = gemm_args(dt_, M, D, dm, a.x, dm, at(w_in, D * dm), dm, z, D);
+    // in_proj: x_in and z side by side in one (M, 2D) output.
+    SaccGemmArgs g = gemm_args(dt_, M, 2 * D, dm, a.x, dm, w_in, dm, xz, 2 * D);
     g.row_scale = norm ? r : nullptr;
     if ((err = launch_gemm(g, stream)) != cudaSuccess) return err;
 
-    // Causal depthwise conv1d (width d_conv) + SiLU.
-    if ((err = launch_conv_silu(dt_, static_cast<int>(a.d_conv), xin, D, a.conv_w, a.conv_b, a.batch, a.length, D, u,
+    // Causal depthwise conv1d (width d_conv) + SiLU on the x_in half.
+    if ((err = launch_conv_silu(dt_, static_cast<int>(a.d_conv), xz, 2 * D, a.conv_w, a.conv_b, a.batch, a.length, D, u,
                                 stream)) != cudaSuccess)
         return err;
 
-    // x_proj as three GEMMs over row slices of W_x: dt (R), B (N), C (N).
-    if ((err = launch_gemm(gemm_args(dt_, M, R, D, u, D, a.w_x, D, dt, R), stream)) != cudaSuccess) return err;
-    if ((err = launch_gemm(gemm_args(dt_, M, N, D, u, D, at(a.w_x, R * D), D, bm, N), stream)) != cudaSuccess) return err;
-    if ((err = launch_gemm(gemm_args(dt_, M, N, D, u, D, at(a.w_x, (R + N) * D), D, cm, N), stream)) != cudaSuccess)
-        return err;
-    // dt_proj (bias added inside the scan, before softplus).
-    if ((err = launch_gemm(gemm_args(dt_, M, D, R, dt, R, a.w_dt, R, delta, D), stream)) != cudaSuccess) return err;
+    // x_proj in one GEMM: dt (R), B (N), C (N) as column slices of dbc.
+    if ((err = launch_gemm(gemm_args(dt_, M, W, D, u, D, a.w_x, D, dbc, W), stream)) != cudaSuccess) return err;
+    // dt_proj on the dt columns (bias added inside the scan, before softplus).
+    if ((err = launch_gemm(gemm_args(dt_, M, D, R, dbc, W, a.w_dt, R, delta, D), stream)) != cudaSuccess) return err;
 
-    // Selective scan with D skip and SiLU(z) gate, (B, L, D) layout, chunked by
-    // batch so that each call stays within the int32 element capacity.
+    // Selective scan with D skip and SiLU(z) gate, (B, L, D) layout, z / B / C
+    // read in place through their row pitches; chunked by batch so that each
+    // call stays within the int32 element capacity.
+    const RowStrides pitch{2 * D, W, W};
     const std::uint64_t per_seq = a.length * D;
     std::uint64_t chunk = a.batch;
-    while (chunk > 1 && chunk * per_seq > kMaxElements) chunk = (chunk + 1) / 2;
+    while (chunk > 1 && chunk * per_seq * 2 > kMaxElements) chunk = (chunk + 1) / 2;
     for (std::uint64_t b0 = 0; b0 < a.batch; b0 += chunk) {
         const std::uint64_t nb = (a.batch - b0 < chunk) ? a.batch - b0 : chunk;
         const std::size_t tok = b0 * a.length;
         SaccScanExArgs s{};
         s.batch = nb; s.length = a.length; s.channels = D; s.state = N; s.groups = 1; s.a_rows = D; s.c_width = N;
         s.layout = SACC_LAYOUT_BLD; s.dtype = dt_; s.delta_softplus = 1; s.nseq = 0;
-        s.u = at(u, tok * D); s.delta = at(delta, tok * D); s.b = at(bm, tok * N); s.c = at(cm, tok * N);
-        s.z = at(z, tok * D);
+        s.u = at(u, tok * D); s.delta = at(delta, tok * D);
+        s.z = at(xz, tok * 2 * D + D);
+        s.b = at(dbc, tok * W + R); s.c = at(dbc, tok * W + R + N);
         s.a = a.a; s.d = a.d; s.delta_bias = a.dt_bias;
         s.y = static_cast<unsigned char*>(y) + tok * D * e;
-        if ((err = launch_scan_ex(s, 0, stream)) != cudaSuccess) return err;
+        if (!bulk_eligible(s, &pitch)) return cudaErrorInvalidValue; // shapes are checked by the caller
+        if ((err = launch_scan_bulk(s, stream, &pitch)) != cudaSuccess) return err;
     }
 
     // out_proj + residual.

@@ -384,13 +384,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 3D map (inner, mid, outer) with a (box_inner, box_mid, 1) box, no swizzle.
+// 3D map (inner, mid, outer) with a (box_inner, box_mid, 1) box, no swizzle;
+// consecutive mid rows `row_stride` elements apart (0: dense, = inner).
 bool make_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, unsigned long long inner,
-                 unsigned long long mid, unsigned long long outer, unsigned box_inner, unsigned box_mid) {
+                 unsigned long long mid, unsigned long long outer, unsigned box_inner, unsigned box_mid,
+                 unsigned long long row_stride = 0) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const unsigned long long rs = row_stride ? row_stride : inner;
     const cuuint64_t dims[3] = {inner, mid, outer};
-    const cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
+    const cuuint64_t strides[2] = {rs * 2, rs * mid * 2};
     const cuuint32_t box[3] = {box_inner, box_mid, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -452,7 +455,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15
 // in 128-wide tiles inside one group, 16-byte aligned tensors and 16-byte row
 // strides for the TMA ((B, D, L): L % 8 == 0; (B, L, D): a full-width C, whose
 // rows are then 16 * groups * 2 bytes).  Other calls use the general kernel.
-bool bulk_eligible(const SaccScanExArgs& a) {
+bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
+    if (rs) {
+        // Strided z / B / C rows (the block's fused projection outputs): dense
+        // (B, L, D) rows only, 16-byte row pitches, rows at least as wide as the data.
+        const unsigned long long cw = a.c_width;
+        if (a.layout != SACC_LAYOUT_BLD || a.cu_seqlens != nullptr || (rs->z && (rs->z < a.channels || rs->z % 8)) ||
+            (rs->b && (rs->b < a.groups * kN || rs->b % 8)) || (rs->c && (rs->c < a.groups * cw || rs->c % 8)))
+            return false;
+    }
     if ((a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16) || a.state != kN || a.length == 0 || a.groups == 0 ||
         a.channels % kLanes != 0 || (a.channels / a.groups) % kLanes != 0)
         return false;
@@ -474,7 +485,9 @@ bool bulk_eligible(const SaccScanExArgs& a) {
     return rows <= 0x7fffffffull && tokens <= 0x7fffffffull && a.batch * a.groups * kN <= 0x7fffffffull;
 }
 
-cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream) {
+cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs) {
+    const RowStrides dense{0, 0, 0};
+    if (!rs) rs = &dense;
     const bool bdl = a.layout == SACC_LAYOUT_BDL;
     const unsigned long long cw = a.c_width, B = a.batch, D = a.channels, L = a.length, G = a.groups;
     const CUtensorMapDataType dt = a.dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -490,9 +503,9 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream) {
              make_map_2d(&tc, dt, a.c, L, B * G * cw, L * 2, kT, static_cast<unsigned>(cw), CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
         ok = make_map_3d(&tu, dt, a.u, D, L, B, kLanes, kT) && make_map_3d(&td, dt, a.delta, D, L, B, kLanes, kT) &&
-             make_map_3d(&tz, dt, a.z ? a.z : a.u, D, L, B, kLanes, kT) && make_map_3d(&ty, dt, a.y, D, L, B, kLanes, kT) &&
-             make_map_3d(&tb, dt, a.b, G * kN, L, B, kN, kT) &&
-             make_map_3d(&tc, dt, a.c, G * cw, L, B, static_cast<unsigned>(cw), kT);
+             make_map_3d(&tz, dt, a.z ? a.z : a.u, D, L, B, kLanes, kT, a.z ? rs->z : 0) &&
+             make_map_3d(&ty, dt, a.y, D, L, B, kLanes, kT) && make_map_3d(&tb, dt, a.b, G * kN, L, B, kN, kT, rs->b) &&
+             make_map_3d(&tc, dt, a.c, G * cw, L, B, static_cast<unsigned>(cw), kT, rs->c);
     }
     if (!ok) return cudaErrorInvalidValue; // tensor-map encoding refused the (checked) layout
     BulkParams p{};

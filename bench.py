@@ -328,6 +328,11 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
 
+    # Config 4 (4-layer stack, batch-sharded): every rank takes part.
+    c4 = None
+    if not args.no_secondary and not args.no_c4:
+        c4 = c4_stack(torch, device, stream, rank, world, barrier, max_over_ranks)
+
     if rank != 0:
         return None
     nbytes = algorithmic_bytes(batch=args.batch)
@@ -337,6 +342,8 @@ def run_ours(args, rank, world, local_rank):
     achieved = nbytes / (kernel_ms / 1e3) / 1e9
     cpu = cpu_baseline(args) if world == 1 and not args.no_cpu_baseline else None
     extra = secondary(torch, device, stream, peaks()[0]) if not args.no_secondary else None
+    if extra is not None and c4 is not None:
+        extra["c4_stack"] = c4
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
@@ -461,9 +468,12 @@ def hr_deploy(torch, device, stream, peak):
 def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
     """Other rows of the hot path, device-timed on this GPU (not part of `value`); `only` runs one of them."""
     runs = {"c3_step": c3_step, "c3_rescan": c3_rescan, "hr_deploy_f32_us": hr_deploy,
-            "c1_block": lambda *a: c1_block(*a[:3]), "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m)}
+            "c1_block": lambda *a: c1_block(*a[:3]), "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m),
+            "c4_stack": lambda *a: c4_stack(*a[:3])}
     out = {}
     for name, fn in runs.items():
+        if name == "c4_stack" and only != name:
+            continue  # run on every rank by run_ours
         if only is None or name == only:
             out[name] = fn(torch, device, stream, peak)
             stream.synchronize()
@@ -472,6 +482,76 @@ def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
         out["c3_frame_avg_us"] = round(us + us_r / 30.0, 2)
         out["c3_tracks_frames_per_s"] = round(4096 / ((us + us_r / 30.0) * 1e-6), 1)
     return out
+
+
+def c4_stack(torch, device, stream, rank=0, world=1, barrier=lambda: None, max_over_ranks=lambda v: v, forwards=2):
+    """a 4-layer Mamba stack (d_model 1024, D 2048, N 16, d_conv 4, dt_rank 64, bf16, fp32
+    state) over B = 512 tracks x L = 4096 frames, split by batch over the ranks (no collective inside the stack),
+    then an NCCL all-gather of the last layer's output.  Device-timed, max over ranks; every rank takes the
+    same steps."""
+    import saccade_v1_b200 as sb
+    from saccade_v1_b200.shard import gather_batch, shard_rows
+    B4, L4, dm, D4, N4, R4, layers = 512, 4096, 1024, 2048, 16, 64, 4
+    shard = shard_rows(B4, world, rank)
+    bf = torch.bfloat16
+    g = torch.Generator(device=device)
+    g.manual_seed(4000 + rank)
+    with torch.cuda.stream(stream):
+        params = []
+        for li in range(layers):
+            p = synthetic_block(400 + li, dm, D4, N4, R4)
+            params.append({k: (torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device=device, dtype=bf)
+                               if k in ("w_in", "w_x", "w_dt", "w_out") else
+                               torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device)) for k, v in p.items()})
+        x = torch.randn(shard.size, L4, dm, device=device, generator=g, dtype=bf) * 0.1
+        bufs = [torch.empty_like(x), torch.empty_like(x)]
+        ws = torch.empty(sb.mamba_block_workspace(x, params[0]) + 256, dtype=torch.uint8, device=device)
+
+        def forward():
+            h = x
+            for li in range(layers):
+                out = bufs[li % 2]
+                sb.mamba_block_forward(h, params[li], out=out, workspace=ws, stream=stream)
+                h = out
+            return h
+
+        forward()
+    stream.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(forwards):
+        with torch.cuda.stream(stream):
+            h = forward()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / forwards
+    gms = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            gather_batch(h, shard, B4)
+        torch.cuda.synchronize(device)
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            g0.record(stream)
+            full = gather_batch(h, shard, B4)
+            g1.record(stream)
+        g1.synchronize()
+        barrier()
+        gms = max_over_ranks(g0.elapsed_time(g1))
+        del full
+    tokens = B4 * L4
+    flop = layers * 2 * tokens * (dm * 2 * D4 + D4 * (R4 + 2 * N4) + R4 * D4 + D4 * dm)
+    res = {"ms_per_forward": round(ms, 3), "tracks_frames_per_s": round(tokens / (ms / 1e3), 1),
+           "gemm_tflops": round(flop / (ms / 1e3) / 1e12, 1), "ranks": world, "tracks_per_rank": shard.size,
+           "allgather_ms": None if gms is None else round(gms, 3),
+           "tracks_frames_per_s_with_allgather": round(tokens / ((ms + (gms or 0.0)) / 1e3), 1),
+           "workload": "4 layers, d_model 1024, D 2048, N 16, dt_rank 64, bf16, B=512 x L=4096, batch-sharded"}
+    del x, bufs, ws, params
+    torch.cuda.empty_cache()
+    return res
 
 
 def synthetic_block(seed, d_model, d_inner, d_state, dt_rank, d_conv=4):
@@ -624,7 +704,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
-    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "gemm"],
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-4 stack (52 GB on one GPU)")
+    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "gemm", "c4_stack"],
                     help="run one secondary measurement alone on cuda:0 and print it (for profiling)")
     ap.add_argument("--gemm-m", type=int, default=64 * 4096, help="rows of the GEMM probe (smaller only for profiling)")
     args = ap.parse_args()

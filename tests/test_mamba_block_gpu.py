@@ -86,3 +86,15 @@ def test_block_rejections():
     bad = dict(p, conv_w=torch.zeros(256, 3, device="cuda"))
     with pytest.raises(sb.ScanInvalidArgument, match="d_conv must be 4"):
         sb.mamba_block_forward(x, bad, stream=torch.cuda.Stream())
+
+
+def test_config4_layer_sampled_tracks():
+    """BASELINE config 4 layer shape (L 4096, d_model 1024, D 2048, N 16, dt_rank 64, bf16) on 8 tracks; two
+    tracks against the oracle."""
+    B, L, dm, D, N, R = 8, 4096, 1024, 2048, 16, 64
+    p = mo.random_block(13, dm, D, N, R, 4, "bf16")
+    x = mo.rnd(np.random.default_rng(6).standard_normal((B, L, dm)) * 0.1, "bf16")
+    got = run_block(x, p, "bf16")
+    pick = [1, 6]
+    check("config4_tracks", got[pick], mo.block_forward(x[pick], p, "bf16"))
+    assert sb.scan_fault() == 0

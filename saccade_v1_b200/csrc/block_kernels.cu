@@ -94,11 +94,12 @@ __global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restric
                                                               unsigned long long batch, unsigned long long len,
                                                               unsigned long long dim, T* __restrict__ u) {
     constexpr int K = 4, R = 4; // taps, rows per thread
-    const unsigned long long groups = dim / 8, quads = (len + R - 1) / R;
-    const unsigned long long gid = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
-    if (gid >= batch * quads * groups) return;
-    const unsigned long long g = gid % groups, bq = gid / groups;
-    const unsigned long long b = bq / quads, t0 = (bq % quads) * R, d0 = g * 8;
+    // 32-bit index arithmetic (the launcher keeps the thread count below 2^32).
+    const unsigned groups = static_cast<unsigned>(dim / 8), quads = static_cast<unsigned>((len + R - 1) / R);
+    const unsigned gid = blockIdx.x * 256u + threadIdx.x;
+    if (static_cast<unsigned long long>(gid) >= batch * quads * groups) return;
+    const unsigned g = gid % groups, bq = gid / groups;
+    const unsigned long long b = bq / quads, t0 = static_cast<unsigned long long>(bq % quads) * R, d0 = g * 8ull;
     float wk[8][K], bv[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -181,8 +182,8 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
                              cudaStream_t stream) {
     if (kwidth != 4) return cudaErrorInvalidConfiguration;
     const auto al16 = [](const void* ptr) { return reinterpret_cast<std::uintptr_t>(ptr) % 16 == 0; };
-    const unsigned long long row_blocks = (batch * ((len + 3) / 4) * (dim / 8) + 255) / 256;
-    if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks <= 0x7fffffffull && len > 0) {
+    const unsigned long long threads = batch * ((len + 3) / 4) * (dim / 8), row_blocks = (threads + 255) / 256;
+    if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks * 256 < 0xffffffffull && len > 0) {
         if (row_blocks == 0) return cudaSuccess;
         if (dtype == SACC_DTYPE_BF16)
             conv4_silu_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(

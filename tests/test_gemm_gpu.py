@@ -25,7 +25,7 @@ def check(c, ref, mag, out_dtype):
 
 
 @pytest.mark.parametrize("shape", [(256, 512, 128), (200, 40, 256), (300, 1000, 520), (8192, 512, 128), (128, 64, 64),
-                                   (1000, 256, 2048), (16384, 2048, 320), (5000, 700, 72)])
+                                   (1000, 256, 2048), (16384, 2048, 320), (5000, 700, 72), (20000, 1000, 512)])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_gemm_matches_fp32_reference(shape, dt):
     m, n, k = shape
@@ -56,6 +56,25 @@ def test_gemm_bias_residual_and_16bit_out():
     s.synchronize()
     ref = a.float() @ b.float().T + bias + r.float()
     check(c, ref, a.float().abs() @ b.float().abs().T + bias.abs() + r.float().abs(), torch.bfloat16)
+
+
+def test_gemm_large_epilogue():
+    """Large m, n, k (persistent tiles, many per CTA): row scale, bias, residual, 16-bit output, ragged m."""
+    m, n, k = 16390, 2048, 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(12)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+        b = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+        bias = torch.randn(n, device="cuda", generator=g)
+        r = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+        rs = torch.rand(m, device="cuda", generator=g) + 0.5
+        c = sb.gemm(a, b, bias=bias, residual=r, row_scale=rs, stream=s)
+    s.synchronize()
+    ref = (a.float() @ b.float().T) * rs[:, None] + bias + r.float()
+    check(c, ref, (a.float().abs() @ b.float().abs().T) * rs[:, None] + bias.abs() + r.float().abs(), torch.bfloat16)
+    assert sb.scan_fault() == 0
 
 
 def test_gemm_strided_rows():

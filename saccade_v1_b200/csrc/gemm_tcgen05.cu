@@ -15,8 +15,10 @@
 //               tcgen05.commit to free the stage and, per tile, to signal
 //               the epilogue;
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, row
-//               scale, bias, residual, conversion, 16-byte stores, then
-//               release the accumulator buffer.
+//               scale, bias, residual, conversion; 16-bit results go through a
+//               double-buffered, swizzled 32 x 32 shared tile per warp and a
+//               TMA store (coalesced full lines), FP32 results straight to
+//               global memory; then release the accumulator buffer.
 // No multicast, no clusters.  Every mbarrier wait has an iteration limit and
 // sets the library fault word when it runs out.
 #include <cuda.h>
@@ -42,14 +44,22 @@ namespace {
 constexpr int kBM = 128, kBK = 64, kStages = 4;
 constexpr int kThreads = 192;
 
+// Ring depth: 4 stages, 3 at BN = 64 so that two CTAs fit on an SM.
+template <int BN>
+__host__ __device__ constexpr int stages_for() {
+    return BN == 64 ? 3 : kStages;
+}
+
 template <int BN>
 struct GemmSmem {
-    alignas(1024) std::uint16_t a[kStages][kBM * kBK];
-    alignas(1024) std::uint16_t b[kStages][BN * kBK];
-    alignas(8) std::uint64_t full[kStages];
-    alignas(8) std::uint64_t empty[kStages];
+    alignas(1024) std::uint16_t a[stages_for<BN>()][kBM * kBK];
+    alignas(1024) std::uint16_t b[stages_for<BN>()][BN * kBK];
+    alignas(8) std::uint64_t full[stages_for<BN>()];
+    alignas(8) std::uint64_t empty[stages_for<BN>()];
     alignas(8) std::uint64_t acc_full[2];
     alignas(8) std::uint64_t acc_empty[2];
+    // 16-bit epilogue staging: per epilogue warp two 32 x 32 tiles (64-byte swizzle) for TMA stores.
+    alignas(1024) std::uint16_t stage[4][2][32 * 32];
     std::uint32_t tmem_base;
 };
 
@@ -59,7 +69,7 @@ struct GemmParams {
     const float* bias;
     const float* row_scale;
     unsigned long long m, n, k, ldc, ldr;
-    int out_dtype, in_dtype, kblocks, tiles_m, tiles_n, vec_store;
+    int out_dtype, in_dtype, kblocks, tiles_m, tiles_n, vec_store, tma_store, res_vec;
 };
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with the
@@ -100,9 +110,17 @@ __device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 TMEM lanes (one per thread of the warp) x 32 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld32(std::uint32_t taddr, float (&v)[32]) {
-    std::uint32_t r[32];
+// 32 TMEM lanes (one per thread of the warp) x 32 consecutive 32-bit columns:
+// tmem_ld32_issue starts the load, tmem_ld32_wait waits for every load of the
+// thread and takes the destination registers as read-write operands, so that
+// no use of them can be scheduled before the wait.
+#define SACC_R32(r)                                                                                                  \
+    "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),     \
+        "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),      \
+        "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),     \
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+
+__device__ __forceinline__ void tmem_ld32_issue(std::uint32_t taddr, std::uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -112,9 +130,10 @@ __device__ __forceinline__ void tmem_ld32(std::uint32_t taddr, float (&v)[32]) {
           "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32_wait(std::uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : SACC_R32(r)::"memory");
 }
 
 __device__ __forceinline__ float load_elem(const void* p, unsigned long long i, int dtype) {
@@ -129,31 +148,89 @@ __device__ __forceinline__ void store_elem(void* p, unsigned long long i, int dt
     else static_cast<float*>(p)[i] = v;
 }
 
-__device__ __forceinline__ std::uint32_t pack_out(float lo, float hi, int dtype) {
-    if (dtype == SACC_DTYPE_BF16) {
-        const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-        return *reinterpret_cast<const std::uint32_t*>(&v);
-    }
-    const __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const std::uint32_t*>(&v);
-}
-
-// Epilogue of 32 consecutive columns of one row: row scale, bias, residual,
-// conversion; 16-byte stores when the row segment is aligned and complete.
-__device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long long row, unsigned long long col0, float (&v)[32]) {
-    const float rs = p.row_scale ? p.row_scale[row] : 1.0f;
+// Row scale, bias and residual on 32 consecutive columns of one row (the
+// residual as 16-byte loads when its rows allow).  Every test is uniform
+// across the warp and sits outside the element loops, which stay branch-free.
+__device__ __forceinline__ void apply_chunk(const GemmParams& p, unsigned long long row, unsigned long long col0, float (&v)[32]) {
     const bool full = col0 + 32 <= p.n;
+    if (p.row_scale) {
+        const float rs = p.row_scale[row];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        float x = v[i] * rs;
-        if (p.bias && (full || col0 + i < p.n)) x += p.bias[col0 + i];
-        v[i] = x;
+        for (int i = 0; i < 32; ++i) v[i] *= rs;
+    }
+    if (p.bias) {
+        if (full) {
+            const float4* bq = reinterpret_cast<const float4*>(p.bias + col0);
+            if ((reinterpret_cast<std::uintptr_t>(bq) & 15u) == 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 t = bq[q];
+                    v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += p.bias[col0 + i];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.n) v[i] += p.bias[col0 + i];
+        }
     }
     if (p.residual) {
+        if (full && p.res_vec) {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const std::uint16_t*>(p.residual) + row * p.ldr + col0);
+            const bool bf = p.out_dtype == SACC_DTYPE_BF16;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (full || col0 + i < p.n) v[i] += load_elem(p.residual, row * p.ldr + col0 + i, p.out_dtype);
+            for (int q = 0; q < 4; ++q) {
+                const uint4 w = src[q];
+                const std::uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float lo, hi;
+                    if (bf) {
+                        lo = __uint_as_float(ws[j] << 16);
+                        hi = __uint_as_float(ws[j] & 0xffff0000u);
+                    } else {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[j]));
+                        lo = f.x;
+                        hi = f.y;
+                    }
+                    v[8 * q + 2 * j] += lo;
+                    v[8 * q + 2 * j + 1] += hi;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full || col0 + i < p.n) v[i] += load_elem(p.residual, row * p.ldr + col0 + i, p.out_dtype);
+        }
     }
+}
+
+// 32 results to 16-bit pairs, the output type chosen once.
+__device__ __forceinline__ void pack16(const float (&v)[32], int dtype, std::uint32_t (&w)[16]) {
+    if (dtype == SACC_DTYPE_BF16) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<const std::uint32_t*>(&t);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const __half2 t = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<const std::uint32_t*>(&t);
+        }
+    }
+}
+
+// Epilogue of 32 consecutive columns of one row straight to global memory
+// (FP32 output, or a C the TMA cannot address): 16-byte stores when the row
+// segment is aligned and complete.
+__device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long long row, unsigned long long col0, float (&v)[32]) {
+    apply_chunk(p, row, col0, v);
+    const bool full = col0 + 32 <= p.n;
     if (full && p.vec_store) {
         if (p.out_dtype == SACC_DTYPE_F32) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.c) + row * p.ldc + col0);
@@ -161,11 +238,10 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long l
             for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         } else {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<std::uint16_t*>(p.c) + row * p.ldc + col0);
+            std::uint32_t w[16];
+            pack16(v, p.out_dtype, w);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                dst[q] = make_uint4(pack_out(v[8 * q], v[8 * q + 1], p.out_dtype), pack_out(v[8 * q + 2], v[8 * q + 3], p.out_dtype),
-                                    pack_out(v[8 * q + 4], v[8 * q + 5], p.out_dtype),
-                                    pack_out(v[8 * q + 6], v[8 * q + 7], p.out_dtype));
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
         return;
     }
@@ -178,7 +254,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long l
 // two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
-                                                           const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+                                                           const __grid_constant__ CUtensorMap tm_b,
+                                                           const __grid_constant__ CUtensorMap tm_c, GemmParams p) {
+    constexpr int S = stages_for<BN>();
     extern __shared__ unsigned char smem_raw[];
     auto& sm = *reinterpret_cast<GemmSmem<BN>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -187,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         prefetch_tensor_map(&tm_a);
         prefetch_tensor_map(&tm_b);
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
@@ -216,8 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             for (int tile = blockIdx.x; tile < tiles && !fault; tile += gridDim.x) {
                 const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
                 for (int kb = 0; kb < p.kblocks; ++kb, ++g) {
-                    const unsigned s = g % kStages;
-                    if (g >= kStages && !mbar_wait_bounded(&sm.empty[s], ((g / kStages) - 1) & 1u)) {
+                    const unsigned s = g % S;
+                    if (g >= S && !mbar_wait_bounded(&sm.empty[s], ((g / S) - 1) & 1u)) {
                         fault = true;
                         break;
                     }
@@ -240,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 tmem_fence_after();
                 const std::uint32_t acc = tmem + ab * BN;
                 for (int kb = 0; kb < p.kblocks; ++kb, ++g) {
-                    const unsigned s = g % kStages;
-                    if (!mbar_wait_bounded(&sm.full[s], (g / kStages) & 1u)) {
+                    const unsigned s = g % S;
+                    if (!mbar_wait_bounded(&sm.full[s], (g / S) & 1u)) {
                         fault = true;
                         break;
                     }
@@ -259,7 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     } else {
         // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
         const int quarter = warp % 4;
-        unsigned it = 0;
+        unsigned it = 0, st = 0; // st: staging tiles used by this warp
+        if (p.tma_store && lane == 0) prefetch_tensor_map(&tm_c);
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
             const unsigned ab = it & 1u;
             if (!mbar_wait_bounded(&sm.acc_full[ab], (it / 2) & 1u)) {
@@ -268,13 +347,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
             tmem_fence_after();
             const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
-            const unsigned long long row = static_cast<unsigned long long>(m0 + quarter * 32 + lane);
+            const int r0 = m0 + quarter * 32; // first row of this warp
+            const unsigned long long row = static_cast<unsigned long long>(r0 + lane);
+            const std::uint32_t tbase = tmem + ab * BN + (static_cast<std::uint32_t>(quarter * 32) << 16);
+            // Chunk c + 1 loads from TMEM while chunk c is finished and stored.
+            std::uint32_t ra[32], rb[32];
+            tmem_ld32_issue(tbase, ra);
+#pragma unroll
             for (int c = 0; c < BN / 32; ++c) {
                 float v[32];
-                tmem_ld32(tmem + ab * BN + (static_cast<std::uint32_t>(quarter * 32) << 16) + static_cast<std::uint32_t>(c * 32),
-                          v);
+                if (c % 2 == 0) {
+                    tmem_ld32_wait(ra);
+                    if (c + 1 < BN / 32) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), rb);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
+                } else {
+                    tmem_ld32_wait(rb);
+                    if (c + 1 < BN / 32) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), ra);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rb[i]);
+                }
                 const unsigned long long col0 = static_cast<unsigned long long>(n0 + c * 32);
-                if (row < p.m && col0 < p.n) store_chunk(p, row, col0, v);
+                if (!p.tma_store) {
+                    if (row < p.m && col0 < p.n) store_chunk(p, row, col0, v);
+                    continue;
+                }
+                if (static_cast<unsigned long long>(r0) >= p.m || col0 >= p.n) continue; // warp-uniform
+                // Coalesced path: the warp's 32 x 32 block goes through a swizzled
+                // shared tile and one TMA store (rows / columns past C are clipped).
+                if (row < p.m) apply_chunk(p, row, col0, v);
+                std::uint16_t* buf = sm.stage[quarter][st & 1u];
+                if (lane == 0) bulk_wait_read<1>(); // the store that last used this buffer has read it
+                __syncwarp();
+                std::uint32_t w[16];
+                pack16(v, p.out_dtype, w);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(buf + lane * 32 + ((q ^ ((lane >> 1) & 3)) << 3)) =
+                        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tm_c, buf, static_cast<int>(col0), r0);
+                    bulk_commit();
+                }
+                ++st;
             }
             tmem_fence_before();
             __syncwarp();
@@ -282,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     }
     if (fault) atomicOr(&g_gemm_fault, 1u);
+    if (warp >= 2 && lane == 0 && p.tma_store) bulk_wait<0>(); // staged stores have left shared memory
     tmem_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -331,8 +449,23 @@ cudaError_t prepare_gemm() {
     return st;
 }
 
+// C as a 2D map {n, m} with a 32 x 32 box and the 64-byte swizzle (16-bit
+// output) for the epilogue's TMA stores.
+bool c_map(CUtensorMap* map, int dtype, void* base, unsigned long long n, unsigned long long m, unsigned long long ld) {
+    auto fn = encode();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {n, m};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN>
-cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, int sm_count, cudaStream_t stream) {
+cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p, int sm_count,
+                      cudaStream_t stream) {
     const cudaError_t e = prepare_gemm<BN>();
     if (e != cudaSuccess) return e;
     p.tiles_m = static_cast<int>((p.m + kBM - 1) / kBM);
@@ -341,7 +474,7 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p
     // One CTA per SM; two at BN = 64 (2 x 97 KB of shared memory, 2 x 128 TMEM columns).
     const long long slots = static_cast<long long>(sm_count) * (BN == 64 ? 2 : 1);
     const unsigned grid = static_cast<unsigned>(tiles < slots ? tiles : slots);
-    void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), &p};
+    void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), const_cast<CUtensorMap*>(&tc), &p};
     return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), args,
                             gemm_smem<BN>(), stream);
 }
@@ -366,9 +499,13 @@ cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     p.kblocks = static_cast<int>((a.k + kBK - 1) / kBK);
     const std::size_t eo = a.out_dtype == SACC_DTYPE_F32 ? 4 : 2;
     p.vec_store = (reinterpret_cast<std::uintptr_t>(a.c) % 16 == 0) && ((a.ldc * eo) % 16 == 0);
-    if (bn == 64) return launch_bn<64>(ta, tb, p, sms, stream);
-    if (bn == 128) return launch_bn<128>(ta, tb, p, sms, stream);
-    return launch_bn<256>(ta, tb, p, sms, stream);
+    p.res_vec = a.residual && a.out_dtype != SACC_DTYPE_F32 && (reinterpret_cast<std::uintptr_t>(a.residual) % 16 == 0) &&
+                ((a.ldr * 2) % 16 == 0);
+    CUtensorMap tc{};
+    p.tma_store = a.out_dtype != SACC_DTYPE_F32 && p.vec_store && c_map(&tc, a.out_dtype, a.c, a.n, a.m, a.ldc);
+    if (bn == 64) return launch_bn<64>(ta, tb, tc, p, sms, stream);
+    if (bn == 128) return launch_bn<128>(ta, tb, tc, p, sms, stream);
+    return launch_bn<256>(ta, tb, tc, p, sms, stream);
 }
 
 cudaError_t load_gemm_kernels(std::string& report) {

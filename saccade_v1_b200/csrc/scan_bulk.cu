@@ -28,8 +28,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <random>
 #include <mutex>
 #include <string>
 
@@ -49,6 +51,20 @@ constexpr int kStages = 2;
 constexpr int kN = 16;
 constexpr int kMinBlocks = 4; // four CTAs per SM: 128 registers per thread
 
+// One item of work: 128 channels of one row (or packed sequence) over the
+// chunk range of one part, with the tensor-map coordinates of the unit.
+struct Item {
+    unsigned long long b, d0, tok0, len;
+    int c0, c1, part, row0, bb, brow0, crow0;
+};
+
+// The producer's position in a CTA's list of (item, chunk) loads.
+struct Cursor {
+    Item w;
+    unsigned long long it;
+    int chunk, more;
+};
+
 template <typename T, bool kHasZ>
 struct Smem {
     alignas(1024) T u[kStages][kLanes * kT];
@@ -59,6 +75,7 @@ struct Smem {
     alignas(128) T craw[kStages][kN * kT];
     alignas(16) float bc[kT][2 * kN]; // per token: B[0..15], C[16..31] (C[16] only when rank 1)
     alignas(8) std::uint64_t full[kStages];
+    Cursor next; // thread 0 only
 };
 
 template <typename T, bool kHasZ>
@@ -72,9 +89,13 @@ struct BulkParams {
     const int32_t* cu; // packed varlen sequences ((B, L, D) with batch 1), else null
     void* y;           // plain stores of a varlen sequence's last, partial chunk
     unsigned long long length, channels, per_group;
+    unsigned long long units;    // (rows or packed sequences) x 128-channel tiles
+    unsigned long long epoch;    // this launch's hand-off flag value (split launches)
     unsigned groups;
     int a_shared, c_full, has_d, softplus, nchunks;
+    int parts;                   // chunk ranges per unit (> 1: split launch, cooperative)
 };
+
 
 template <typename T>
 __device__ __forceinline__ float2 unpack2(std::uint32_t w);
@@ -226,7 +247,133 @@ __device__ __forceinline__ void scan_block8(const float (*bc)[2 * kN], int q, in
     }
 }
 
-template <typename T, bool kBDL, bool kHasZ, bool kFullC>
+template <bool kBDL, bool kFullC>
+__device__ __forceinline__ Item item_at(const BulkParams& p, unsigned long long it) {
+    Item w;
+    // 32-bit index arithmetic: the launcher keeps items, units and channels
+    // below 2^31 (64-bit divisions would sit on every CTA's start-up path).
+    const unsigned long long D = p.channels, L = p.length;
+    const unsigned tiles = static_cast<unsigned>(D / kLanes), units = static_cast<unsigned>(p.units);
+    const unsigned it32 = static_cast<unsigned>(it);
+    const unsigned u = it32 % units;
+    w.part = static_cast<int>(it32 / units);
+    w.b = u / tiles;
+    w.d0 = static_cast<unsigned long long>(u % tiles) * kLanes;
+    const unsigned long long g = static_cast<unsigned>(w.d0) / static_cast<unsigned>(p.per_group);
+    const int cw = kFullC ? kN : 1;
+    // Token range: the whole row, or packed sequence b ((B, L, D), batch 1),
+    // its cu_seqlens entries clamped to [0, L] so no access leaves the tensors.
+    w.tok0 = 0;
+    w.len = L;
+    if (!kBDL && p.cu) {
+        const long long lo = p.cu[w.b], hi = p.cu[w.b + 1];
+        w.tok0 = lo < 0 ? 0 : (static_cast<unsigned long long>(lo) > L ? L : static_cast<unsigned long long>(lo));
+        const unsigned long long end = hi < 0 ? 0 : (static_cast<unsigned long long>(hi) > L ? L : static_cast<unsigned long long>(hi));
+        w.len = end > w.tok0 ? end - w.tok0 : 0;
+    }
+    const int nch = (!kBDL && p.cu) ? static_cast<int>((w.len + kT - 1) / kT) : p.nchunks;
+    w.c0 = p.parts == 1 ? 0 : static_cast<int>(static_cast<unsigned>(w.part * nch) / static_cast<unsigned>(p.parts));
+    w.c1 = p.parts == 1 ? nch : static_cast<int>(static_cast<unsigned>((w.part + 1) * nch) / static_cast<unsigned>(p.parts));
+    w.row0 = kBDL ? static_cast<int>(w.b * D + w.d0) : static_cast<int>(w.d0);
+    w.bb = (!kBDL && p.cu) ? 0 : static_cast<int>(w.b);
+    w.brow0 = kBDL ? static_cast<int>((w.b * p.groups + g) * kN) : static_cast<int>(g * kN);
+    w.crow0 = kBDL ? static_cast<int>((w.b * p.groups + g) * cw) : static_cast<int>(g * cw);
+    return w;
+}
+
+// Moves the producer to the next (item, chunk) of this CTA's list, skipping
+// items without chunks; `more` drops to 0 past the last one.
+template <bool kBDL, bool kFullC>
+__device__ __forceinline__ void cursor_next(Cursor& c, const BulkParams& p) {
+    if (++c.chunk < c.w.c1) return;
+    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts);
+    for (c.it += gridDim.x; c.it < items; c.it += gridDim.x) {
+        c.w = item_at<kBDL, kFullC>(p, c.it);
+        if (c.w.c1 > c.w.c0) {
+            c.chunk = c.w.c0;
+            return;
+        }
+    }
+    c.more = 0;
+}
+
+// Hand-off of a lane's 16 FP32 states from one part of a split unit to the
+// next, through the lane's own first 32 outputs of the next part (not yet
+// written: that part's CTA reads them before it stores its outputs there),
+// and a 64-bit flag = this launch's epoch in outputs 32..35 of the CTA's first
+// lane ((B, D, L)) or in channels 0..3 of token 32 ((B, L, D)).
+template <typename T, bool kBDL>
+__device__ __forceinline__ T* stash_at(const BulkParams& p, const Item& w, unsigned long long d, unsigned long long tp) {
+    T* y = static_cast<T*>(p.y);
+    return kBDL ? y + (w.b * p.channels + d) * p.length + tp : y + (w.b * p.length + tp) * p.channels + d;
+}
+
+template <typename T, bool kBDL>
+__device__ __forceinline__ void stash_store(const BulkParams& p, const Item& w, unsigned long long d, const float (&h)[kN]) {
+    T* at = stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c1) * kT);
+    if (kBDL) {
+        uint4* q = reinterpret_cast<uint4*>(at);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            q[k] = make_uint4(__float_as_uint(h[4 * k]), __float_as_uint(h[4 * k + 1]), __float_as_uint(h[4 * k + 2]),
+                              __float_as_uint(h[4 * k + 3]));
+    } else {
+        std::uint16_t* q = reinterpret_cast<std::uint16_t*>(at);
+#pragma unroll
+        for (int k = 0; k < kN; ++k) {
+            const std::uint32_t v = __float_as_uint(h[k]);
+            q[(2 * k) * p.channels] = static_cast<std::uint16_t>(v & 0xffffu);
+            q[(2 * k + 1) * p.channels] = static_cast<std::uint16_t>(v >> 16);
+        }
+    }
+}
+
+template <typename T, bool kBDL>
+__device__ __forceinline__ void stash_load(const BulkParams& p, const Item& w, unsigned long long d, float (&h)[kN]) {
+    const T* at = stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c0) * kT);
+    if (kBDL) {
+        const uint4* q = reinterpret_cast<const uint4*>(at);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 v = __ldcg(q + k);
+            h[4 * k] = __uint_as_float(v.x); h[4 * k + 1] = __uint_as_float(v.y);
+            h[4 * k + 2] = __uint_as_float(v.z); h[4 * k + 3] = __uint_as_float(v.w);
+        }
+    } else {
+        const unsigned short* q = reinterpret_cast<const unsigned short*>(at);
+#pragma unroll
+        for (int k = 0; k < kN; ++k) {
+            const std::uint32_t lo = __ldcg(q + (2 * k) * p.channels), hi = __ldcg(q + (2 * k + 1) * p.channels);
+            h[k] = __uint_as_float(lo | (hi << 16));
+        }
+    }
+}
+
+template <typename T, bool kBDL>
+__device__ __forceinline__ unsigned long long* flag_at(const BulkParams& p, const Item& w, unsigned long long tp) {
+    T* at = stash_at<T, kBDL>(p, w, w.d0, tp + (kBDL ? 32 : 32));
+    return reinterpret_cast<unsigned long long*>(at);
+}
+
+__device__ __forceinline__ void flag_release(unsigned long long* f, unsigned long long v) {
+    asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(f), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long flag_acquire(const unsigned long long* f) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+    return v;
+}
+
+// With kLoop each CTA walks items blockIdx.x, blockIdx.x + gridDim.x, ... (a
+// one-wave grid for split launches: parts > 1, cooperative so that every CTA
+// is resident, an item's part k waiting on part k - 1 of the same unit one
+// round earlier); without it a CTA takes exactly its own item (plain and
+// packed varlen launches, one CTA per unit: the straight-line form is 2 us
+// faster on one-chunk items).  Thread 0 keeps kStages chunk loads in
+// flight along the CTA's whole list, so the next item's first chunks arrive
+// while the current item computes.
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, bool kLoop>
 __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
                                                                   const __grid_constant__ CUtensorMap tm_d,
                                                                   const __grid_constant__ CUtensorMap tm_z,
@@ -236,29 +383,10 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     extern __shared__ unsigned char smem_raw[];
     auto& sm = *reinterpret_cast<Smem<T, kHasZ>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
     const int tid = threadIdx.x;
-    const unsigned long long D = p.channels, L = p.length;
-    const unsigned long long tiles_per_row = D / kLanes;
-    const unsigned long long b = blockIdx.x / tiles_per_row;
-    const unsigned long long d0 = (blockIdx.x % tiles_per_row) * kLanes, d = d0 + tid;
-    const unsigned long long lane = b * D + d;
-    const unsigned long long g = d0 / p.per_group;
+    const unsigned long long D = p.channels;
     const int cw = kFullC ? kN : 1;
-    // Token range: the whole row, or packed sequence b ((B, L, D), batch 1),
-    // its cu_seqlens entries clamped to [0, L] so no access leaves the tensors.
-    unsigned long long tok0 = 0, len = L;
-    if (!kBDL && p.cu) {
-        const long long lo = p.cu[b], hi = p.cu[b + 1];
-        tok0 = lo < 0 ? 0 : (static_cast<unsigned long long>(lo) > L ? L : static_cast<unsigned long long>(lo));
-        const unsigned long long end = hi < 0 ? 0 : (static_cast<unsigned long long>(hi) > L ? L : static_cast<unsigned long long>(hi));
-        len = end > tok0 ? end - tok0 : 0;
-    }
-    const int nchunks = (!kBDL && p.cu) ? static_cast<int>((len + kT - 1) / kT) : p.nchunks;
-    // Tensor-map coordinates of this CTA.
-    const int row0 = kBDL ? static_cast<int>(b * D + d0) : static_cast<int>(d0);
-    const int bb = (!kBDL && p.cu) ? 0 : static_cast<int>(b);
-    const int brow0 = kBDL ? static_cast<int>((b * p.groups + g) * kN) : static_cast<int>(g * kN);
-    const int crow0 = kBDL ? static_cast<int>((b * p.groups + g) * cw) : static_cast<int>(g * cw);
     const std::uint32_t c_bytes = static_cast<std::uint32_t>(cw) * kT * sizeof(T);
+    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts);
 
     if (tid == 0) {
         prefetch_tensor_map(&tm_u);
@@ -268,89 +396,142 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         prefetch_tensor_map(&tm_y);
         for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
         fence_barrier_init();
+        // First kStages loads of this CTA's (item, chunk) list.
+        Cursor& c = sm.next;
+        c.more = 1;
+        c.it = blockIdx.x;
+        if (c.it >= items) {
+            c.more = 0;
+        } else {
+            c.w = item_at<kBDL, kFullC>(p, c.it);
+            c.chunk = c.w.c0 - 1;
+            cursor_next<kBDL, kFullC>(c, p); // to the first chunk of the first item with chunks
+        }
+        for (int s = 0; s < kStages && c.more; ++s) {
+            issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
+                                        c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+            cursor_next<kBDL, kFullC>(c, p);
+        }
     }
     __syncthreads();
-    if (tid == 0)
-        for (int s = 0; s < kStages && s < nchunks; ++s)
-            issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(tok0) + s * kT, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d,
-                                        &tm_z, &tm_b, &tm_c);
-
-    // Per-lane constants: A * log2(e), D, dt bias, initial state.
-    float a[kN], h[kN];
-    const float* arow = p.a + (p.a_shared ? 0 : d * kN);
-#pragma unroll
-    for (int n = 0; n < kN; ++n) {
-        a[n] = arow[n] * kLog2e;
-        h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
-    }
-    const float dskip = p.has_d ? p.d[d] : 0.0f;
-    const float bias = p.bias ? p.bias[d] : 0.0f;
 
     bool fault = false;
-    for (int chunk = 0; chunk < nchunks; ++chunk) {
-        const int s = chunk % kStages;
-        const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((chunk / kStages) & 1));
-        if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
-        if (!__syncthreads_and(ok)) {
-            fault = true;
-            break;
-        }
-        // B / C tiles to an FP32 token-major table.
-        if (kBDL) {
-            // raw [state][token]: a thread takes 8 tokens of one state (16 bytes).
-            for (int i = tid; i < (kN + cw) * (kT / 8); i += kLanes) {
-                const int rowi = i / (kT / 8), t0 = (i % (kT / 8)) * 8;
-                const T* src = rowi < kN ? sm.braw[s] + rowi * kT + t0 : sm.craw[s] + (rowi - kN) * kT + t0;
-                const uint4 v = *reinterpret_cast<const uint4*>(src);
-                const std::uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    int gc = 0; // chunks this CTA has consumed: stage gc % kStages, its (gc / kStages)-th use
+    const unsigned long long it_end = kLoop ? items : blockIdx.x + 1ull;
+    for (unsigned long long it = blockIdx.x; it < it_end && (!kLoop || !fault); it += kLoop ? gridDim.x : 1u) {
+        const Item w = item_at<kBDL, kFullC>(p, it);
+        const unsigned long long d = w.d0 + tid, lane = w.b * D + d;
+        // Per-lane constants: A * log2(e), D, dt bias; the state from h0 (or
+        // zero) for a unit's first part, else from the previous part's hand-off.
+        float a[kN], h[kN];
+        const float* arow = p.a + (p.a_shared ? 0 : d * kN);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 f = unpack2<T>(w[j]);
-                    sm.bc[t0 + 2 * j][rowi] = f.x;
-                    sm.bc[t0 + 2 * j + 1][rowi] = f.y;
+        for (int n = 0; n < kN; ++n) a[n] = arow[n] * kLog2e;
+        const float dskip = p.has_d ? p.d[d] : 0.0f;
+        const float bias = p.bias ? p.bias[d] : 0.0f;
+        if (w.part == 0) {
+#pragma unroll
+            for (int n = 0; n < kN; ++n) h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
+        } else {
+            bool ready = true;
+            if (tid == 0) {
+                const unsigned long long* f = flag_at<T, kBDL>(p, w, static_cast<unsigned long long>(w.c0) * kT);
+                ready = false;
+                for (std::uint32_t i = 0; i < (1u << 24); ++i) {
+                    if (flag_acquire(f) == p.epoch) {
+                        ready = true;
+                        break;
+                    }
+                    __nanosleep(128);
                 }
             }
-        } else {
-            // raw [token][state]: already token-major.
-            for (int i = tid; i < kN * kT; i += kLanes) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
-            for (int i = tid; i < cw * kT; i += kLanes) sm.bc[i / cw][kN + i % cw] = to_f32(sm.craw[s][i]);
-        }
-        __syncthreads();
-
-        // Tokens past the end of the sequence (zero-filled by the TMA, or the
-        // next packed sequence) are not run through the recurrence.
-        const unsigned long long left = len - static_cast<unsigned long long>(chunk) * kT;
-        const int valid = static_cast<int>(left < kT ? left : kT);
-        const int blocks8 = (valid + 7) / 8;
-#pragma unroll 1
-        for (int q = 0; q < blocks8; ++q) {
-            Block8 blk;
-            if (kBDL) load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
-            else load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
-            float out[8];
-            scan_block8<kFullC, kHasZ, true>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out);
-            if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
-            else store_block_bld<T>(sm.y, tid, q, out);
-        }
-        fence_async_shared();
-        __syncthreads();
-        const int tc0 = static_cast<int>(tok0) + chunk * kT;
-        const bool tail = !kBDL && p.cu && valid < kT;
-        if (tail) {
-            // A packed sequence's partial last chunk: a tile store would also
-            // write the next sequence's rows, so store the valid rows only.
-            T* yg = static_cast<T*>(p.y);
-            for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
-        }
-        if (tid == 0) {
-            if (!tail) {
-                if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, row0);
-                else tma_store_3d(&tm_y, sm.y, row0, tc0, bb);
+            if (!__syncthreads_and(ready)) {
+                fault = true;
+                break;
             }
-            bulk_commit();
-            if (chunk + kStages < nchunks)
-                issue_chunk<T, kBDL, kHasZ>(sm, s, tc0 + kStages * kT, row0, brow0, crow0, bb, c_bytes, &tm_u, &tm_d, &tm_z,
-                                            &tm_b, &tm_c);
+            stash_load<T, kBDL>(p, w, d, h);
+        }
+
+        for (int chunk = w.c0; chunk < w.c1; ++chunk, ++gc) {
+            const int s = gc % kStages;
+            const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((gc / kStages) & 1));
+            if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
+            if (!__syncthreads_and(ok)) {
+                fault = true;
+                break;
+            }
+            // B / C tiles to an FP32 token-major table.
+            if (kBDL) {
+                // raw [state][token]: a thread takes 8 tokens of one state (16 bytes).
+                for (int i = tid; i < (kN + cw) * (kT / 8); i += kLanes) {
+                    const int rowi = i / (kT / 8), t0 = (i % (kT / 8)) * 8;
+                    const T* src = rowi < kN ? sm.braw[s] + rowi * kT + t0 : sm.craw[s] + (rowi - kN) * kT + t0;
+                    const uint4 v = *reinterpret_cast<const uint4*>(src);
+                    const std::uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = unpack2<T>(wv[j]);
+                        sm.bc[t0 + 2 * j][rowi] = f.x;
+                        sm.bc[t0 + 2 * j + 1][rowi] = f.y;
+                    }
+                }
+            } else {
+                // raw [token][state]: already token-major.
+                for (int i = tid; i < kN * kT; i += kLanes) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
+                for (int i = tid; i < cw * kT; i += kLanes) sm.bc[i / cw][kN + i % cw] = to_f32(sm.craw[s][i]);
+            }
+            __syncthreads();
+
+            // Tokens past the end of the sequence (zero-filled by the TMA, or the
+            // next packed sequence) are not run through the recurrence.
+            const unsigned long long left = w.len - static_cast<unsigned long long>(chunk) * kT;
+            const int valid = static_cast<int>(left < kT ? left : kT);
+            const int blocks8 = (valid + 7) / 8;
+#pragma unroll 1
+            for (int q = 0; q < blocks8; ++q) {
+                Block8 blk;
+                if (kBDL) load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                else load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                float out[8];
+                scan_block8<kFullC, kHasZ, true>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out);
+                if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
+                else store_block_bld<T>(sm.y, tid, q, out);
+            }
+            fence_async_shared();
+            __syncthreads();
+            const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
+            const bool tail = !kBDL && p.cu && valid < kT;
+            if (tail) {
+                // A packed sequence's partial last chunk: a tile store would also
+                // write the next sequence's rows, so store the valid rows only.
+                T* yg = static_cast<T*>(p.y);
+                for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
+            }
+            if (tid == 0) {
+                if (!tail) {
+                    if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, w.row0);
+                    else tma_store_3d(&tm_y, sm.y, w.row0, tc0, w.bb);
+                }
+                bulk_commit();
+                Cursor& c = sm.next;
+                if (c.more) {
+                    // Stage s is free again: the chunk kStages ahead in this CTA's list.
+                    issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
+                                                c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+                    cursor_next<kBDL, kFullC>(c, p);
+                }
+            }
+        }
+        if (fault) break;
+        if (w.part + 1 < p.parts) {
+            // Hand the state to the unit's next part.
+            stash_store<T, kBDL>(p, w, d, h);
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) flag_release(flag_at<T, kBDL>(p, w, static_cast<unsigned long long>(w.c1) * kT), p.epoch);
+        } else if (p.h_final) {
+#pragma unroll
+            for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
         }
     }
     if (fault) {
@@ -363,10 +544,6 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         return;
     }
     if (tid == 0) bulk_wait<0>();
-    if (p.h_final) {
-#pragma unroll
-        for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
-    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -413,9 +590,9 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, bool kBDL, bool kHasZ, bool kFullC>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, bool kLoop>
 struct Variant {
-    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC>); }
+    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kLoop>); }
     static cudaError_t prepare() {
         static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                                static_cast<int>(smem_bytes<T, kHasZ>()));
@@ -431,23 +608,90 @@ struct Pick {
 };
 
 template <typename T, bool kBDL, bool kHasZ, bool kFullC>
-Pick make_pick() {
-    using V = Variant<T, kBDL, kHasZ, kFullC>;
+Pick make_pick(bool loop) {
+    if (loop) {
+        using V = Variant<T, kBDL, kHasZ, kFullC, true>;
+        return {V::fn(), V::smem(), &V::prepare};
+    }
+    using V = Variant<T, kBDL, kHasZ, kFullC, false>;
     return {V::fn(), V::smem(), &V::prepare};
 }
 
 template <typename T, bool kBDL>
-Pick pick_z(bool z, bool full_c) {
-    if (z) return full_c ? make_pick<T, kBDL, true, true>() : make_pick<T, kBDL, true, false>();
-    return full_c ? make_pick<T, kBDL, false, true>() : make_pick<T, kBDL, false, false>();
+Pick pick_z(bool z, bool full_c, bool loop) {
+    if (z) return full_c ? make_pick<T, kBDL, true, true>(loop) : make_pick<T, kBDL, true, false>(loop);
+    return full_c ? make_pick<T, kBDL, false, true>(loop) : make_pick<T, kBDL, false, false>(loop);
 }
 
-Pick pick(int dtype, bool bdl, bool z, bool full_c) {
-    if (dtype == SACC_DTYPE_BF16) return bdl ? pick_z<__nv_bfloat16, true>(z, full_c) : pick_z<__nv_bfloat16, false>(z, full_c);
-    return bdl ? pick_z<__half, true>(z, full_c) : pick_z<__half, false>(z, full_c);
+Pick pick(int dtype, bool bdl, bool z, bool full_c, bool loop) {
+    if (dtype == SACC_DTYPE_BF16)
+        return bdl ? pick_z<__nv_bfloat16, true>(z, full_c, loop) : pick_z<__nv_bfloat16, false>(z, full_c, loop);
+    return bdl ? pick_z<__half, true>(z, full_c, loop) : pick_z<__half, false>(z, full_c, loop);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
+
+// CTAs of a variant resident at once on the current device (SMs x CTAs per
+// SM), queried once per (variant, device).
+unsigned long long resident_ctas(const Pick& k) {
+    struct Entry {
+        const void* fn;
+        int dev;
+        unsigned long long ctas;
+    };
+    static std::mutex mu;
+    static Entry cache[64];
+    static int used = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (int i = 0; i < used; ++i)
+            if (cache[i].fn == k.fn && cache[i].dev == dev) return cache[i].ctas;
+    }
+    int sms = 148, per_sm = 1;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kLanes, k.smem) != cudaSuccess || per_sm < 1) per_sm = 1;
+    const unsigned long long ctas = static_cast<unsigned long long>(sms) * static_cast<unsigned long long>(per_sm);
+    std::lock_guard<std::mutex> lock(mu);
+    if (used < 64) cache[used++] = Entry{k.fn, dev, ctas};
+    return ctas;
+}
+
+// Parts per unit for a launch of `units` one-CTA units onto `wave` resident
+// CTAs: 1 when they fit one wave; else the P in 2..8 that minimises the
+// makespan ceil(units * P / wave) / P (in units of one whole-unit time), each
+// part keeping at least two chunks (the hand-off needs 36 tokens of the next
+// part), if that is at least 10 % below the unsplit ceil(units / wave) (the
+// hand-offs and per-part pipeline starts cost a few percent).
+int split_parts(unsigned long long units, unsigned long long wave, int nchunks) {
+    if (units <= wave || wave == 0) return 1;
+    const double unsplit = static_cast<double>((units + wave - 1) / wave);
+    double best = 0.9 * unsplit;
+    int parts = 1;
+    for (int P = 2; P <= 8; ++P) {
+        if (nchunks / P < 2) break;
+        const double span = static_cast<double>((units * P + wave - 1) / wave) / P;
+        if (span < best - 1e-9) {
+            best = span;
+            parts = P;
+        }
+    }
+    return parts;
+}
+
+// A value no earlier split launch of this process used, never zero: the
+// hand-off flags in the output are compared against it.
+unsigned long long next_epoch() {
+    static std::atomic<unsigned long long> counter{0};
+    static const unsigned long long salt = [] {
+        std::random_device rd;
+        return (static_cast<unsigned long long>(rd()) << 32) ^ rd() ^ 0x9E3779B97F4A7C15ull;
+    }();
+    unsigned long long v = 0;
+    while (v == 0) v = (counter.fetch_add(1) + 1) * 0xD6E8FEB86659FD93ull ^ salt;
+    return v;
+}
 
 } // namespace
 
@@ -516,11 +760,38 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     p.cu = bdl ? nullptr : a.cu_seqlens;
     p.y = a.y;
     const unsigned long long rows = a.cu_seqlens ? static_cast<unsigned long long>(a.nseq) : B; // sequences
-    const Pick k = pick(a.dtype, bdl, a.z != nullptr, cw != 1);
-    const cudaError_t attr = k.prepare();
+    p.units = rows * (D / kLanes);
+    p.parts = 1;
+    p.epoch = 0;
+    const Pick loop = pick(a.dtype, bdl, a.z != nullptr, cw != 1, true);
+    cudaError_t attr = loop.prepare();
     if (attr != cudaSuccess) return attr;
+    const unsigned long long wave = resident_ctas(loop);
     void* args[] = {&tu, &td, &tz, &tb, &tc, &ty, &p};
-    return cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(rows * D / kLanes)), dim3(kLanes), args, k.smem, stream);
+    // Packed varlen sequences (one CTA per sequence x 128 channels: persistent
+    // CTAs were slower, each sequence's start waiting on its h0 row) and
+    // launches that fit one wave or gain nothing from a split: one item per CTA.
+    p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks);
+    if (p.parts == 1) {
+        const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
+        if ((attr = one.prepare()) != cudaSuccess) return attr;
+        return cudaLaunchKernel(one.fn, dim3(static_cast<unsigned>(p.units)), dim3(kLanes), args, one.smem, stream);
+    }
+    const Pick& k = loop;
+    // Split launch: every CTA resident (cooperative), one wave, a fresh epoch
+    // for the hand-off flags.
+    p.epoch = next_epoch();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(wave));
+    cfg.blockDim = dim3(kLanes);
+    cfg.dynamicSmemBytes = k.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute coop{};
+    coop.id = cudaLaunchAttributeCooperative;
+    coop.val.cooperative = 1;
+    cfg.attrs = &coop;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, k.fn, args);
 }
 
 cudaError_t load_scan_bulk_kernels(std::string& report) {
@@ -529,11 +800,13 @@ cudaError_t load_scan_bulk_kernels(std::string& report) {
         for (int bdl = 0; bdl < 2; ++bdl)
             for (int z = 0; z < 4; ++z) {
                 if (!bdl && (z & 2) == 0) continue; // (B, L, D) always has a full-width C
-                const Pick k = pick(dtype, bdl != 0, (z & 1) != 0, (z & 2) != 0);
-                cudaFuncAttributes attr{};
+                const Pick k = pick(dtype, bdl != 0, (z & 1) != 0, (z & 2) != 0, false);
+                const Pick kl = pick(dtype, bdl != 0, (z & 1) != 0, (z & 2) != 0, true);
+                cudaFuncAttributes attr{}, attr_loop{};
                 cudaError_t e = cudaFuncGetAttributes(&attr, k.fn);
-                if (e != cudaSuccess) return e;
-                e = k.prepare();
+                if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr_loop, kl.fn);
+                if (e == cudaSuccess) e = k.prepare();
+                if (e == cudaSuccess) e = kl.prepare();
                 if (e != cudaSuccess) return e;
                 report += std::string("kernel=scan_bulk_") + names[bdl] + (dtype == SACC_DTYPE_BF16 ? "_bf16" : "_f16") +
                           ((z & 1) ? "_gate" : "") + ((z & 2) ? "" : "_rank1c") + " registers=" + std::to_string(attr.numRegs) +

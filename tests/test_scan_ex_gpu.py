@@ -316,3 +316,43 @@ def test_varlen_entries_are_clamped(dt):
     np.testing.assert_array_equal(hf[1], h0[1])
     np.testing.assert_array_equal(hf[3], h0[3])
     assert ctypes_fault() == 0
+
+
+@pytest.mark.parametrize("layout", ["BDL", "BLD"])
+def test_bulk_split_launch_bitwise_equals_unsplit(layout):
+    """A batch large enough that the units exceed one wave of CTAs is split
+    along L (each unit's parts hand their state over through the output, under
+    a cooperative launch); the same rows run as slices small enough for one
+    wave are not split.  The hand-off moves exact FP32 states, so outputs and
+    final states agree bit for bit.  Gate, h0 and h_final included."""
+    B, L, D, N = 48, 1024, 1536, 16
+    s = torch.cuda.Stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(61)
+    bf = torch.bfloat16
+    with torch.cuda.stream(s):
+        if layout == "BDL":
+            mk = lambda: torch.randn(B, D, L, device="cuda", generator=g).to(bf)
+            mkbc = lambda: torch.randn(B, 1, N, L, device="cuda", generator=g).to(bf)
+        else:
+            mk = lambda: torch.randn(B, L, D, device="cuda", generator=g).to(bf)
+            mkbc = lambda: torch.randn(B, L, 1, N, device="cuda", generator=g).to(bf)
+        u, dl, z, bm, cm = mk(), mk(), mk(), mkbc(), mkbc()
+        A = -(torch.rand(D, N, device="cuda", generator=g) * 4 + 0.1)
+        Dv = torch.randn(D, device="cuda", generator=g)
+        bias = torch.full((D,), -3.0, device="cuda")
+        h0 = torch.randn(B, D, N, device="cuda", generator=g) * 0.5
+        hf = torch.empty(B, D, N, device="cuda")
+        y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
+        ys, hs = [], []
+        for b0 in range(0, B, 8):
+            sl = slice(b0, b0 + 8)
+            hfi = torch.empty(8, D, N, device="cuda")
+            ys.append(sb.selective_scan_ex(u[sl].contiguous(), dl[sl].contiguous(), A, bm[sl].contiguous(), cm[sl].contiguous(),
+                                           D=Dv, z=z[sl].contiguous(), delta_bias=bias, h0=h0[sl].contiguous(), h_final=hfi,
+                                           layout=layout, stream=s))
+            hs.append(hfi)
+    s.synchronize()
+    assert torch.equal(y.view(torch.int16), torch.cat(ys).view(torch.int16))
+    assert torch.equal(hf.view(torch.int32), torch.cat(hs).view(torch.int32))
+    assert ctypes_fault() == 0

@@ -7,18 +7,25 @@
 // diag(r) x (W diag(w))^T with r = 1 / sqrt(mean(x^2) + eps) per token, so the
 // prologue is one pass computing r (applied as a row scale in the GEMM
 // epilogue) and a once-per-call scaling of the weight columns by w.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <type_traits>
 
 #include "internal.h"
 #include "scan_common.cuh"
+#include "tma.cuh"
 
 namespace sacc {
+
+__device__ unsigned int g_block_fault; // set when a bounded wait of a block kernel ran out
+
 namespace {
 
 // One warp per token row: r[m] = 1 / sqrt(mean_k x[m,k]^2 + eps).
@@ -150,7 +157,82 @@ __global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restric
     }
 }
 
+// Same conv + SiLU over TMA tiles: a CTA takes 64 token rows x 128 channels
+// of one sequence, loads rows t0 - 3 .. t0 + 63 in one 3D tile (channel, token,
+// sequence) -- rows before the sequence start and past its end read as zeros,
+// which is the causal padding -- and each thread slides the 4-tap window down
+// its channel, so every input row is read once (plus a 3-row halo per tile).
+// Same operations in the same order as the kernels above, so the same bits.
+constexpr int kConvRows = 64, kConvCh = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kConvCh) conv4_silu_tile_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                                 const float* __restrict__ w, const float* __restrict__ bias,
+                                                                 unsigned long long len, unsigned long long dim,
+                                                                 unsigned tiles_per_seq, T* __restrict__ u) {
+    __shared__ alignas(128) T tile[(kConvRows + 3) * kConvCh];
+    __shared__ alignas(8) std::uint64_t bar;
+    const int tid = threadIdx.x;
+    const unsigned long long b = blockIdx.x / tiles_per_seq;
+    const int t0 = static_cast<int>(blockIdx.x % tiles_per_seq) * kConvRows;
+    const unsigned d0 = blockIdx.y * kConvCh;
+    if (tid == 0) {
+        prefetch_tensor_map(&tm_x);
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&bar, static_cast<std::uint32_t>(sizeof(tile)));
+        tma_load_3d(tile, &tm_x, &bar, static_cast<int>(d0), t0 - 3, static_cast<int>(b));
+    }
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (d0 + tid) * 4ull));
+    const float bv = bias ? __ldg(bias + d0 + tid) : 0.0f;
+    const bool ok = mbar_wait_bounded(&bar, 0u);
+    if (!__syncthreads_and(ok)) {
+        if (tid == 0) atomicOr(&g_block_fault, 1u);
+        return;
+    }
+    float x0 = to_f32(tile[tid]), x1 = to_f32(tile[kConvCh + tid]), x2 = to_f32(tile[2 * kConvCh + tid]);
+    const unsigned long long left = len - static_cast<unsigned long long>(t0);
+    const int rows = left < static_cast<unsigned long long>(kConvRows) ? static_cast<int>(left) : kConvRows;
+    T* out = u + (b * len + static_cast<unsigned long long>(t0)) * dim + d0 + tid;
+#pragma unroll 4
+    for (int r = 0; r < rows; ++r) {
+        const float x3 = to_f32(tile[(r + 3) * kConvCh + tid]);
+        float acc = bv;
+        acc = fmaf(wv.x, x0, acc);
+        acc = fmaf(wv.y, x1, acc);
+        acc = fmaf(wv.z, x2, acc);
+        acc = fmaf(wv.w, x3, acc);
+        out[static_cast<unsigned long long>(r) * dim] = from_f32<T>(silu(acc));
+        x0 = x1;
+        x1 = x2;
+        x2 = x3;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 conv_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
 } // namespace
+
+cudaError_t read_block_fault(unsigned* out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_block_fault, sizeof(unsigned));
+    if (e != cudaSuccess || !clear) return e;
+    const unsigned zero = 0;
+    return cudaMemcpyToSymbol(g_block_fault, &zero, sizeof(unsigned));
+}
 
 cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
                              cudaStream_t stream) {
@@ -182,6 +264,29 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
                              cudaStream_t stream) {
     if (kwidth != 4) return cudaErrorInvalidConfiguration;
     const auto al16 = [](const void* ptr) { return reinterpret_cast<std::uintptr_t>(ptr) % 16 == 0; };
+    // TMA tiles: channels in 128-wide blocks, 16-byte aligned rows.
+    const unsigned long long tiles_per_seq = (len + kConvRows - 1) / kConvRows;
+    auto enc = conv_encoder();
+    if (enc && dim % kConvCh == 0 && ldx % 8 == 0 && al16(x) && al16(w) && len > 0 && batch * tiles_per_seq <= 0x7fffffffull &&
+        dim / kConvCh <= 65535 && len < 0x7fffffffull && batch < 0x7fffffffull) {
+        CUtensorMap tm{};
+        const cuuint64_t dims[3] = {dim, len, batch};
+        const cuuint64_t strides[2] = {ldx * 2, ldx * 2 * len};
+        const cuuint32_t box[3] = {kConvCh, kConvRows + 3, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        const CUtensorMapDataType dt = dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if (enc(&tm, dt, 3, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            const dim3 grid(static_cast<unsigned>(batch * tiles_per_seq), static_cast<unsigned>(dim / kConvCh));
+            const unsigned tps = static_cast<unsigned>(tiles_per_seq);
+            if (dtype == SACC_DTYPE_BF16)
+                conv4_silu_tile_kernel<__nv_bfloat16><<<grid, kConvCh, 0, stream>>>(tm, w, bias, len, dim, tps,
+                                                                                      static_cast<__nv_bfloat16*>(u));
+            else
+                conv4_silu_tile_kernel<__half><<<grid, kConvCh, 0, stream>>>(tm, w, bias, len, dim, tps, static_cast<__half*>(u));
+            return cudaGetLastError();
+        }
+    }
     const unsigned long long threads = batch * ((len + 3) / 4) * (dim / 8), row_blocks = (threads + 255) / 256;
     if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks * 256 < 0xffffffffull && len > 0) {
         if (row_blocks == 0) return cudaSuccess;
@@ -212,13 +317,15 @@ cudaError_t load_block_kernels(std::string& report) {
                         reinterpret_cast<const void*>(conv_silu_kernel<__nv_bfloat16, 4>),
                         reinterpret_cast<const void*>(conv_silu_kernel<__half, 4>),
                         reinterpret_cast<const void*>(conv4_silu_rows_kernel<__nv_bfloat16>),
-                        reinterpret_cast<const void*>(conv4_silu_rows_kernel<__half>)};
+                        reinterpret_cast<const void*>(conv4_silu_rows_kernel<__half>),
+                        reinterpret_cast<const void*>(conv4_silu_tile_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(conv4_silu_tile_kernel<__half>)};
     for (const void* k : ks) {
         cudaFuncAttributes attr{};
         const cudaError_t e = cudaFuncGetAttributes(&attr, k);
         if (e != cudaSuccess) return e;
     }
-    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x8\n";
+    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x10\n";
     return cudaSuccess;
 }
 

@@ -253,11 +253,12 @@ int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, f
 int sacc_scan_fault(uint32_t* out, int clear) {
     return guarded([&] {
         if (out == nullptr) reject("sacc_scan_fault", "out is required");
-        unsigned scan = 0, step = 0, gemm = 0;
+        unsigned scan = 0, step = 0, gemm = 0, block = 0;
         CK(read_bulk_fault(&scan, clear != 0));
         CK(read_step_fault(&step, clear != 0));
         CK(read_gemm_fault(&gemm, clear != 0));
-        *out = (scan || step ? 1u : 0u) | (gemm ? 2u : 0u);
+        CK(read_block_fault(&block, clear != 0));
+        *out = (scan || step || block ? 1u : 0u) | (gemm ? 2u : 0u);
     });
 }
 

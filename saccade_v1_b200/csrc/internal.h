@@ -70,6 +70,7 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
                              unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
                              cudaStream_t stream);
 cudaError_t load_block_kernels(std::string& report);
+cudaError_t read_block_fault(unsigned* out, bool clear);
 std::size_t mamba_block_workspace(const SaccMambaBlockArgs& a);
 cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cudaStream_t stream);
 // Same forward with the intermediates in a static device array of

@@ -65,11 +65,14 @@ struct Cursor {
     int chunk, more;
 };
 
-template <typename T, bool kHasZ>
+// kZTile: the gate z staged by TMA ((B, D, L) with a gate); in (B, L, D) a
+// warp's z of one token is 64 contiguous bytes, read straight from global
+// memory, so the gated kernel keeps four CTAs per SM.
+template <typename T, bool kZTile>
 struct Smem {
     alignas(1024) T u[kStages][kLanes * kT];
     alignas(1024) T dl[kStages][kLanes * kT];
-    alignas(1024) T z[kHasZ ? kStages : 1][kHasZ ? kLanes * kT : 8];
+    alignas(1024) T z[kZTile ? kStages : 1][kZTile ? kLanes * kT : 8];
     alignas(1024) T y[kLanes * kT];
     alignas(128) T braw[kStages][kN * kT];
     alignas(128) T craw[kStages][kN * kT];
@@ -78,9 +81,9 @@ struct Smem {
     Cursor next; // thread 0 only
 };
 
-template <typename T, bool kHasZ>
+template <typename T, bool kZTile>
 constexpr size_t smem_bytes() {
-    return sizeof(Smem<T, kHasZ>) + 1024; // + alignment slack for the 1024-byte swizzle atoms
+    return sizeof(Smem<T, kZTile>) + 1024; // + alignment slack for the 1024-byte swizzle atoms
 }
 
 struct BulkParams {
@@ -88,6 +91,8 @@ struct BulkParams {
     float* h_final;
     const int32_t* cu; // packed varlen sequences ((B, L, D) with batch 1), else null
     void* y;           // plain stores of a varlen sequence's last, partial chunk
+    const void* zg;    // (B, L, D) gate, read from global memory
+    unsigned long long zld; // its row pitch (elements between tokens)
     unsigned long long length, channels, per_group;
     unsigned long long units;    // (rows or packed sequences) x 128-channel tiles
     unsigned long long epoch;    // this launch's hand-off flag value (split launches)
@@ -166,13 +171,20 @@ __device__ __forceinline__ void store_block_bdl(T* y, int tid, int q, const floa
 
 // (B, L, D): token-major [32][128] tile; lane `tid` is column tid.
 template <typename T, bool kHasZ>
-__device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T* z, int tid, int q, Block8& blk) {
+// The gate of the first `count` tokens from global memory (token rows zrow0 + ...).
+__device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T* zg, unsigned long long zrow0,
+                                               unsigned long long zld, unsigned long long d, int tid, int q, int count,
+                                               Block8& blk) {
+    if constexpr (kHasZ) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            blk.z[j] = j < count ? to_f32(zg[(zrow0 + static_cast<unsigned long long>(q * 8 + j)) * zld + d]) : 0.0f;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int at = (q * 8 + j) * kLanes + tid;
         blk.u[j] = to_f32(u[at]);
         blk.x[j] = to_f32(dl[at]);
-        if constexpr (kHasZ) blk.z[j] = to_f32(z[at]);
     }
 }
 
@@ -187,11 +199,11 @@ __device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const floa
 // so that a chunk past the end of a sequence reads zeros instead of the next
 // sequence; a packed varlen sequence reads whatever follows it, unused.
 template <typename T, bool kBDL, bool kHasZ>
-__device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
+__device__ __forceinline__ void issue_chunk(Smem<T, kBDL && kHasZ>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
                                             std::uint32_t c_bytes, const CUtensorMap* tu, const CUtensorMap* td,
                                             const CUtensorMap* tz, const CUtensorMap* tb, const CUtensorMap* tc) {
     constexpr std::uint32_t tile = kLanes * kT * sizeof(T), btile = kN * kT * sizeof(T);
-    mbar_arrive_expect_tx(&sm.full[s], tile * (kHasZ ? 3u : 2u) + btile + c_bytes);
+    mbar_arrive_expect_tx(&sm.full[s], tile * (kBDL && kHasZ ? 3u : 2u) + btile + c_bytes);
     if (kBDL) {
         tma_load_2d(sm.u[s], tu, &sm.full[s], t0, row0);
         tma_load_2d(sm.dl[s], td, &sm.full[s], t0, row0);
@@ -201,7 +213,6 @@ __device__ __forceinline__ void issue_chunk(Smem<T, kHasZ>& sm, int s, int t0, i
     } else {
         tma_load_3d(sm.u[s], tu, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.dl[s], td, &sm.full[s], row0, t0, bb);
-        if constexpr (kHasZ) tma_load_3d(sm.z[s], tz, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
         tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
     }
@@ -381,7 +392,8 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                                                                   const __grid_constant__ CUtensorMap tm_c,
                                                                   const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
     extern __shared__ unsigned char smem_raw[];
-    auto& sm = *reinterpret_cast<Smem<T, kHasZ>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    auto& sm = *reinterpret_cast<Smem<T, kBDL && kHasZ>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) &
+                                                       ~std::uintptr_t(1023));
     const int tid = threadIdx.x;
     const unsigned long long D = p.channels;
     const int cw = kFullC ? kN : 1;
@@ -490,8 +502,13 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
 #pragma unroll 1
             for (int q = 0; q < blocks8; ++q) {
                 Block8 blk;
-                if (kBDL) load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
-                else load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                if constexpr (kBDL)
+                    load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                else
+                    load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], static_cast<const T*>(p.zg),
+                                             static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
+                                                 static_cast<unsigned long long>(chunk) * kT,
+                                             p.zld, d, tid, q, valid - q * 8, blk);
                 float out[8];
                 scan_block8<kFullC, kHasZ, true>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out);
                 if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
@@ -595,10 +612,10 @@ struct Variant {
     static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kLoop>); }
     static cudaError_t prepare() {
         static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                               static_cast<int>(smem_bytes<T, kHasZ>()));
+                                                               static_cast<int>(smem_bytes<T, kBDL && kHasZ>()));
         return status;
     }
-    static size_t smem() { return smem_bytes<T, kHasZ>(); }
+    static size_t smem() { return smem_bytes<T, kBDL && kHasZ>(); }
 };
 
 struct Pick {
@@ -662,12 +679,13 @@ unsigned long long resident_ctas(const Pick& k) {
 // CTAs: 1 when they fit one wave; else the P in 2..8 that minimises the
 // makespan ceil(units * P / wave) / P (in units of one whole-unit time), each
 // part keeping at least two chunks (the hand-off needs 36 tokens of the next
-// part), if that is at least 10 % below the unsplit ceil(units / wave) (the
-// hand-offs and per-part pipeline starts cost a few percent).
+// part), if that is at least 15 % below the unsplit ceil(units / wave) (the
+// hand-offs and per-part pipeline starts cost a few percent; a 12.5 % gain
+// measured as a loss at config 4).
 int split_parts(unsigned long long units, unsigned long long wave, int nchunks) {
     if (units <= wave || wave == 0) return 1;
     const double unsplit = static_cast<double>((units + wave - 1) / wave);
-    double best = 0.9 * unsplit;
+    double best = 0.85 * unsplit;
     int parts = 1;
     for (int P = 2; P <= 8; ++P) {
         if (nchunks / P < 2) break;
@@ -759,6 +777,8 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     p.nchunks = static_cast<int>((L + kT - 1) / kT);
     p.cu = bdl ? nullptr : a.cu_seqlens;
     p.y = a.y;
+    p.zg = a.z;
+    p.zld = rs->z ? rs->z : D;
     const unsigned long long rows = a.cu_seqlens ? static_cast<unsigned long long>(a.nseq) : B; // sequences
     p.units = rows * (D / kLanes);
     p.parts = 1;

@@ -325,7 +325,7 @@ def test_bulk_split_launch_bitwise_equals_unsplit(layout):
     a cooperative launch); the same rows run as slices small enough for one
     wave are not split.  The hand-off moves exact FP32 states, so outputs and
     final states agree bit for bit.  Gate, h0 and h_final included."""
-    B, L, D, N = 48, 1024, 1536, 16
+    B, L, D, N = 64, 1024, 1536, 16  # 768 units of 128 channels: more than one wave in either layout
     s = torch.cuda.Stream()
     g = torch.Generator(device="cuda")
     g.manual_seed(61)

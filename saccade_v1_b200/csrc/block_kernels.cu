@@ -32,6 +32,7 @@ namespace {
 template <typename T>
 __global__ void __launch_bounds__(256) rms_scale_kernel(const T* __restrict__ x, unsigned long long m, unsigned k,
                                                         float eps, float* __restrict__ r) {
+    pdl_wait();
     const unsigned long long row = (static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x) / 32;
     const int lane = threadIdx.x % 32;
     if (row >= m) return;
@@ -50,6 +51,7 @@ __global__ void __launch_bounds__(256) rms_scale_kernel(const T* __restrict__ x,
 template <typename T>
 __global__ void __launch_bounds__(256) scale_columns_kernel(const T* __restrict__ w_in, const float* __restrict__ w,
                                                             unsigned long long n, unsigned k, T* __restrict__ out) {
+    pdl_wait();
     const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
     if (i >= n * k) return;
     out[i] = from_f32<T>(to_f32(w_in[i]) * w[i % k]);
@@ -66,6 +68,7 @@ __global__ void __launch_bounds__(256) conv_silu_kernel(const T* __restrict__ x,
                                                         const float* __restrict__ w, const float* __restrict__ bias,
                                                         unsigned long long batch, unsigned long long len,
                                                         unsigned long long dim, T* __restrict__ u) {
+    pdl_wait();
     const unsigned long long lane = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
     if (lane >= batch * dim) return;
     const unsigned long long b = lane / dim, d = lane % dim;
@@ -100,6 +103,7 @@ __global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restric
                                                               const float* __restrict__ w, const float* __restrict__ bias,
                                                               unsigned long long batch, unsigned long long len,
                                                               unsigned long long dim, T* __restrict__ u) {
+    pdl_wait();
     constexpr int K = 4, R = 4; // taps, rows per thread
     // 32-bit index arithmetic (the launcher keeps the thread count below 2^32).
     const unsigned groups = static_cast<unsigned>(dim / 8), quads = static_cast<unsigned>((len + R - 1) / R);
@@ -170,6 +174,7 @@ __global__ void __launch_bounds__(kConvCh) conv4_silu_tile_kernel(const __grid_c
                                                                  const float* __restrict__ w, const float* __restrict__ bias,
                                                                  unsigned long long len, unsigned long long dim,
                                                                  unsigned tiles_per_seq, T* __restrict__ u) {
+    pdl_wait();
     __shared__ alignas(128) T tile[(kConvRows + 3) * kConvCh];
     __shared__ alignas(8) std::uint64_t bar;
     const int tid = threadIdx.x;
@@ -239,11 +244,10 @@ cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, uns
     const unsigned long long blocks = (m * 32 + 255) / 256;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
     if (dtype == SACC_DTYPE_BF16)
-        rms_scale_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), m, k, eps, r);
-    else
-        rms_scale_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __half*>(x), m, k, eps, r);
-    return cudaGetLastError();
+        return launch_pdl_k(rms_scale_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                            static_cast<const __nv_bfloat16*>(x), m, k, eps, r);
+    return launch_pdl_k(rms_scale_kernel<__half>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                        static_cast<const __half*>(x), m, k, eps, r);
 }
 
 cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
@@ -251,12 +255,10 @@ cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, un
     const unsigned long long blocks = (n * k + 255) / 256;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
     if (dtype == SACC_DTYPE_BF16)
-        scale_columns_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(w_in), w, n, k, static_cast<__nv_bfloat16*>(out));
-    else
-        scale_columns_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __half*>(w_in), w, n,
-                                                                                        k, static_cast<__half*>(out));
-    return cudaGetLastError();
+        return launch_pdl_k(scale_columns_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                            static_cast<const __nv_bfloat16*>(w_in), w, n, k, static_cast<__nv_bfloat16*>(out));
+    return launch_pdl_k(scale_columns_kernel<__half>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                        static_cast<const __half*>(w_in), w, n, k, static_cast<__half*>(out));
 }
 
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
@@ -280,23 +282,21 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
             const dim3 grid(static_cast<unsigned>(batch * tiles_per_seq), static_cast<unsigned>(dim / kConvCh));
             const unsigned tps = static_cast<unsigned>(tiles_per_seq);
             if (dtype == SACC_DTYPE_BF16)
-                conv4_silu_tile_kernel<__nv_bfloat16><<<grid, kConvCh, 0, stream>>>(tm, w, bias, len, dim, tps,
-                                                                                      static_cast<__nv_bfloat16*>(u));
-            else
-                conv4_silu_tile_kernel<__half><<<grid, kConvCh, 0, stream>>>(tm, w, bias, len, dim, tps, static_cast<__half*>(u));
-            return cudaGetLastError();
+                return launch_pdl_k(conv4_silu_tile_kernel<__nv_bfloat16>, grid, dim3(kConvCh), 0, stream, tm, w, bias, len, dim,
+                                    tps, static_cast<__nv_bfloat16*>(u));
+            return launch_pdl_k(conv4_silu_tile_kernel<__half>, grid, dim3(kConvCh), 0, stream, tm, w, bias, len, dim, tps,
+                                static_cast<__half*>(u));
         }
     }
     const unsigned long long threads = batch * ((len + 3) / 4) * (dim / 8), row_blocks = (threads + 255) / 256;
     if (dim % 8 == 0 && ldx % 8 == 0 && al16(x) && al16(u) && al16(w) && row_blocks * 256 < 0xffffffffull && len > 0) {
         if (row_blocks == 0) return cudaSuccess;
         if (dtype == SACC_DTYPE_BF16)
-            conv4_silu_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
-                static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u));
-        else
-            conv4_silu_rows_kernel<__half><<<static_cast<unsigned>(row_blocks), 256, 0, stream>>>(
-                static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
-        return cudaGetLastError();
+            return launch_pdl_k(conv4_silu_rows_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(row_blocks)), dim3(256), 0,
+                                stream, static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim,
+                                static_cast<__nv_bfloat16*>(u));
+        return launch_pdl_k(conv4_silu_rows_kernel<__half>, dim3(static_cast<unsigned>(row_blocks)), dim3(256), 0, stream,
+                            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
     }
     const unsigned long long blocks = (batch * dim + 255) / 256;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;

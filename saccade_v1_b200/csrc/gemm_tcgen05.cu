@@ -285,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     tmem_fence_after();
     const std::uint32_t tmem = sm.tmem_base;
+    // barriers and TMEM are set up; the previous kernel's results come next
+    pdl_wait();
 
     bool fault = false;
     if (warp == 0) {
@@ -475,8 +477,8 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
     const long long slots = static_cast<long long>(sm_count) * (BN == 64 ? 2 : 1);
     const unsigned grid = static_cast<unsigned>(tiles < slots ? tiles : slots);
     void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), const_cast<CUtensorMap*>(&tc), &p};
-    return cudaLaunchKernel(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), args,
-                            gemm_smem<BN>(), stream);
+    return launch_pdl(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), gemm_smem<BN>(), stream,
+                      args);
 }
 
 } // namespace

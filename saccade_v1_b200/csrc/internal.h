@@ -12,6 +12,23 @@
 
 namespace sacc {
 
+// Launches `fn` with programmatic stream serialization (its set-up may overlap
+// the previous kernel of the stream; the kernel itself waits for that
+// kernel's results with griddepcontrol.wait).
+inline cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, std::size_t smem, cudaStream_t stream, void** args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 // int32 element capacity of every tensor of the reference ABI
 // (reference src/selective_scan.cpp:79, cuda/selective_scan.cu:119).
 constexpr std::size_t kMaxElements = 2147483647u;

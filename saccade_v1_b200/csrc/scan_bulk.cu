@@ -391,6 +391,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                                                                   const __grid_constant__ CUtensorMap tm_b,
                                                                   const __grid_constant__ CUtensorMap tm_c,
                                                                   const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
+    pdl_wait();
     extern __shared__ unsigned char smem_raw[];
     auto& sm = *reinterpret_cast<Smem<T, kBDL && kHasZ>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) &
                                                        ~std::uintptr_t(1023));
@@ -795,7 +796,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     if (p.parts == 1) {
         const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
         if ((attr = one.prepare()) != cudaSuccess) return attr;
-        return cudaLaunchKernel(one.fn, dim3(static_cast<unsigned>(p.units)), dim3(kLanes), args, one.smem, stream);
+        return launch_pdl(one.fn, dim3(static_cast<unsigned>(p.units)), dim3(kLanes), one.smem, stream, args);
     }
     const Pick& k = loop;
     // Split launch: every CTA resident (cooperative), one wave, a fresh epoch

@@ -1,6 +1,9 @@
 // scan_common.cuh -- device helpers shared by the extended scan kernels.
 #pragma once
 
+#include <cstddef>
+#include <utility>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -23,6 +26,34 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel of the stream still runs.
+// pdl_launch_dependents lets the next kernel start its own set-up once every
+// block of this grid has called it (or exited); pdl_wait returns when the
+// previous grid has completed and its writes are visible.  Every kernel calls
+// both before it reads anything another kernel wrote.  Without the launch
+// attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Typed form of launch_pdl (internal.h) for kernels launched with their
+// arguments: programmatic stream serialization on this launch.
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl_k(void (*kernel)(P...), dim3 grid, dim3 block, std::size_t smem, cudaStream_t stream,
+                                A&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
 
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32).
 __device__ __forceinline__ float fast_exp2(float x) {

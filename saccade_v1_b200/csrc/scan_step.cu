@@ -51,6 +51,7 @@ struct StepShape {
 
 template <typename T, int N, bool kPrecise>
 __global__ void __launch_bounds__(kThreads) step_kernel(StepParams p) {
+    pdl_wait();
     using S = StepShape<N>;
     const unsigned long long gid = static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x;
     const unsigned long long lane = gid / S::kSub;
@@ -151,6 +152,7 @@ __device__ __forceinline__ void unpack8(uint4 v, float* f) {
 // blockIdx.x is the sequence and blockIdx.y the channel block: no division.
 template <typename T>
 __global__ void __launch_bounds__(kLanes) step16_kernel(StepParams p) {
+    pdl_wait();
     constexpr int N = 16;
     const unsigned d = blockIdx.y * kLanes + threadIdx.x;
     const unsigned long long seq = blockIdx.x;
@@ -312,6 +314,7 @@ __device__ __forceinline__ void pipe_issue(PipeSmem<T>& sm, int s, const CUtenso
 // wait that runs out sets g_step_fault and the CTA leaves.
 template <typename T>
 __global__ void __launch_bounds__(kPipeLanes) step16_pipe_kernel(const __grid_constant__ CUtensorMap tm_state, StepParams p) {
+    pdl_wait();
     constexpr int N = 16;
     extern __shared__ unsigned char smem_raw[];
     auto& sm = *reinterpret_cast<PipeSmem<T>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
@@ -505,21 +508,21 @@ cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream) {
         void* pargs[] = {&tm, &p};
         const void* fn = bf ? reinterpret_cast<const void*>(step16_pipe_kernel<__nv_bfloat16>)
                             : reinterpret_cast<const void*>(step16_pipe_kernel<__half>);
-        return cudaLaunchKernel(fn, dim3(static_cast<unsigned>(gx), cblocks), dim3(kPipeLanes), pargs,
-                                bf ? pipe_smem_bytes<__nv_bfloat16>() : pipe_smem_bytes<__half>(), stream);
+        return launch_pdl(fn, dim3(static_cast<unsigned>(gx), cblocks), dim3(kPipeLanes),
+                          bf ? pipe_smem_bytes<__nv_bfloat16>() : pipe_smem_bytes<__half>(), stream, pargs);
     }
     if (step16_eligible(a)) {
         if (threads == 0) return cudaSuccess;
         const dim3 grid(static_cast<unsigned>(a.nseq), static_cast<unsigned>((a.channels + kLanes - 1) / kLanes));
         const void* fn = a.dtype == SACC_DTYPE_BF16 ? reinterpret_cast<const void*>(step16_kernel<__nv_bfloat16>)
                                                     : reinterpret_cast<const void*>(step16_kernel<__half>);
-        return cudaLaunchKernel(fn, grid, dim3(kLanes), args, 0, stream);
+        return launch_pdl(fn, grid, dim3(kLanes), 0, stream, args);
     }
     const unsigned long long blocks = (threads + kThreads - 1) / kThreads;
     if (blocks == 0) return cudaSuccess;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
-    return cudaLaunchKernel(pick_step(a.dtype, static_cast<unsigned>(a.state)), dim3(static_cast<unsigned>(blocks)),
-                            dim3(kThreads), args, 0, stream);
+    return launch_pdl(pick_step(a.dtype, static_cast<unsigned>(a.state)), dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
+                      stream, args);
 }
 
 cudaError_t read_step_fault(unsigned* out, bool clear) {

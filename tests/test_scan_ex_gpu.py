@@ -356,3 +356,34 @@ def test_bulk_split_launch_bitwise_equals_unsplit(layout):
     assert torch.equal(y.view(torch.int16), torch.cat(ys).view(torch.int16))
     assert torch.equal(hf.view(torch.int32), torch.cat(hs).view(torch.int32))
     assert ctypes_fault() == 0
+
+
+def test_bulk_split_launch_in_cuda_graph():
+    """The split launch (cooperative, one wave) captured in a CUDA graph and
+    replayed twice gives the eager launch's bits."""
+    B, L, D, N = 64, 512, 1536, 16
+    s = torch.cuda.Stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(71)
+    bf = torch.bfloat16
+    with torch.cuda.stream(s):
+        u = torch.randn(B, D, L, device="cuda", generator=g).to(bf)
+        dl = torch.randn(B, D, L, device="cuda", generator=g).to(bf)
+        bm = torch.randn(B, 1, N, L, device="cuda", generator=g).to(bf)
+        cm = torch.randn(B, 1, N, L, device="cuda", generator=g).to(bf)
+        A = -(torch.rand(D, N, device="cuda", generator=g) * 4 + 0.1)
+        Dv = torch.randn(D, device="cuda", generator=g)
+        bias = torch.full((D,), -3.0, device="cuda")
+        ref = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, delta_bias=bias, layout="BDL", stream=s)
+        out = torch.zeros_like(ref)
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, delta_bias=bias, layout="BDL", out=out, stream=s)
+    for _ in range(2):
+        out.zero_()
+        with torch.cuda.stream(s):
+            graph.replay()
+        s.synchronize()
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    assert ctypes_fault() == 0

@@ -469,7 +469,8 @@ def hr_deploy(torch, device, stream, peak):
 def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
     """Other rows of the hot path, device-timed on this GPU (not part of `value`); `only` runs one of them."""
     runs = {"c3_step": c3_step, "c3_rescan": c3_rescan, "hr_deploy_f32_us": hr_deploy,
-            "c1_block": lambda *a: c1_block(*a[:3]), "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m),
+            "c1_block": lambda *a: c1_block(*a[:3]), "hr_head_block": lambda *a: hr_head_block(*a[:3]),
+            "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m),
             "c4_stack": lambda *a: c4_stack(*a[:3])}
     out = {}
     for name, fn in runs.items():
@@ -601,6 +602,47 @@ def c1_block(torch, device, stream):
             "workload": "256 tracks x 32 frames, d_model 128, D 256, N 16, dt_rank 8, fp16, RMSNorm + residual"}
 
 
+def hr_head_block(torch, device, stream):
+    """The reference head's Mamba block at its three HR deploy levels (4 Cross-Scan directions x L = 960 / 240 /
+    60 tokens, d_model 128, d_inner 256, N 16, dt_rank 16, rank-1 C, A shared by the channels, no RMSNorm,
+    residual; fp16), one forward per level replayed from one CUDA graph."""
+    import saccade_v1_b200 as sb
+    dm, D1, N1, R1 = 128, 256, 16, 16
+    p = synthetic_block(21, dm, D1, N1, R1)
+    r = np.random.default_rng(22)
+    p["w_x"] = p["w_x"][:R1 + N1 + 1]  # x_proj 256 -> 16 + 16 + 1
+    p["A"] = np.tile(-np.exp(r.uniform(-1, 1.5, (1, N1))).astype(np.float32), (D1, 1))
+    del p["norm_w"]
+    with torch.cuda.stream(stream):
+        dev = {k: (torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device=device, dtype=torch.float16)
+                   if k in ("w_in", "w_x", "w_dt", "w_out") else torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device))
+               for k, v in p.items()}
+        levels = []
+        for L_ in (960, 240, 60):
+            x = (torch.randn(4, L_, dm, device=device) * 0.5).to(torch.float16)
+            y = torch.empty_like(x)
+            ws = torch.empty(sb.mamba_block_workspace(x, dev) + 256, dtype=torch.uint8, device=device)
+            levels.append((L_, x, y, ws))
+        fwd = lambda lv: sb.mamba_block_forward(lv[1], dev, out=lv[2], workspace=lv[3], stream=stream)
+        for lv in levels:
+            fwd(lv)
+    stream.synchronize()
+    out = {f"L{lv[0]}_us_eager": round(time_device(torch, stream, lambda lv=lv: fwd(lv), 50), 2) for lv in levels}
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for lv in levels:
+            fwd(lv)
+
+    def replay():
+        with torch.cuda.stream(stream):
+            g.replay()
+
+    out["three_levels_us_graph"] = round(time_device(torch, stream, replay, 200), 2)
+    out["workload"] = ("reference head block x 3 HR levels: (4, L, 128) fp16, d_inner 256, N 16, dt_rank 16, "
+                       "rank-1 C, shared A, residual, no RMSNorm")
+    return out
+
+
 def gemm_probe(torch, device, stream, m=64 * 4096):
     """The tcgen05 projection GEMM at the config-4 in_proj shape of one 8-GPU shard (bf16 in, bf16 out;
     m = 64 tracks x 4096 tokens, n = 2 x d_inner, k = d_model)."""
@@ -706,7 +748,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 stack (52 GB on one GPU)")
-    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "gemm", "c4_stack"],
+    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "hr_head_block", "gemm",
+                                       "c4_stack"],
                     help="run one secondary measurement alone on cuda:0 and print it (for profiling)")
     ap.add_argument("--gemm-m", type=int, default=64 * 4096, help="rows of the GEMM probe (smaller only for profiling)")
     args = ap.parse_args()

@@ -218,11 +218,13 @@ int sacc_gemm(const SaccGemmArgs* args, cudaStream_t stream);
  *   [dt, B, C] = u W_x^T; delta = dt W_dt^T; y = scan(u, delta + dt_bias, A, B, C, D) * silu(z);
  *   out = y W_out^T (+ x when residual).
  * Activations and projection weights bf16 or fp16 (dtype); x, out
- * (batch, length, d_model); w_in (2 d_inner, d_model); w_x (dt_rank + 2 d_state,
- * d_inner); w_dt (d_inner, dt_rank); w_out (d_model, d_inner).  FP32: norm_w
+ * (batch, length, d_model); w_in (2 d_inner, d_model); w_x (dt_rank + d_state +
+ * c_width, d_inner) with c_width = d_state (also written 0) or 1 (one C per token
+ * broadcast over the states, as in the reference head's x_proj 256 -> 16 + 16 + 1);
+ * w_dt (d_inner, dt_rank); w_out (d_model, d_inner).  FP32: norm_w
  * (d_model, optional), conv_w (d_inner, d_conv), conv_b, dt_bias, d (d_inner),
  * a (d_inner, d_state) = -exp(A_log).  d_conv must be 4, d_state 16, d_inner
- * and d_model multiples of 128, length a multiple of 8, dt_rank a multiple of 8.
+ * and d_model multiples of 128, dt_rank a multiple of 8.
  * Intermediates go to `workspace` (at least sacc_mamba_block_workspace bytes,
  * 256-byte aligned); the call allocates nothing.
  * ------------------------------------------------------------------------ */
@@ -239,6 +241,7 @@ typedef struct SaccMambaBlockArgs {
     const float *dt_bias, *a, *d;
     const void* w_out;
     void* out;
+    int32_t c_width; /* C per token: 0 or d_state (full), or 1 */
 } SaccMambaBlockArgs;
 
 int sacc_mamba_block_workspace(const SaccMambaBlockArgs* args, size_t* bytes);

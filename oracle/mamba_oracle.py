@@ -44,13 +44,14 @@ def block_forward(x, p, dt: str, eps: float = 1e-5, residual: bool = True) -> np
         shift = K - 1 - k
         conv[:, shift:, :] += w[:, k] * xin[:, : L - shift, :]
     u = rnd(conv / (1.0 + np.exp(-conv)), dt)
+    cw = p["w_x"].shape[0] - R - N                          # C width: N, or 1 (one C per token, the reference head)
     dbc = u @ f("w_x").T                                    # x_proj
-    dtl, bm, cm = rnd(dbc[..., :R], dt), rnd(dbc[..., R:R + N], dt), rnd(dbc[..., R + N:R + 2 * N], dt)
+    dtl, bm, cm = rnd(dbc[..., :R], dt), rnd(dbc[..., R:R + N], dt), rnd(dbc[..., R + N:R + N + cw], dt)
     delta = rnd(dtl @ f("w_dt").T, dt)                      # dt_proj (bias added in the scan)
     y, _ = oracle.scan_ex(u.astype(np.float32), delta.astype(np.float32), np.asarray(p["A"], np.float32),
                           bm[:, :, None, :].astype(np.float32), cm[:, :, None, :].astype(np.float32), layout="BLD",
                           d=np.asarray(p["D"], np.float32), z=z.astype(np.float32),
-                          delta_bias=np.asarray(p["dt_bias"], np.float32))
+                          delta_bias=np.asarray(p["dt_bias"], np.float32), c_width=cw)
     y = rnd(y, dt)
     out = y @ f("w_out").T
     if residual:
@@ -59,7 +60,7 @@ def block_forward(x, p, dt: str, eps: float = 1e-5, residual: bool = True) -> np
 
 
 def random_block(seed: int, d_model: int, d_inner: int, d_state: int, dt_rank: int, d_conv: int, dt: str,
-                 norm: bool = True):
+                 norm: bool = True, c_width: int | None = None):
     """Synthetic block weights: uniform +-1/sqrt(fan_in) (as the reference's synthetic head weights,
     include/saccade/head_reference.hpp:125-127), A = -(1..N), D = 1, dt_bias = softplus^-1(logU[1e-3, 1e-1])."""
     r = np.random.default_rng(seed)
@@ -68,7 +69,7 @@ def random_block(seed: int, d_model: int, d_inner: int, d_state: int, dt_rank: i
         "w_in": rnd(u((2 * d_inner, d_model), d_model), dt),
         "conv_w": u((d_inner, d_conv), d_conv).astype(np.float32),
         "conv_b": u((d_inner,), d_conv).astype(np.float32),
-        "w_x": rnd(u((dt_rank + 2 * d_state, d_inner), d_inner), dt),
+        "w_x": rnd(u((dt_rank + d_state + (d_state if c_width is None else c_width), d_inner), d_inner), dt),
         "w_dt": rnd(u((d_inner, dt_rank), dt_rank), dt),
         "dt_bias": np.log(np.expm1(np.exp(r.uniform(np.log(1e-3), np.log(1e-1), d_inner)))).astype(np.float32),
         "A": -np.tile(np.arange(1, d_state + 1, dtype=np.float32), (d_inner, 1)),

@@ -81,7 +81,7 @@ class MambaBlockArgs(ctypes.Structure):
     _fields_ = [(k, ctypes.c_uint64) for k in ("batch", "length", "d_model", "d_inner", "d_state", "d_conv", "dt_rank")] + [
         ("dtype", ctypes.c_int32), ("residual", ctypes.c_int32), ("eps", ctypes.c_float)] + [
         (k, ctypes.c_void_p) for k in ("x", "norm_w", "w_in", "conv_w", "conv_b", "w_x", "w_dt", "dt_bias", "a", "d",
-                                       "w_out", "out")]
+                                       "w_out", "out")] + [("c_width", ctypes.c_int32)]
 
 
 _lib = None

@@ -217,6 +217,19 @@ __global__ void __launch_bounds__(kConvCh) conv4_silu_tile_kernel(const __grid_c
     }
 }
 
+// dst = src (rows x cols, 16-bit) followed by copies - 1 more copies of its
+// last row: the block's W_x for a rank-1 C.
+__global__ void __launch_bounds__(256) repeat_last_row_kernel(const std::uint16_t* __restrict__ src, unsigned long long rows,
+                                                              unsigned long long copies, unsigned long long cols,
+                                                              std::uint16_t* __restrict__ dst) {
+    pdl_wait();
+    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
+    const unsigned long long out_rows = rows - 1 + copies;
+    if (i >= out_rows * cols) return;
+    const unsigned long long r = i / cols, c = i % cols;
+    dst[i] = src[(r < rows ? r : rows - 1) * cols + c];
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 conv_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -237,6 +250,15 @@ cudaError_t read_block_fault(unsigned* out, bool clear) {
     if (e != cudaSuccess || !clear) return e;
     const unsigned zero = 0;
     return cudaMemcpyToSymbol(g_block_fault, &zero, sizeof(unsigned));
+}
+
+cudaError_t launch_repeat_last_row(int dtype, const void* src, unsigned long long rows, unsigned long long copies,
+                                   unsigned long long cols, void* dst, cudaStream_t stream) {
+    (void)dtype; // a bit copy of 16-bit elements
+    const unsigned long long blocks = ((rows - 1 + copies) * cols + 255) / 256;
+    if (rows == 0 || copies == 0 || blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    return launch_pdl_k(repeat_last_row_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                        static_cast<const std::uint16_t*>(src), rows, copies, cols, static_cast<std::uint16_t*>(dst));
 }
 
 cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
@@ -319,13 +341,14 @@ cudaError_t load_block_kernels(std::string& report) {
                         reinterpret_cast<const void*>(conv4_silu_rows_kernel<__nv_bfloat16>),
                         reinterpret_cast<const void*>(conv4_silu_rows_kernel<__half>),
                         reinterpret_cast<const void*>(conv4_silu_tile_kernel<__nv_bfloat16>),
-                        reinterpret_cast<const void*>(conv4_silu_tile_kernel<__half>)};
+                        reinterpret_cast<const void*>(conv4_silu_tile_kernel<__half>),
+                        reinterpret_cast<const void*>(repeat_last_row_kernel)};
     for (const void* k : ks) {
         cudaFuncAttributes attr{};
         const cudaError_t e = cudaFuncGetAttributes(&attr, k);
         if (e != cudaSuccess) return e;
     }
-    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu) x10\n";
+    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu, repeat_last_row) x11\n";
     return cudaSuccess;
 }
 

@@ -396,8 +396,9 @@ static void check_block_shape(const char* api, const SaccMambaBlockArgs& a) {
     if (a.d_state != 16) reject(api, "d_state must be 16");
     if (a.d_inner == 0 || a.d_inner % 128 != 0 || a.d_model == 0 || a.d_model % 128 != 0)
         reject(api, "d_inner and d_model must be positive multiples of 128");
-    if (a.length % 8 != 0) reject(api, "length must be a multiple of 8");
     if (a.dt_rank == 0 || a.dt_rank % 8 != 0) reject(api, "dt_rank must be a positive multiple of 8");
+    if (a.c_width != 0 && a.c_width != 1 && static_cast<std::uint64_t>(a.c_width) != a.d_state)
+        reject(api, "c_width must be 1 or d_state");
     if (!(a.eps > 0.0f) && a.norm_w) reject(api, "eps must be positive");
     const std::uint64_t M = a.batch * a.length;
     if (M > 0x7fffffffull) reject(api, "batch * length exceeds int32");
@@ -409,7 +410,7 @@ static void check_block(const char* api, const SaccMambaBlockArgs& a) {
     const std::uint64_t M = a.batch * a.length;
     const std::uint64_t D = a.d_inner, dm = a.d_model, R = a.dt_rank, N = a.d_state;
     for (const Region& r : {Region{a.x, M * dm * 2, "x"}, Region{a.w_in, 2 * D * dm * 2, "w_in"},
-                            Region{a.w_x, (R + 2 * N) * D * 2, "w_x"}, Region{a.w_dt, D * R * 2, "w_dt"},
+                            Region{a.w_x, (R + N + (a.c_width == 1 ? 1 : N)) * D * 2, "w_x"}, Region{a.w_dt, D * R * 2, "w_dt"},
                             Region{a.w_out, dm * D * 2, "w_out"}, Region{a.out, M * dm * 2, "out"}})
         require_pointer(api, r, 16);
     for (const Region& r : {Region{a.conv_w, D * 4 * 4, "conv_w"}, Region{a.a, D * N * 4, "A"}})

@@ -86,6 +86,9 @@ cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, un
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
                              unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
                              cudaStream_t stream);
+// dst = src (rows x cols) with its last row repeated `copies` times in total.
+cudaError_t launch_repeat_last_row(int dtype, const void* src, unsigned long long rows, unsigned long long copies,
+                                   unsigned long long cols, void* dst, cudaStream_t stream);
 cudaError_t load_block_kernels(std::string& report);
 cudaError_t read_block_fault(unsigned* out, bool clear);
 std::size_t mamba_block_workspace(const SaccMambaBlockArgs& a);

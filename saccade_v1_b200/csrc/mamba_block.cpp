@@ -27,7 +27,7 @@ namespace sacc {
 namespace {
 
 struct Layout {
-    std::size_t r, wn, xz, u, dbc, delta, y, total;
+    std::size_t r, wn, wx, xz, u, dbc, delta, y, total;
 };
 
 std::size_t align256(std::size_t v) { return (v + 255) & ~std::size_t(255); }
@@ -44,6 +44,7 @@ Layout plan(const SaccMambaBlockArgs& a) {
     };
     l.r = take(M * sizeof(float));
     l.wn = take(2 * D * dm * e);
+    l.wx = a.c_width == 1 ? take((R + 2 * N) * D * e) : 0; // W_x with its C row repeated d_state times
     l.xz = take(M * 2 * D * e);
     l.u = take(M * D * e);
     l.dbc = take(M * (R + 2 * N) * e);
@@ -98,8 +99,17 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
                                 stream)) != cudaSuccess)
         return err;
 
-    // x_proj in one GEMM: dt (R), B (N), C (N) as column slices of dbc.
-    if ((err = launch_gemm(gemm_args(dt_, M, W, D, u, D, a.w_x, D, dbc, W), stream)) != cudaSuccess) return err;
+    // x_proj in one GEMM: dt (R), B (N), C (N) as column slices of dbc.  A
+    // rank-1 C (one value per token) runs as a full C whose N columns are
+    // that value: W_x's C row is repeated N times, so every C column is the
+    // same dot product and the scan's sum over C_n h_n is the rank-1 result.
+    const void* w_x = a.w_x;
+    if (a.c_width == 1) {
+        void* wx = ws + l.wx;
+        if ((err = launch_repeat_last_row(dt_, a.w_x, R + N + 1, N, D, wx, stream)) != cudaSuccess) return err;
+        w_x = wx;
+    }
+    if ((err = launch_gemm(gemm_args(dt_, M, W, D, u, D, w_x, D, dbc, W), stream)) != cudaSuccess) return err;
     // dt_proj on the dt columns (bias added inside the scan, before softplus).
     if ((err = launch_gemm(gemm_args(dt_, M, D, R, dbc, W, a.w_dt, R, delta, D), stream)) != cudaSuccess) return err;
 

@@ -683,8 +683,8 @@ unsigned long long resident_ctas(const Pick& k) {
 // part), if that is at least 15 % below the unsplit ceil(units / wave) (the
 // hand-offs and per-part pipeline starts cost a few percent; a 12.5 % gain
 // measured as a loss at config 4).
-int split_parts(unsigned long long units, unsigned long long wave, int nchunks) {
-    if (units <= wave || wave == 0) return 1;
+int split_parts(unsigned long long units, unsigned long long wave, int nchunks, unsigned long long length) {
+    if (units <= wave || wave == 0 || length % 8 != 0) return 1; // L % 8: every part keeps >= 40 tokens
     const double unsplit = static_cast<double>((units + wave - 1) / wave);
     double best = 0.85 * unsplit;
     int parts = 1;
@@ -714,10 +714,11 @@ unsigned long long next_epoch() {
 
 } // namespace
 
-// The bulk kernel's domain: 16-bit activations, N = 16, no varlen, channels
-// in 128-wide tiles inside one group, 16-byte aligned tensors and 16-byte row
-// strides for the TMA ((B, D, L): L % 8 == 0; (B, L, D): a full-width C, whose
-// rows are then 16 * groups * 2 bytes).  Other calls use the general kernel.
+// The bulk kernel's domain: 16-bit activations, N = 16, channels in 128-wide
+// tiles inside one group, 16-byte aligned tensors and 16-byte row strides for
+// the TMA ((B, D, L): L % 8 == 0; (B, L, D): a full-width C, whose rows are
+// then 16 * groups * 2 bytes, any L, packed varlen sequences too).  Other
+// calls use the general kernel.
 bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
     if (rs) {
         // Strided z / B / C rows (the block's fused projection outputs): dense
@@ -738,7 +739,9 @@ bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
     } else if (a.layout == SACC_LAYOUT_BDL) {
         if (a.length % 8 != 0) return false;
     } else if (a.layout == SACC_LAYOUT_BLD) {
-        if (a.c_width != kN || a.length % 8 != 0 || a.channels % 8 != 0) return false;
+        // Any length: the 3D maps stop at L (tokens past it read zero and are
+        // kept out of the state; the y store stops at L).
+        if (a.c_width != kN || a.channels % 8 != 0) return false;
     } else {
         return false;
     }
@@ -792,7 +795,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     // Packed varlen sequences (one CTA per sequence x 128 channels: persistent
     // CTAs were slower, each sequence's start waiting on its h0 row) and
     // launches that fit one wave or gain nothing from a split: one item per CTA.
-    p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks);
+    p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks, L);
     if (p.parts == 1) {
         const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
         if ((attr = one.prepare()) != cudaSuccess) return attr;

@@ -235,10 +235,11 @@ def _block_args(x, p, eps, residual, out):
         t = p.get(k)
         if t is not None and not t.is_contiguous():
             raise ScanInvalidArgument(f"mamba_block: {k} must be contiguous")
+    c_width = p["w_x"].shape[0] - dt_rank - d_state  # d_state, or 1 (rank-1 C)
     return _lib.MambaBlockArgs(batch, length, d_model, d_inner, d_state, d_conv, dt_rank, _DTYPES[x.dtype], int(residual),
                                float(eps), _ptr(x), _ptr(p.get("norm_w")), _ptr(p["w_in"]), _ptr(p["conv_w"]),
                                _ptr(p.get("conv_b")), _ptr(p["w_x"]), _ptr(p["w_dt"]), _ptr(p.get("dt_bias")),
-                               _ptr(p["A"]), _ptr(p.get("D")), _ptr(p["w_out"]), _ptr(out))
+                               _ptr(p["A"]), _ptr(p.get("D")), _ptr(p["w_out"]), _ptr(out), c_width)
 
 
 def mamba_block_workspace(x, params, eps=1e-5, residual=True) -> int:

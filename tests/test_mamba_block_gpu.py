@@ -81,8 +81,6 @@ def test_block_rejections():
     p = to_dev(mo.random_block(1, 128, 256, 16, 8, 4, "f16"), "f16")
     with pytest.raises(sb.ScanInvalidArgument, match="non-default stream"):
         sb.mamba_block_forward(x, p, stream=0)
-    with pytest.raises(sb.ScanInvalidArgument, match="length must be a multiple of 8"):
-        sb.mamba_block_forward(torch.zeros(2, 6, 128, dtype=torch.float16, device="cuda"), p, stream=torch.cuda.Stream())
     bad = dict(p, conv_w=torch.zeros(256, 3, device="cuda"))
     with pytest.raises(sb.ScanInvalidArgument, match="d_conv must be 4"):
         sb.mamba_block_forward(x, bad, stream=torch.cuda.Stream())
@@ -97,4 +95,33 @@ def test_config4_layer_sampled_tracks():
     got = run_block(x, p, "bf16")
     pick = [1, 6]
     check("config4_tracks", got[pick], mo.block_forward(x[pick], p, "bf16"))
+    assert sb.scan_fault() == 0
+
+
+@pytest.mark.parametrize("L", [240, 64])
+def test_block_rank1_c_reference_head_shapes(L):
+    """The reference head's Mamba block (src/head_trt_network.cpp:192-230): 4 Cross-Scan directions x L tokens,
+    d_model 128, d_inner 256, N 16, dt_rank 16, x_proj 256 -> 16 + 16 + 1 (one C per token), A shared by all
+    channels (A_log of shape (1, 16)), no RMSNorm, residual; fp16 activations."""
+    B, dm, D, N, R = 4, 128, 256, 16, 16
+    p = mo.random_block(14, dm, D, N, R, 4, "f16", norm=False, c_width=1)
+    p["A"] = np.tile(-np.exp(np.random.default_rng(15).uniform(-1, 1.5, (1, N))).astype(np.float32), (D, 1))
+    x = mo.rnd(np.random.default_rng(16).standard_normal((B, L, dm)) * 0.5, "f16")
+    check(f"head_rank1_L{L}", run_block(x, p, "f16"), mo.block_forward(x, p, "f16"))
+    assert sb.scan_fault() == 0
+
+
+def test_block_rejects_other_c_widths():
+    p = to_dev(mo.random_block(1, 128, 256, 16, 8, 4, "f16", c_width=2), "f16")
+    x = torch.zeros(2, 8, 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(sb.ScanInvalidArgument, match="c_width must be 1 or d_state"):
+        sb.mamba_block_forward(x, p, stream=torch.cuda.Stream())
+
+
+@pytest.mark.parametrize("L", [6, 37, 60])
+def test_block_lengths_not_multiple_of_8(L):
+    B, dm, D, N, R = 3, 128, 256, 16, 8
+    p = mo.random_block(17, dm, D, N, R, 4, "bf16")
+    x = mo.rnd(np.random.default_rng(18).standard_normal((B, L, dm)) * 0.1, "bf16")
+    check(f"block_L{L}", run_block(x, p, "bf16"), mo.block_forward(x, p, "bf16"))
     assert sb.scan_fault() == 0

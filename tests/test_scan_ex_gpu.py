@@ -196,7 +196,7 @@ def test_rejections():
 
 # ---------------------------------------------------------------- bulk path
 # Shapes inside the bulk kernel's domain: 16-bit (B, D, L), N = 16,
-# D a multiple of 128 (per group), L a multiple of 8.
+# D a multiple of 128 (per group); (B, D, L) needs L a multiple of 8, (B, L, D) any L.
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("layout", ["BDL", "BLD"])
@@ -205,6 +205,7 @@ def test_rejections():
     dict(B=2, L=200, D=128, G=1, c_full=True, use=("D", "bias")),        # partial last chunk
     dict(B=2, L=64, D=256, G=2, c_full=False, use=("D", "z", "bias")),   # groups, rank-1 C
     dict(B=3, L=40, D=384, G=1, c_full=True, use=()),                    # no bias / D / gate
+    dict(B=2, L=37, D=256, G=1, c_full=True, use=("D", "z", "bias")),   # (B, L, D): any length
 ])
 def test_bulk_path_matches_oracle(dt, layout, case):
     t = make(21, case["B"], case["L"], case["D"], 16, case["G"], layout, dt, c_full=case["c_full"])

@@ -98,7 +98,9 @@ struct BulkParams {
     unsigned long long epoch;    // this launch's hand-off flag value (split launches)
     unsigned groups;
     int a_shared, c_full, has_d, softplus, nchunks;
-    int parts;                   // chunk ranges per unit (> 1: split launch, cooperative)
+    int parts;                   // chunk ranges per unit (> 1: split launch, cooperative, or chunk-parallel phases)
+    int phase;                   // 0 one pass; chunk-parallel: 1 local pass (parts from zero), 2 final pass
+    unsigned long long item0;    // first item of this launch (the final pass starts at part 1)
 };
 
 
@@ -220,10 +222,13 @@ __device__ __forceinline__ void issue_chunk(Smem<T, kBDL && kHasZ>& sm, int s, i
 
 // Eight tokens of one lane through the recurrence; with kGuard only the first
 // `count` (fewer in a sequence's last, partial block; the others are left out
-// of the state).
-template <bool kFullC, bool kHasZ, bool kGuard>
+// of the state).  With kSum the block's Deltas are added to `dtsum` (the
+// chunk-parallel local pass needs them; the split launch's variant, issue
+// bound, leaves the add out).
+template <bool kFullC, bool kHasZ, bool kGuard, bool kSum>
 __device__ __forceinline__ void scan_block8(const float (*bc)[2 * kN], int q, int count, const Block8& blk, const float (&a)[kN],
-                                            float (&h)[kN], float bias, float dskip, int softplus, float (&out)[8]) {
+                                            float (&h)[kN], float bias, float dskip, int softplus, float (&out)[8],
+                                            float& dtsum) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         out[j] = 0.0f;
@@ -231,6 +236,7 @@ __device__ __forceinline__ void scan_block8(const float (*bc)[2 * kN], int q, in
         const int t = q * 8 + j;
         const float xv = blk.x[j] + bias;
         const float dt = softplus ? softplus_poly(xv) : xv;
+        if constexpr (kSum) dtsum += dt;
         const float du = dt * blk.u[j];
         const float4* bcv = reinterpret_cast<const float4*>(bc[t]);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -319,15 +325,17 @@ __device__ __forceinline__ T* stash_at(const BulkParams& p, const Item& w, unsig
     return kBDL ? y + (w.b * p.channels + d) * p.length + tp : y + (w.b * p.length + tp) * p.channels + d;
 }
 
+// 16 states (and, for the chunk-parallel local pass, a 17th value: the
+// part's sum of Delta) at tokens tp .. tp + 33 of the lane's outputs.
 template <typename T, bool kBDL>
-__device__ __forceinline__ void stash_store(const BulkParams& p, const Item& w, unsigned long long d, const float (&h)[kN]) {
-    T* at = stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c1) * kT);
+__device__ __forceinline__ void stash_put(const BulkParams& p, T* at, const float (&h)[kN], const float* extra) {
     if (kBDL) {
         uint4* q = reinterpret_cast<uint4*>(at);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
             q[k] = make_uint4(__float_as_uint(h[4 * k]), __float_as_uint(h[4 * k + 1]), __float_as_uint(h[4 * k + 2]),
                               __float_as_uint(h[4 * k + 3]));
+        if (extra) *reinterpret_cast<float*>(at + 2 * kN) = *extra;
     } else {
         std::uint16_t* q = reinterpret_cast<std::uint16_t*>(at);
 #pragma unroll
@@ -336,7 +344,33 @@ __device__ __forceinline__ void stash_store(const BulkParams& p, const Item& w, 
             q[(2 * k) * p.channels] = static_cast<std::uint16_t>(v & 0xffffu);
             q[(2 * k + 1) * p.channels] = static_cast<std::uint16_t>(v >> 16);
         }
+        if (extra) {
+            const std::uint32_t v = __float_as_uint(*extra);
+            q[(2 * kN) * p.channels] = static_cast<std::uint16_t>(v & 0xffffu);
+            q[(2 * kN + 1) * p.channels] = static_cast<std::uint16_t>(v >> 16);
+        }
     }
+}
+
+template <typename T, bool kBDL>
+__device__ __forceinline__ void stash_store(const BulkParams& p, const Item& w, unsigned long long d, const float (&h)[kN]) {
+    stash_put<T, kBDL>(p, stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c1) * kT), h, nullptr);
+}
+
+template <typename T, bool kBDL>
+__device__ __forceinline__ void stash_store(const BulkParams& p, const Item& w, unsigned long long d, const float (&h)[kN],
+                                            float extra) {
+    stash_put<T, kBDL>(p, stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c1) * kT), h, &extra);
+}
+
+// The 17th stashed value (sum of Delta) at the start of `w`'s part.
+template <typename T, bool kBDL>
+__device__ __forceinline__ float stash_extra(const BulkParams& p, const Item& w, unsigned long long d) {
+    const T* at = stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c0) * kT);
+    if (kBDL) return __ldcg(reinterpret_cast<const float*>(at + 2 * kN));
+    const unsigned short* q = reinterpret_cast<const unsigned short*>(at);
+    const std::uint32_t lo = __ldcg(q + (2 * kN) * p.channels), hi = __ldcg(q + (2 * kN + 1) * p.channels);
+    return __uint_as_float(lo | (hi << 16));
 }
 
 template <typename T, bool kBDL>
@@ -412,7 +446,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         // First kStages loads of this CTA's (item, chunk) list.
         Cursor& c = sm.next;
         c.more = 1;
-        c.it = blockIdx.x;
+        c.it = blockIdx.x + p.item0;
         if (c.it >= items) {
             c.more = 0;
         } else {
@@ -430,8 +464,9 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
 
     bool fault = false;
     int gc = 0; // chunks this CTA has consumed: stage gc % kStages, its (gc / kStages)-th use
-    const unsigned long long it_end = kLoop ? items : blockIdx.x + 1ull;
-    for (unsigned long long it = blockIdx.x; it < it_end && (!kLoop || !fault); it += kLoop ? gridDim.x : 1u) {
+    const unsigned long long first = blockIdx.x + p.item0;
+    const unsigned long long it_end = kLoop ? items : first + 1ull;
+    for (unsigned long long it = first; it < it_end && (!kLoop || !fault); it += kLoop ? gridDim.x : 1u) {
         const Item w = item_at<kBDL, kFullC>(p, it);
         const unsigned long long d = w.d0 + tid, lane = w.b * D + d;
         // Per-lane constants: A * log2(e), D, dt bias; the state from h0 (or
@@ -442,9 +477,15 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         for (int n = 0; n < kN; ++n) a[n] = arow[n] * kLog2e;
         const float dskip = p.has_d ? p.d[d] : 0.0f;
         const float bias = p.bias ? p.bias[d] : 0.0f;
+        float dtsum = 0.0f; // sum of Delta over the part (chunk-parallel local pass)
         if (w.part == 0) {
 #pragma unroll
             for (int n = 0; n < kN; ++n) h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
+        } else if (p.phase == 1) {
+#pragma unroll
+            for (int n = 0; n < kN; ++n) h[n] = 0.0f; // local pass: from zero, corrected by the final pass
+        } else if (p.phase == 2) {
+            stash_load<T, kBDL>(p, w, d, h); // the part's true initial state, from the combine
         } else {
             bool ready = true;
             if (tid == 0) {
@@ -511,22 +552,23 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                                                  static_cast<unsigned long long>(chunk) * kT,
                                              p.zld, d, tid, q, valid - q * 8, blk);
                 float out[8];
-                scan_block8<kFullC, kHasZ, true>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out);
+                scan_block8<kFullC, kHasZ, true, !kLoop>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out, dtsum);
                 if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
                 else store_block_bld<T>(sm.y, tid, q, out);
             }
             fence_async_shared();
             __syncthreads();
             const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
+            const bool write_y = !(p.phase == 1 && w.part > 0); // local-pass outputs are not final
             const bool tail = !kBDL && p.cu && valid < kT;
-            if (tail) {
+            if (tail && write_y) {
                 // A packed sequence's partial last chunk: a tile store would also
                 // write the next sequence's rows, so store the valid rows only.
                 T* yg = static_cast<T*>(p.y);
                 for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
             }
             if (tid == 0) {
-                if (!tail) {
+                if (!tail && write_y) {
                     if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, w.row0);
                     else tma_store_3d(&tm_y, sm.y, w.row0, tc0, w.bb);
                 }
@@ -541,13 +583,18 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             }
         }
         if (fault) break;
-        if (w.part + 1 < p.parts) {
+        if (p.phase == 1) {
+            // Local pass: the part's end state and its sum of Delta go to the
+            // next part's first outputs for the combine (the last part's are
+            // not needed).
+            if (w.part + 1 < p.parts) stash_store<T, kBDL>(p, w, d, h, dtsum);
+        } else if (p.phase == 0 && w.part + 1 < p.parts) {
             // Hand the state to the unit's next part.
             stash_store<T, kBDL>(p, w, d, h);
             __threadfence();
             __syncthreads();
             if (tid == 0) flag_release(flag_at<T, kBDL>(p, w, static_cast<unsigned long long>(w.c1) * kT), p.epoch);
-        } else if (p.h_final) {
+        } else if (p.h_final && w.part + 1 == p.parts) {
 #pragma unroll
             for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
         }
@@ -618,6 +665,39 @@ struct Variant {
     }
     static size_t smem() { return smem_bytes<T, kBDL && kHasZ>(); }
 };
+
+// Chunk-parallel combine, one thread per (batch row, channel): the local
+// pass left each part k < K - 1's end state S_k (from zero; part 0 from h0)
+// and its sum of Delta at part k + 1's first outputs.  Over the parts in
+// order the true initial state of part k is H_1 = S_0 and
+// H_k = exp(A * sum Delta_{k-1}) H_{k-1} + S_{k-1} (the recurrence is linear in
+// h and the decays of a part multiply to one exponential), written back in
+// place for the final pass.
+template <typename T, bool kBDL>
+__global__ void __launch_bounds__(256) combine_kernel(BulkParams p, unsigned long long rows) {
+    pdl_wait();
+    const unsigned long long idx = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= rows * p.channels) return;
+    const unsigned long long d = idx % p.channels;
+    Item w{};
+    w.b = idx / p.channels;
+    float a[kN], h[kN], s[kN];
+    const float* arow = p.a + (p.a_shared ? 0 : d * kN);
+#pragma unroll
+    for (int n = 0; n < kN; ++n) a[n] = arow[n] * kLog2e;
+    for (int k = 1; k < p.parts; ++k) {
+        w.c0 = k * p.nchunks / p.parts;
+        if (k == 1) {
+            stash_load<T, kBDL>(p, w, d, h); // part 0 ran from h0: already the true state
+            continue;
+        }
+        stash_load<T, kBDL>(p, w, d, s);
+        const float sum = stash_extra<T, kBDL>(p, w, d);
+#pragma unroll
+        for (int n = 0; n < kN; ++n) h[n] = fmaf(fast_exp2(sum * a[n]), h[n], s[n]);
+        stash_put<T, kBDL>(p, stash_at<T, kBDL>(p, w, d, static_cast<unsigned long long>(w.c0) * kT), h, nullptr);
+    }
+}
 
 struct Pick {
     const void* fn;
@@ -697,6 +777,19 @@ int split_parts(unsigned long long units, unsigned long long wave, int nchunks, 
         }
     }
     return parts;
+}
+
+// Parts for the chunk-parallel mode (a local pass over all parts, a combine,
+// a final pass over parts 1..K-1): for launches that leave most SMs idle
+// (units at most a quarter of the SMs), sequences of at least four chunks and
+// L % 8 == 0 (each part keeps >= 2 chunks, the stash 34 tokens).  K fills the
+// SMs with one part per SM in the local pass; 0 when the mode does not apply.
+int chunk_parts(unsigned long long units, unsigned long long sms, int nchunks, unsigned long long length) {
+    if (units == 0 || units * 4 > sms || nchunks < 4 || length % 8 != 0) return 0;
+    unsigned long long k = sms / units;
+    if (k > static_cast<unsigned long long>(nchunks / 2)) k = static_cast<unsigned long long>(nchunks / 2);
+    if (k > 32) k = 32;
+    return k >= 3 ? static_cast<int>(k) : 0; // two passes over 2/K of the sequence: below 3 parts no gain
 }
 
 // A value no earlier split launch of this process used, never zero: the
@@ -795,6 +888,31 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     // Packed varlen sequences (one CTA per sequence x 128 channels: persistent
     // CTAs were slower, each sequence's start waiting on its h0 row) and
     // launches that fit one wave or gain nothing from a split: one item per CTA.
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int chunked = p.cu ? 0 : chunk_parts(p.units, static_cast<unsigned long long>(sms), p.nchunks, L);
+    if (chunked) {
+        // Few units over long sequences: the chunk-parallel passes (stream
+        // ordered, no workspace: the hand-offs live in y like the split's).
+        const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
+        if ((attr = one.prepare()) != cudaSuccess) return attr;
+        p.parts = chunked;
+        p.phase = 1;
+        cudaError_t e = launch_pdl(one.fn, dim3(static_cast<unsigned>(p.units * chunked)), dim3(kLanes), one.smem, stream, args);
+        if (e != cudaSuccess) return e;
+        const unsigned long long threads = rows * D;
+        const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+        if (a.dtype == SACC_DTYPE_BF16)
+            e = bdl ? launch_pdl_k(combine_kernel<__nv_bfloat16, true>, dim3(blocks), dim3(256), 0, stream, p, rows)
+                    : launch_pdl_k(combine_kernel<__nv_bfloat16, false>, dim3(blocks), dim3(256), 0, stream, p, rows);
+        else
+            e = bdl ? launch_pdl_k(combine_kernel<__half, true>, dim3(blocks), dim3(256), 0, stream, p, rows)
+                    : launch_pdl_k(combine_kernel<__half, false>, dim3(blocks), dim3(256), 0, stream, p, rows);
+        if (e != cudaSuccess) return e;
+        p.phase = 2;
+        p.item0 = p.units;
+        return launch_pdl(one.fn, dim3(static_cast<unsigned>(p.units * (chunked - 1))), dim3(kLanes), one.smem, stream, args);
+    }
     p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks, L);
     if (p.parts == 1) {
         const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);

@@ -1,4 +1,5 @@
-"""ctypes binding of libsacc_scan.so (the C ABI declared in include/sacc_scan.h).
+"""ctypes binding of libsacc_scan.so (the C ABI declared in include/sacc_scan.h
+and include/sacc_frame.h).
 
 The library is built in-tree (saccade_v1_b200/libsacc_scan.so).  There is no
 fallback: if the library is missing or does not load, every entry point
@@ -32,7 +33,25 @@ EXPORTS = (
     "sacc_mamba_block_workspace",
     "sacc_mamba_block_forward",
     "sacc_mamba_block_forward_noalloc",
+    # include/sacc_frame.h
+    "sacc_scan_frame_load_kernels",
+    "sacc_scan_frame_initialize",
+    "sacc_scan_frame_begin",
+    "sacc_scan_frame_gate",
+    "sacc_scan_frame_publish",
+    "sacc_scan_frame_commit",
+    "sacc_scan_frame_packet",
+    "sacc_scan_frame_step",
+    "sacc_scan_frame_check_finite",
+    "sacc_scan_frame_delay",
+    "sacc_scan_frame_digest",
+    "sacc_model_producer_workspace_bytes",
+    "sacc_model_producer_load_kernels",
+    "sacc_model_producer_cuda",
 )
+
+FRAME_MAX_STATUSES = 16
+MODEL_PRODUCER_PLUGINS = 9
 
 
 class ScanShape(ctypes.Structure):
@@ -84,6 +103,27 @@ class MambaBlockArgs(ctypes.Structure):
                                        "w_out", "out")] + [("c_width", ctypes.c_int32)]
 
 
+class FrameControl(ctypes.Structure):
+    _fields_ = [("epoch", ctypes.c_uint64), ("current", ctypes.c_int64), ("committed", ctypes.c_int64),
+                ("fail_frame", ctypes.c_int64)] + [
+        (k, ctypes.c_uint32) for k in ("committed_slot", "working_slot", "frame_status", "fail_code", "run_stage",
+                                       "published", "scan_flags", "arrivals")] + [("digest_sum", ctypes.c_uint64)]
+
+
+class FrameRecord(ctypes.Structure):
+    _fields_ = [("flags", ctypes.c_uint32 * FRAME_MAX_STATUSES), ("done", ctypes.c_uint32 * FRAME_MAX_STATUSES),
+                ("frame_status", ctypes.c_uint32), ("published", ctypes.c_uint32), ("digest", ctypes.c_uint64)]
+
+
+class StatusList(ctypes.Structure):
+    _fields_ = [("status", ctypes.c_void_p * FRAME_MAX_STATUSES), ("count", ctypes.c_uint)]
+
+
+class RawView(ctypes.Structure):
+    _fields_ = [("cls", ctypes.c_void_p * 3), ("reg", ctypes.c_void_p * 3), ("cls_elements", ctypes.c_size_t * 3),
+                ("reg_elements", ctypes.c_size_t * 3)]
+
+
 _lib = None
 
 
@@ -123,6 +163,27 @@ def load() -> ctypes.CDLL:
     L.sacc_mamba_block_forward.restype = i
     L.sacc_mamba_block_forward_noalloc.argtypes = [ctypes.POINTER(MambaBlockArgs), vp]
     L.sacc_mamba_block_forward_noalloc.restype = i
+    i64, u64 = ctypes.c_int64, ctypes.c_uint64
+    for name, args in (
+            ("sacc_scan_frame_load_kernels", [ctypes.c_char_p, sz]),
+            ("sacc_scan_frame_initialize", [vp, u64, vp, vp]),
+            ("sacc_scan_frame_begin", [vp, u64, i64, vp]),
+            ("sacc_scan_frame_gate", [vp, ctypes.POINTER(StatusList), vp, i64, vp]),
+            ("sacc_scan_frame_publish", [vp, vp, sz, vp, vp, vp, i64, vp]),
+            ("sacc_scan_frame_commit", [vp, vp]),
+            ("sacc_scan_frame_packet", [vp, vp, vp]),
+            ("sacc_scan_frame_step", [vp, u64, i64, ctypes.POINTER(StatusList), vp, sz, vp, vp, vp, i64, vp, vp]),
+            ("sacc_scan_frame_check_finite", [vp, sz, vp, ctypes.c_uint32, vp]),
+            ("sacc_scan_frame_delay", [ctypes.c_uint, vp]),
+            ("sacc_model_producer_load_kernels", [ctypes.c_char_p, sz]),
+            ("sacc_model_producer_cuda", [vp, sz, ctypes.POINTER(RawView), ctypes.c_void_p * MODEL_PRODUCER_PLUGINS, vp,
+                                          vp, sz, vp, i])):
+        getattr(L, name).argtypes = args
+        getattr(L, name).restype = i
+    L.sacc_scan_frame_digest.argtypes = [vp, sz]
+    L.sacc_scan_frame_digest.restype = u64
+    L.sacc_model_producer_workspace_bytes.argtypes = []
+    L.sacc_model_producer_workspace_bytes.restype = sz
     _lib = L
     return L
 

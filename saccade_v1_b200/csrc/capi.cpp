@@ -124,6 +124,74 @@ int guarded(F&& body) {
 
 std::size_t dtype_bytes(int dtype) { return dtype == SACC_DTYPE_F32 ? 4 : 2; }
 
+// ---- frame protocol / producer argument checks
+
+void require_frame_control(const char* api, const SaccScanFrameControl* c) {
+    require_pointer(api, {c, sizeof(SaccScanFrameControl), "control"}, alignof(SaccScanFrameControl));
+}
+
+void require_status_list(const char* api, const SaccScanStatusList* list) {
+    if (list == nullptr) reject(api, "status list is required");
+    if (list->count > SACC_FRAME_MAX_STATUSES) reject(api, "too many statuses"); // reference cuda/scan_frame.cu:169
+    for (unsigned i = 0; i < list->count; ++i)
+        require_pointer(api, {list->status[i], sizeof(SaccScanStatus), "status"}, alignof(SaccScanStatus));
+}
+
+void require_records(const char* api, const SaccScanFrameRecord* records, int64_t capacity) {
+    if (records == nullptr || capacity <= 0) return; // no record is written
+    if (static_cast<std::uint64_t>(capacity) > SIZE_MAX / sizeof(SaccScanFrameRecord)) reject(api, "record capacity overflows");
+    require_pointer(api, {records, static_cast<std::size_t>(capacity) * sizeof(SaccScanFrameRecord), "records"},
+                    alignof(SaccScanFrameRecord));
+}
+
+void require_payload(const char* api, const float* payload, std::size_t count, const float* results, const int64_t* result_frames) {
+    if (count > SIZE_MAX / (2 * sizeof(float))) reject(api, "payload count overflows");
+    const Region in{payload, count * sizeof(float), "payload"}, out{results, 2 * count * sizeof(float), "results"};
+    require_pointer(api, in);
+    require_pointer(api, out);
+    require_pointer(api, {result_frames, 2 * sizeof(int64_t), "result_frames"}, alignof(int64_t));
+    if (overlaps(in, out)) reject(api, "results overlap payload");
+}
+
+// cuMemGetAddressRange through the runtime's driver entry point (no link
+// against libcuda).
+using AddressRangeFn = int (*)(unsigned long long* base, std::size_t* size, unsigned long long ptr);
+AddressRangeFn address_range_fn() {
+    static AddressRangeFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<AddressRangeFn>(nullptr);
+        return reinterpret_cast<AddressRangeFn>(ptr);
+    }();
+    return fn;
+}
+
+// reference cuda/model_producer.cu:75-105: non-null, aligned, device memory of
+// the current device, inside one queryable allocation.
+void require_device_range(const char* api, const Region& r, int device) {
+    const auto start = reinterpret_cast<std::uintptr_t>(r.data);
+    if (r.data == nullptr || start % alignof(float) != 0 || r.bytes > UINTPTR_MAX - start)
+        reject(api, "null, unaligned or overflowing model producer pointer");
+    cudaPointerAttributes attr{};
+    const cudaError_t e = cudaPointerGetAttributes(&attr, r.data);
+    if (e == cudaErrorInvalidValue) {
+        (void)cudaGetLastError();
+        reject(api, "model producer pointer must be device memory");
+    }
+    CK(e);
+    if (attr.type != cudaMemoryTypeDevice || attr.device != device)
+        reject(api, "model producer pointer must be on the current CUDA device");
+    const AddressRangeFn range = address_range_fn();
+    if (range == nullptr) throw CudaFail{"cuMemGetAddressRange is unavailable"};
+    unsigned long long base = 0;
+    std::size_t bytes = 0;
+    const int rc = range(&base, &bytes, static_cast<unsigned long long>(start));
+    if (rc != 0) reject(api, "model producer requires a queryable device allocation extent");
+    if (start < base || r.bytes > base + bytes - start) reject(api, "model producer range exceeds its device allocation");
+}
+
 } // namespace
 } // namespace sacc
 
@@ -154,6 +222,8 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
         CK(load_scan_step_kernels(text));
         CK(load_gemm_kernels(text));
         CK(load_block_kernels(text));
+        CK(load_frame_kernels(text));
+        CK(load_producer_kernels(text));
         (void)sm_count();
         if (report && report_bytes) {
             std::snprintf(report, report_bytes, "%s", text.c_str());
@@ -454,6 +524,182 @@ int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_
             reject(api, "needs " + std::to_string(need) + " bytes of scratch, more than the static maximum of " +
                             std::to_string(kNoAllocScratchBytes) + "; use sacc_mamba_block_forward with a workspace");
         CK(launch_mamba_block_noalloc(*args, stream));
+    });
+}
+
+// ------------------------------------------------------------ frame protocol
+// reference cuda/scan_frame.cu:144-209; kernels in scan_frame.cu.
+
+int sacc_scan_frame_load_kernels(char* report, size_t report_bytes) {
+    return guarded([&] {
+        std::string text;
+        CK(load_frame_kernels(text));
+        if (report && report_bytes) std::snprintf(report, report_bytes, "%s", text.c_str());
+    });
+}
+
+int sacc_scan_frame_initialize(SaccScanFrameControl* control, uint64_t epoch, int64_t* result_frames, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_initialize";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        require_pointer(api, {result_frames, 2 * sizeof(int64_t), "result_frames"}, alignof(int64_t));
+        CK(launch_frame_initialize(control, epoch, result_frames, stream));
+    });
+}
+
+int sacc_scan_frame_begin(SaccScanFrameControl* control, uint64_t epoch, int64_t frame, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_begin";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        CK(launch_frame_begin(control, epoch, frame, stream));
+    });
+}
+
+int sacc_scan_frame_gate(SaccScanFrameControl* control, const SaccScanStatusList* statuses, SaccScanFrameRecord* records,
+                         int64_t capacity, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_gate";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        require_status_list(api, statuses);
+        require_records(api, records, capacity);
+        CK(launch_frame_gate(control, *statuses, records, capacity, stream));
+    });
+}
+
+int sacc_scan_frame_publish(SaccScanFrameControl* control, const float* payload, size_t count, float* results,
+                            int64_t* result_frames, SaccScanFrameRecord* records, int64_t capacity, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_publish";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        require_payload(api, payload, count, results, result_frames);
+        require_records(api, records, capacity);
+        CK(launch_frame_publish(control, payload, count, results, result_frames, records, capacity, sm_count(), stream));
+    });
+}
+
+int sacc_scan_frame_commit(SaccScanFrameControl* control, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_commit";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        CK(launch_frame_commit(control, stream));
+    });
+}
+
+int sacc_scan_frame_packet(const SaccScanFrameControl* control, unsigned char* packet, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_packet";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        require_pointer(api, {packet, SACC_PACKET_BYTES, "packet"}, 1);
+        CK(launch_frame_packet(control, packet, stream));
+    });
+}
+
+int sacc_scan_frame_step(SaccScanFrameControl* control, uint64_t epoch, int64_t frame, const SaccScanStatusList* statuses,
+                         const float* payload, size_t count, float* results, int64_t* result_frames,
+                         SaccScanFrameRecord* records, int64_t capacity, unsigned char* packet, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_step";
+        require_stream(api, stream);
+        require_frame_control(api, control);
+        require_status_list(api, statuses);
+        require_payload(api, payload, count, results, result_frames);
+        require_records(api, records, capacity);
+        const FrameStep f{*statuses, payload, count, results, result_frames, records, capacity, packet, epoch, frame};
+        CK(launch_frame_step(control, f, sm_count(), stream));
+    });
+}
+
+int sacc_scan_frame_check_finite(const float* data, size_t count, SaccScanStatus* status, uint32_t flag, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "scan_frame_check_finite";
+        require_stream(api, stream);
+        require_pointer(api, {data, count * sizeof(float), "data"});
+        require_pointer(api, {status, sizeof(SaccScanStatus), "status"});
+        if (overlaps({data, count * sizeof(float), "data"}, {status, sizeof(SaccScanStatus), "status"}))
+            reject(api, "status overlaps data");
+        CK(launch_frame_check_finite(data, count, status, flag, sm_count(), stream));
+    });
+}
+
+int sacc_scan_frame_delay(unsigned cycles, cudaStream_t stream) {
+    return guarded([&] {
+        require_stream("scan_frame_delay", stream);
+        CK(launch_frame_delay(cycles, stream));
+    });
+}
+
+uint64_t sacc_scan_frame_digest(const float* payload, size_t count) { return payload ? frame_digest(payload, count) : 0; }
+
+// ---------------------------------------------------- model producer status
+// reference cuda/model_producer.cu:117-196; kernels in model_producer.cu.
+
+size_t sacc_model_producer_workspace_bytes(void) { return producer_workspace_bytes(); }
+
+int sacc_model_producer_load_kernels(char* report, size_t report_bytes) {
+    return guarded([&] {
+        std::string text;
+        CK(load_producer_kernels(text));
+        if (report && report_bytes) std::snprintf(report, report_bytes, "%s", text.c_str());
+    });
+}
+
+int sacc_model_producer_cuda(const float* images, size_t image_elements, const SaccRawView* raw,
+                             SaccScanStatus* const plugins[SACC_MODEL_PRODUCER_PLUGINS], SaccProducerStatus* producer,
+                             void* workspace, size_t workspace_bytes, cudaStream_t stream, int profile) {
+    return guarded([&] {
+        constexpr const char* api = "model_producer_cuda";
+        if (raw == nullptr || plugins == nullptr) reject(api, "raw view and plugin statuses are required");
+        if (profile != SACC_PROFILE_T01_640X640 && profile != SACC_PROFILE_HR_1280X768) reject(api, "unknown model profile");
+        // Profile shapes (include/saccade/model_profile.hpp:14-38): image
+        // 3 x H x W; per level of stride 8 / 16 / 32, cls 80 x h x w, reg 4 x h x w.
+        const std::size_t width = profile == SACC_PROFILE_HR_1280X768 ? 1280 : 640;
+        const std::size_t height = profile == SACC_PROFILE_HR_1280X768 ? 768 : 640;
+        if (image_elements != 3 * width * height || workspace_bytes < producer_workspace_bytes())
+            reject(api, "incorrect model producer input/workspace capacity");
+        // reference src/postprocess.cpp:71-80
+        for (int level = 0; level < 3; ++level) {
+            const std::size_t stride = std::size_t{8} << level, spatial = (height / stride) * (width / stride);
+            if (raw->cls[level] == nullptr || raw->reg[level] == nullptr || raw->cls_elements[level] != 80 * spatial ||
+                raw->reg_elements[level] != 4 * spatial)
+                reject(api, "F04 requires all six fixed-shape raw tensors");
+            if (reinterpret_cast<std::uintptr_t>(raw->cls[level]) % alignof(float) != 0 ||
+                reinterpret_cast<std::uintptr_t>(raw->reg[level]) % alignof(float) != 0)
+                reject(api, "F04 requires aligned FP32 raw tensors");
+        }
+        require_stream(api, stream);
+        int device = -1, stream_device = -1;
+        CK(cudaGetDevice(&device));
+        CK(cudaStreamGetDevice(stream, &stream_device));
+        if (stream_device != device) reject(api, "model producer stream belongs to another CUDA device");
+        ProducerLaunch p{};
+        Region regions[18]{};
+        p.tensor[0] = images;
+        p.count[0] = image_elements;
+        for (int l = 0; l < 3; ++l) {
+            p.tensor[1 + l] = raw->cls[l];
+            p.count[1 + l] = raw->cls_elements[l];
+            p.tensor[4 + l] = raw->reg[l];
+            p.count[4 + l] = raw->reg_elements[l];
+        }
+        for (int i = 0; i < 7; ++i) regions[i] = {p.tensor[i], p.count[i] * sizeof(float), "model producer tensor"};
+        for (unsigned i = 0; i < SACC_MODEL_PRODUCER_PLUGINS; ++i) {
+            p.plugin[i] = plugins[i];
+            regions[7 + i] = {plugins[i], sizeof(SaccScanStatus), "plugin status"};
+        }
+        regions[16] = {producer, sizeof(SaccProducerStatus), "producer"};
+        regions[17] = {workspace, producer_workspace_bytes(), "workspace"};
+        // reference cuda/model_producer.cu:75-110, 159-165
+        for (const auto& r : regions) require_device_range(api, r, device);
+        for (int i = 0; i < 18; ++i)
+            for (int j = i + 1; j < 18; ++j)
+                if (overlaps(regions[i], regions[j])) reject(api, "overlapping model producer buffers");
+        CK(launch_model_producer(p, producer, workspace, sm_count(), stream));
     });
 }
 

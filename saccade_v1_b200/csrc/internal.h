@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <string>
 
+#include "../../include/sacc_frame.h"
 #include "../../include/sacc_scan.h"
 
 namespace sacc {
@@ -112,5 +113,45 @@ cudaError_t read_bulk_fault(unsigned* out, bool clear);
 cudaError_t load_scan_f32_kernels(std::string& report);
 cudaError_t load_cross_kernels(std::string& report);
 cudaError_t load_scan_ex_kernels(std::string& report);
+
+// Frame protocol over the status words (scan_frame.cu).
+struct FrameStep {
+    SaccScanStatusList list;
+    const float* payload;
+    unsigned long long count;
+    float* results;
+    std::int64_t* result_frames;
+    SaccScanFrameRecord* records;
+    std::int64_t capacity;
+    unsigned char* packet;
+    std::uint64_t epoch;
+    std::int64_t frame;
+};
+cudaError_t launch_frame_initialize(SaccScanFrameControl* ctl, std::uint64_t epoch, std::int64_t* result_frames, cudaStream_t s);
+cudaError_t launch_frame_begin(SaccScanFrameControl* ctl, std::uint64_t epoch, std::int64_t frame, cudaStream_t s);
+cudaError_t launch_frame_gate(SaccScanFrameControl* ctl, const SaccScanStatusList& list, SaccScanFrameRecord* records,
+                              std::int64_t capacity, cudaStream_t s);
+cudaError_t launch_frame_publish(SaccScanFrameControl* ctl, const float* payload, unsigned long long count, float* results,
+                                 std::int64_t* result_frames, SaccScanFrameRecord* records, std::int64_t capacity, int sms,
+                                 cudaStream_t s);
+cudaError_t launch_frame_commit(SaccScanFrameControl* ctl, cudaStream_t s);
+cudaError_t launch_frame_packet(const SaccScanFrameControl* ctl, unsigned char* packet, cudaStream_t s);
+cudaError_t launch_frame_step(SaccScanFrameControl* ctl, const FrameStep& f, int sms, cudaStream_t s);
+cudaError_t launch_frame_check_finite(const float* data, unsigned long long count, SaccScanStatus* status, std::uint32_t flag,
+                                      int sms, cudaStream_t s);
+cudaError_t launch_frame_delay(unsigned cycles, cudaStream_t s);
+std::uint64_t frame_digest(const float* payload, std::size_t count);
+cudaError_t load_frame_kernels(std::string& report);
+
+// Model producer status aggregate (model_producer.cu): the image and the six
+// raw tensors checked for NaN / Inf, nine plugin statuses gated.
+struct ProducerLaunch {
+    const float* tensor[7];
+    unsigned long long count[7];
+    SaccScanStatus* plugin[SACC_MODEL_PRODUCER_PLUGINS];
+};
+std::size_t producer_workspace_bytes();
+cudaError_t launch_model_producer(const ProducerLaunch& p, SaccProducerStatus* producer, void* workspace, int sms, cudaStream_t s);
+cudaError_t load_producer_kernels(std::string& report);
 
 } // namespace sacc

@@ -446,7 +446,7 @@ def hr_deploy(torch, device, stream, peak):
     import saccade_v1_b200 as sb
     g = torch.Generator(device=device)
     g.manual_seed(78)
-    levels, calls = {}, []
+    levels, calls, f16, casts = {}, [], [], []
     with torch.cuda.stream(stream):
         st = torch.zeros(2, dtype=torch.int32, device=device)
         for L_ in (960, 240, 60):
@@ -461,9 +461,96 @@ def hr_deploy(torch, device, stream, peak):
             call = (lambda s_=shape, a_=(uu, dd, aa, bb, cc, dv, yy): sb.selective_scan_cuda(s_, *a_, st, stream=stream))
             levels[f"HR_L{L_}"] = round(time_device(torch, stream, call, 50), 2)
             calls.append(call)
+            # FP16 engine: the plugin v3 path on FP16 activations, and the v2 path with the casts an FP16 engine
+            # puts around an FP32 plugin (u, delta, B, C widened, y narrowed).
+            hu, hd, hb, hc = uu.half(), dd.half(), bb.half(), cc.half()
+            hy = torch.empty_like(hu)
+            f16.append(lambda s_=shape, a_=(hu, hd, aa, hb, hc, dv, hy): sb.selective_scan_f16(s_, *a_, st, stream=stream))
+
+            def cast_call(s_=shape, a_=(hu, hd, aa, hb, hc, dv), out=(yy, hy)):
+                u_, d_, a32, b_, c_, dv_ = a_
+                sb.selective_scan_cuda(s_, u_.float(), d_.float(), a32, b_.float(), c_.float(), dv_, out[0], st,
+                                       stream=stream)
+                out[1].copy_(out[0])
+            casts.append(cast_call)
     total = time_device(torch, stream, lambda: [c() for c in calls], 50)
-    return dict(levels, total=round(total, 2), reference_published_total_us=722.351,
+    with torch.cuda.stream(stream):
+        total16 = time_device(torch, stream, lambda: [c() for c in f16], 50)
+        total_cast = time_device(torch, stream, lambda: [c() for c in casts], 50)
+    return dict(levels, total=round(total, 2), fp16_plugin_v3_total=round(total16, 2),
+                fp32_plugin_with_casts_total=round(total_cast, 2), reference_published_total_us=722.351,
                 note="reference figure is its own CUDA kernel on an RTX 5070 Ti laptop GPU")
+
+
+def frame_protocol(torch, device, stream):
+    """Frame-end status handling per frame at the detector's shapes (T01 profile: image 3 x 640 x 640, payload
+    84 x 8400 raw floats): nine plugin status words re-armed, the finite checks of the image and of the payload,
+    then begin / gate (11 statuses) / publish / commit / packet as the reference's five launches, or as the
+    library's one launch; eager and replayed from a CUDA graph."""
+    from saccade_v1_b200 import frame as fr
+    count, cap = 84 * 8400, 64
+    g = torch.Generator(device=device)
+    g.manual_seed(31)
+    with torch.cuda.stream(stream):
+        image = torch.randn(3 * 640 * 640, device=device, generator=g)
+        payload = torch.randn(count, device=device, generator=g)
+        done = np.array([[0, 0x4E414353]] * 11, np.uint32).view(np.int32)
+        armed = torch.from_numpy(done).to(device)
+        st = torch.zeros_like(armed)
+        ctl, rec = fr.new_control(device), fr.new_records(cap, device)
+        results = torch.empty(2 * count, device=device)
+        rf = torch.empty(2, dtype=torch.int64, device=device)
+        packet = torch.empty(fr.PACKET_BYTES, dtype=torch.uint8, device=device)
+        fr.scan_frame_initialize(ctl, 1, rf, stream=stream)
+    frame_no = [0]
+
+    def checks():
+        st.copy_(armed)
+        fr.scan_frame_check_finite(image, st[9], fr.FRAME_NONFINITE_INPUT, stream=stream)
+        fr.scan_frame_check_finite(payload, st[10], fr.FRAME_NONFINITE_OUTPUT, stream=stream)
+
+    def single():
+        checks()
+        fr.scan_frame_begin(ctl, 1, frame_no[0], stream=stream)
+        fr.scan_frame_gate(ctl, st, rec, cap, stream=stream)
+        fr.scan_frame_publish(ctl, payload, results, rf, rec, cap, stream=stream)
+        fr.scan_frame_commit(ctl, stream=stream)
+        fr.scan_frame_packet(ctl, packet, stream=stream)
+        frame_no[0] += 1
+
+    def fused():
+        checks()
+        fr.scan_frame_step(ctl, 1, frame_no[0], st, payload, results, rf, rec, cap, packet, stream=stream)
+        frame_no[0] += 1
+
+    out = {}
+    for name, fn in (("single_steps", single), ("one_launch", fused)):
+        with torch.cuda.stream(stream):
+            fr.scan_frame_initialize(ctl, 1, rf, stream=stream)
+        frame_no[0] = 0
+        out[f"{name}_us"] = round(time_device(torch, stream, fn, 200), 2)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fr.scan_frame_initialize(ctl, 1, rf, stream=stream)
+        stream.synchronize()
+        frame_no[0] = 0
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(10):
+                fn()
+
+        def replay():
+            with torch.cuda.stream(stream):
+                fr.scan_frame_initialize(ctl, 1, rf, stream=stream)
+                graph.replay()
+
+        out[f"{name}_us_graph"] = round(time_device(torch, stream, replay, 50) / 10, 2)
+        del graph
+    stream.synchronize()
+    c = fr.read_control(ctl.cpu().numpy())
+    assert c["fail_code"] == 0 and c["committed"] == 9, c  # every timed frame passed the gate and committed
+    out["workload"] = ("per frame: 9 plugin statuses re-armed, finite checks of a 3 x 640 x 640 image and an "
+                       "84 x 8400 payload, gate over 11 statuses, publish + digest of the payload, commit, packet")
+    return out
 
 
 def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
@@ -471,6 +558,7 @@ def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
     runs = {"c3_step": c3_step, "c3_rescan": c3_rescan, "hr_deploy_f32_us": hr_deploy,
             "c1_block": lambda *a: c1_block(*a[:3]), "hr_head_block": lambda *a: hr_head_block(*a[:3]),
             "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m),
+            "frame_protocol": lambda *a: frame_protocol(*a[:3]),
             "c4_stack": lambda *a: c4_stack(*a[:3])}
     out = {}
     for name, fn in runs.items():
@@ -748,7 +836,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 stack (52 GB on one GPU)")
-    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "hr_head_block", "gemm",
+    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "hr_head_block", "frame_protocol", "gemm",
                                        "c4_stack"],
                     help="run one secondary measurement alone on cuda:0 and print it (for profiling)")
     ap.add_argument("--gemm-m", type=int, default=64 * 4096, help="rows of the GEMM probe (smaller only for profiling)")

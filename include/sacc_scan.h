@@ -17,6 +17,10 @@
  *   sacc_cross_scan_expand_f32      cross_scan_expand_cuda, cuda/selective_scan.cu:402-417
  *   sacc_cross_scan_merge_f32       cross_scan_merge_cuda, cuda/selective_scan.cu:419-434
  *   sacc_scan_identity              selective_scan_cuda_identity, cuda/selective_scan.cu:436-446
+ *   sacc_selective_scan_f16         no counterpart: the FP16-activation form behind plugin
+ *                                   SelectiveScan v3 (the reference's FP16 engine keeps its scan
+ *                                   plugins FP32 and casts around them,
+ *                                   include/saccade/head_trt_network.hpp:25-28)
  * The reference throws std::invalid_argument (host rejection, nothing
  * enqueued) and std::runtime_error (a CUDA API call failed); here those are
  * SACC_EINVAL and SACC_ECUDA with the same diagnostic text.
@@ -94,6 +98,22 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes);
  * non-default stream.  Zero workspace.  Pointers must be 4-byte aligned;
  * y and status must not overlap an input or each other. */
 int sacc_selective_scan_f32(const SaccScanShape* shape, const SaccScanInputs* inputs, float* y, SaccScanStatus* status,
+                            cudaStream_t stream);
+
+/* The same operator with FP16 activations: u, delta, b, c and y are IEEE
+ * binary16 bit patterns (2-byte aligned), a and d stay FP32.  Checks,
+ * arithmetic and status bits are those of sacc_selective_scan_f32 on the
+ * inputs widened to FP32 (a NaN or infinity in an FP16 input sets its input
+ * bit), and y is that call's output rounded to nearest FP16; an output of
+ * magnitude 65520 or more, which FP16 cannot hold, is SACC_SCAN_OUTPUT_RANGE.
+ * On failure every y element is the FP16 quiet NaN 0x7E00. */
+typedef struct SaccScanInputsF16 {
+    const uint16_t *u, *delta;
+    const float* a;
+    const uint16_t *b, *c;
+    const float* d;
+} SaccScanInputsF16;
+int sacc_selective_scan_f16(const SaccScanShape* shape, const SaccScanInputsF16* inputs, uint16_t* y, SaccScanStatus* status,
                             cudaStream_t stream);
 
 /* Cross-Scan (x (batch, channels, height, width) <-> tokens (4 batch,

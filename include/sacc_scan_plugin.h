@@ -4,6 +4,11 @@
  * The reference exposes its scan to TensorRT as three IPluginV3 plugins
  * (include/saccade/scan_trt_plugin.hpp:26-49, src/scan_trt_plugin.cpp):
  *   saccade::SelectiveScan   v2  fields: has_d (INT32)
+ * plus, without a reference counterpart, the FP16-activation version of the
+ * scan for FP16 engines (the reference keeps its scan plugins FP32 there and
+ * lets TensorRT cast around them, include/saccade/head_trt_network.hpp:25-28):
+ *   saccade::SelectiveScan   v3  fields: has_d (INT32); u, delta, B, C and y
+ *                                kHALF, A and D kFLOAT (sacc_selective_scan_f16)
  *   saccade::CrossScanExpand v1  fields: none
  *   saccade::CrossScanMerge  v1  fields: height, width (INT32)
  * Each entry point below implements one IPluginV3 / IPluginCreatorV3One method
@@ -28,6 +33,7 @@ extern "C" {
 #define SACC_PLUGIN_NAMESPACE "saccade"
 #define SACC_PLUGIN_SCAN_NAME "SelectiveScan"
 #define SACC_PLUGIN_SCAN_VERSION "2"
+#define SACC_PLUGIN_SCAN_F16_VERSION "3"
 #define SACC_PLUGIN_EXPAND_NAME "CrossScanExpand"
 #define SACC_PLUGIN_EXPAND_VERSION "1"
 #define SACC_PLUGIN_MERGE_NAME "CrossScanMerge"
@@ -38,6 +44,7 @@ extern "C" {
 #define SACC_FIELD_INT32 1
 #define SACC_FIELD_OTHER 0
 #define SACC_TENSOR_FLOAT 0
+#define SACC_TENSOR_HALF 1
 #define SACC_TENSOR_INT32 3
 #define SACC_TENSOR_OTHER 99
 #define SACC_FORMAT_LINEAR 0

@@ -21,5 +21,6 @@ from .scan import (  # noqa: F401
     scan_fault,
     selective_scan_cuda,
     selective_scan_ex,
+    selective_scan_f16,
     selective_scan_step,
 )

@@ -33,6 +33,7 @@ EXPORTS = (
     "sacc_mamba_block_workspace",
     "sacc_mamba_block_forward",
     "sacc_mamba_block_forward_noalloc",
+    "sacc_selective_scan_f16",
     # include/sacc_frame.h
     "sacc_scan_frame_load_kernels",
     "sacc_scan_frame_initialize",
@@ -61,6 +62,10 @@ class ScanShape(ctypes.Structure):
 
 
 class ScanInputs(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_void_p) for k in ("u", "delta", "a", "b", "c", "d")]
+
+
+class ScanInputsF16(ctypes.Structure):
     _fields_ = [(k, ctypes.c_void_p) for k in ("u", "delta", "a", "b", "c", "d")]
 
 
@@ -141,6 +146,8 @@ def load() -> ctypes.CDLL:
     L.sacc_scan_load_kernels.restype = i
     L.sacc_selective_scan_f32.argtypes = [ctypes.POINTER(ScanShape), ctypes.POINTER(ScanInputs), vp, vp, vp]
     L.sacc_selective_scan_f32.restype = i
+    L.sacc_selective_scan_f16.argtypes = [ctypes.POINTER(ScanShape), ctypes.POINTER(ScanInputsF16), vp, vp, vp]
+    L.sacc_selective_scan_f16.restype = i
     L.sacc_cross_scan_expand_f32.argtypes = [ctypes.POINTER(CrossScanShape), vp, vp, vp, vp]
     L.sacc_cross_scan_expand_f32.restype = i
     L.sacc_cross_scan_merge_f32.argtypes = [ctypes.POINTER(CrossScanShape), vp, vp, vp, vp]

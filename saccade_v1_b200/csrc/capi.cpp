@@ -55,9 +55,11 @@ struct Region {
     const void* data;
     std::size_t bytes;
     const char* name;
+    std::size_t align = alignof(float); // element alignment the kernels need
 };
 
-void require_pointer(const char* api, const Region& r, std::size_t align = alignof(float)) {
+void require_pointer(const char* api, const Region& r, std::size_t align = 0) {
+    if (align == 0) align = r.align;
     if (r.bytes == 0) return;
     if (r.data == nullptr) reject(api, std::string(r.name) + " is null");
     if (reinterpret_cast<std::uintptr_t>(r.data) % align != 0)
@@ -123,6 +125,48 @@ int guarded(F&& body) {
 }
 
 std::size_t dtype_bytes(int dtype) { return dtype == SACC_DTYPE_F32 ? 4 : 2; }
+
+// Host side of the reference ABI (cuda/selective_scan.cu:285-400): FP32
+// activations, or FP16 ones (u, delta, B, C, y) with `half`.
+void reference_scan(const char* api, const SaccScanShape& s, const void* u, const void* delta, const float* a, const void* b,
+                    const void* c, const float* d, void* y, SaccScanStatus* status, cudaStream_t stream, bool half) {
+    require_stream(api, stream);
+    if (s.batch == 0 || s.channels == 0) reject(api, "batch and channels must be positive");
+    if (s.state == 0 || s.state > 32 || (s.state & (s.state - 1)) != 0)
+        reject(api, "state " + std::to_string(s.state) + " must be a power of two in [1, 32]");
+    if (s.a_rows != 1 && s.a_rows != s.channels) reject(api, "A rows must be 1 or channels");
+    if (s.c_width != 1 && s.c_width != s.state) reject(api, "C width must be 1 or state");
+    const auto ud = elements(api, {s.batch, s.length, s.channels}, "u/delta/y");
+    const auto bn = elements(api, {s.batch, s.length, s.state}, "B");
+    const auto cn = elements(api, {s.batch, s.length, s.c_width}, "C");
+    const auto an = elements(api, {s.a_rows, s.state}, "A");
+    const std::size_t dn = s.has_d ? static_cast<std::size_t>(s.channels) : 0;
+    constexpr auto f = sizeof(float);
+    const std::size_t e = half ? 2 : 4; // activation element bytes
+    require_regions(api,
+                    {{u, ud * e, "u", e}, {delta, ud * e, "delta", e}, {a, an * f, "A"}, {b, bn * e, "B", e},
+                     {c, cn * e, "C", e}, {d, dn * f, "D"}},
+                    {y, ud * e, "y", e}, {status, sizeof(SaccScanStatus), "status"});
+    const int sms = sm_count();
+    CK(cudaMemsetAsync(status, 0, sizeof(SaccScanStatus), stream));
+    const int h = half ? 1 : 0;
+    CheckList list{{{u, ud, SACC_SCAN_NONFINITE_U, h},
+                    {delta, ud, SACC_SCAN_NONFINITE_DELTA, h},
+                    {a, an, SACC_SCAN_NONFINITE_A, 0},
+                    {b, bn, SACC_SCAN_NONFINITE_B, h},
+                    {c, cn, SACC_SCAN_NONFINITE_C, h},
+                    {d, dn, SACC_SCAN_NONFINITE_D, 0}},
+                   6};
+    if (s.length > 0) {
+        ScanF32Launch p{u, delta, a, b, c, d, y, s.batch, s.length, s.channels,
+                        s.batch * s.channels, static_cast<unsigned>(s.state), s.a_rows == 1, s.c_width != 1,
+                        s.has_d != 0, list, half};
+        CK(launch_scan_f32(p, status, sms, stream));
+    } else {
+        CK(launch_check(list, status, sms, stream));
+    }
+    CK(launch_finalize(y, ud, status, sms, stream, half));
+}
 
 // ---- frame protocol / producer argument checks
 
@@ -237,41 +281,17 @@ int sacc_selective_scan_f32(const SaccScanShape* shape, const SaccScanInputs* in
     return guarded([&] {
         constexpr const char* api = "selective_scan_cuda";
         if (shape == nullptr || in == nullptr) reject(api, "shape and inputs are required");
-        const SaccScanShape& s = *shape;
-        require_stream(api, stream);
-        if (s.batch == 0 || s.channels == 0) reject(api, "batch and channels must be positive");
-        if (s.state == 0 || s.state > 32 || (s.state & (s.state - 1)) != 0)
-            reject(api, "state " + std::to_string(s.state) + " must be a power of two in [1, 32]");
-        if (s.a_rows != 1 && s.a_rows != s.channels) reject(api, "A rows must be 1 or channels");
-        if (s.c_width != 1 && s.c_width != s.state) reject(api, "C width must be 1 or state");
-        const auto ud = elements(api, {s.batch, s.length, s.channels}, "u/delta/y");
-        const auto bn = elements(api, {s.batch, s.length, s.state}, "B");
-        const auto cn = elements(api, {s.batch, s.length, s.c_width}, "C");
-        const auto an = elements(api, {s.a_rows, s.state}, "A");
-        const std::size_t dn = s.has_d ? static_cast<std::size_t>(s.channels) : 0;
-        constexpr auto f = sizeof(float);
-        require_regions(api,
-                        {{in->u, ud * f, "u"}, {in->delta, ud * f, "delta"}, {in->a, an * f, "A"}, {in->b, bn * f, "B"},
-                         {in->c, cn * f, "C"}, {in->d, dn * f, "D"}},
-                        {y, ud * f, "y"}, {status, sizeof(SaccScanStatus), "status"});
-        const int sms = sm_count();
-        CK(cudaMemsetAsync(status, 0, sizeof(SaccScanStatus), stream));
-        CheckList list{{{in->u, ud, SACC_SCAN_NONFINITE_U},
-                        {in->delta, ud, SACC_SCAN_NONFINITE_DELTA},
-                        {in->a, an, SACC_SCAN_NONFINITE_A},
-                        {in->b, bn, SACC_SCAN_NONFINITE_B},
-                        {in->c, cn, SACC_SCAN_NONFINITE_C},
-                        {in->d, dn, SACC_SCAN_NONFINITE_D}},
-                       6};
-        if (s.length > 0) {
-            ScanF32Launch p{in->u, in->delta, in->a, in->b, in->c, in->d, y, s.batch, s.length, s.channels,
-                            s.batch * s.channels, static_cast<unsigned>(s.state), s.a_rows == 1, s.c_width != 1,
-                            s.has_d != 0, list};
-            CK(launch_scan_f32(p, status, sms, stream));
-        } else {
-            CK(launch_check(list, status, sms, stream));
-        }
-        CK(launch_finalize(y, ud, status, sms, stream));
+        reference_scan(api, *shape, in->u, in->delta, in->a, in->b, in->c, in->d, y, status, stream, false);
+    });
+}
+
+// The reference ABI with FP16 activations (plugin SelectiveScan v3).
+int sacc_selective_scan_f16(const SaccScanShape* shape, const SaccScanInputsF16* in, uint16_t* y, SaccScanStatus* status,
+                            cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "selective_scan_f16";
+        if (shape == nullptr || in == nullptr) reject(api, "shape and inputs are required");
+        reference_scan(api, *shape, in->u, in->delta, in->a, in->b, in->c, in->d, y, status, stream, true);
     });
 }
 

@@ -35,30 +35,38 @@ inline cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, std::size_t
 constexpr std::size_t kMaxElements = 2147483647u;
 
 struct CheckedTensor {
-    const float* data;
+    const void* data; // FP32, or FP16 when `half`
     unsigned long long count;
     std::uint32_t bit;
+    int half = 0;
 };
 struct CheckList {
     CheckedTensor tensor[6];
     unsigned size;
 };
 
-// One reference-ABI call, resolved on the host.
+// One reference-ABI call, resolved on the host; `half`: u, delta, B, C and y
+// are FP16 (plugin v3), A and D FP32 either way.
 struct ScanF32Launch {
-    const float *u, *delta, *a, *b, *c, *d;
-    float* y;
+    const void *u, *delta;
+    const float* a;
+    const void *b, *c;
+    const float* d;
+    void* y;
     unsigned long long batch, length, channels, lanes;
     unsigned state;
     bool a_shared, c_full, has_d;
     CheckList check;
+    bool half = false;
 };
 
 // Enqueues the fused input-check + scan kernel on `stream` (status already
 // cleared by the caller).  Returns a CUDA error (launch only).
 cudaError_t launch_scan_f32(const ScanF32Launch& p, SaccScanStatus* status, int sm_count, cudaStream_t stream);
-// Poisons `count` outputs with quiet NaN when flags != 0, then writes done.
-cudaError_t launch_finalize(float* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream);
+// Poisons `count` outputs (FP32, or FP16 when `half`) with quiet NaN when
+// flags != 0, then writes done.
+cudaError_t launch_finalize(void* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream,
+                            bool half = false);
 // Input check only (Cross-Scan and L = 0 paths).
 cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream);
 

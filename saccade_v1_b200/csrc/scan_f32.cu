@@ -18,18 +18,26 @@
 //  * the input finiteness check runs in the same launch (extra CTAs after the
 //    scan CTAs), so one call is memset + 1 kernel + finalize.
 //
+// The same kernels serve FP16 activations (plugin SelectiveScan v3): u,
+// delta, B and C are widened to FP32 as they are loaded and y is rounded to
+// nearest FP16 as it is stored, so the outputs are the FP32 path's outputs on
+// the widened inputs, rounded; an output at or beyond 65520 (which rounds to
+// infinity in FP16) is reported as an output range failure.
+//
 // Per-token arithmetic keeps the reference's FP32 algorithm, so its running
 // error bound (docs/SCAN_CUDA.md section 5 of the reference) applies: the plain
 // FP32 products are used whenever they provably equal the reference's
 // mantissa/exponent-scaled products (Delta, Delta*B and Delta*B*u normal), and
 // the scaled form is evaluated otherwise.  With K = 1 the outputs are the
 // reference algorithm's bits (same operations, same summation tree).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cfloat>
 #include <climits>
 #include <cstdint>
 #include <string>
+#include <type_traits>
 
 #include "internal.h"
 
@@ -41,6 +49,22 @@ constexpr unsigned kDecay = SACC_SCAN_DECAY_RANGE, kDrive = SACC_SCAN_DRIVE_RANG
                    kTerm = SACC_SCAN_TERM_RANGE, kSkip = SACC_SCAN_SKIP_RANGE, kOutput = SACC_SCAN_OUTPUT_RANGE;
 
 __device__ __forceinline__ bool finite32(float x) { return fabsf(x) <= FLT_MAX; } // false for NaN and +-inf
+
+// Smallest magnitude that rounds to infinity in FP16 (the midpoint between
+// 65504 and 2^16 rounds to the even 2^16).
+constexpr float kHalfOverflow = 65520.0f;
+
+template <typename T>
+__device__ __forceinline__ float load_act(const T* p) {
+    if constexpr (std::is_same_v<T, __half>) return __half2float(__ldg(p));
+    else return __ldg(p);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_act(T* p, float v) {
+    if constexpr (std::is_same_v<T, __half>) *p = __float2half_rn(v);
+    else *p = v;
+}
 
 // value = m * 2^e with m in [0.5, 1) or m == 0 (frexpf / ldexpf are exact).
 struct Scaled {
@@ -83,8 +107,9 @@ __device__ __forceinline__ float tree_sum(float (&v)[N]) {
 }
 
 struct Params {
-    const float *u, *delta, *a, *b, *c, *d;
-    float* y;
+    const void *u, *delta, *b, *c; // FP32 or FP16 (the kernel's T)
+    const float *a, *d;
+    void* y;
     unsigned long long length, channels, lanes;
     int a_shared, c_full, has_d, vec_b, vec_c;
     int chunks, lanes_per_cta;
@@ -92,20 +117,29 @@ struct Params {
     CheckList check;
 };
 
-template <int N>
-__device__ __forceinline__ void load_row(const float* p, float (&out)[N], bool vec) {
+// N values of a row; `vec`: the row starts 16-byte (FP32) or 8-byte (FP16)
+// aligned, four values per load.
+template <typename T, int N>
+__device__ __forceinline__ void load_row(const T* p, float (&out)[N], bool vec) {
     if constexpr (N % 4 == 0) {
         if (vec) {
 #pragma unroll
             for (int i = 0; i < N; i += 4) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i / 4);
-                out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+                if constexpr (std::is_same_v<T, __half>) {
+                    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p) + i / 4);
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+                    out[i] = lo.x; out[i + 1] = lo.y; out[i + 2] = hi.x; out[i + 3] = hi.y;
+                } else {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i / 4);
+                    out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+                }
             }
             return;
         }
     }
 #pragma unroll
-    for (int i = 0; i < N; ++i) out[i] = __ldg(p + i);
+    for (int i = 0; i < N; ++i) out[i] = load_act(p + i);
 }
 
 // Operands of one token of one lane.
@@ -116,16 +150,16 @@ struct Token {
     float c[N];
 };
 
-template <int N>
+template <typename T, int N>
 __device__ __forceinline__ void load_token(const Params& p, unsigned long long token, unsigned long long d, Token<N>& k) {
     const unsigned long long at = token * p.channels + d;
-    k.u = __ldg(p.u + at);
-    k.x = __ldg(p.delta + at);
-    load_row<N>(p.b + token * N, k.b, p.vec_b);
+    k.u = load_act(static_cast<const T*>(p.u) + at);
+    k.x = load_act(static_cast<const T*>(p.delta) + at);
+    load_row<T, N>(static_cast<const T*>(p.b) + token * N, k.b, p.vec_b);
     if (p.c_full) {
-        load_row<N>(p.c + token * N, k.c, p.vec_c);
+        load_row<T, N>(static_cast<const T*>(p.c) + token * N, k.c, p.vec_c);
     } else {
-        const float cv = __ldg(p.c + token);
+        const float cv = load_act(static_cast<const T*>(p.c) + token);
 #pragma unroll
         for (int n = 0; n < N; ++n) k.c[n] = cv;
     }
@@ -177,8 +211,9 @@ __device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], cons
 }
 
 // Pass 2: one token with output and the reference's failure order
-// (cuda/selective_scan.cu:193-212).  Returns the failure bits (0 = ok).
-template <int N>
+// (cuda/selective_scan.cu:193-212).  Returns the failure bits (0 = ok).  With
+// kHalfOut an output that FP16 cannot hold is an output range failure.
+template <int N, bool kHalfOut>
 __device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N], const Token<N>& k, bool has_d, float skip_d,
                                              float& y) {
     float hn[N], decay[N], drive[N];
@@ -210,6 +245,7 @@ __device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N],
         if (fabsf(out) <= FLT_MAX * 0x1p-8f) out = __fmul_rn(out, 0x1p8f);
         else return kOutput;
     }
+    if (kHalfOut && !(fabsf(out) < kHalfOverflow)) return kOutput;
     y = out;
     return 0;
 }
@@ -220,7 +256,28 @@ __device__ void check_tensors(const CheckList& list, unsigned long long first, u
     std::uint32_t found = 0;
     for (unsigned t = 0; t < list.size; ++t) {
         const CheckedTensor ct = list.tensor[t];
-        const float* data = ct.data;
+        if (ct.half) {
+            // FP16: NaN or infinity iff the five exponent bits are all ones.
+            const unsigned short* data = static_cast<const unsigned short*>(ct.data);
+            unsigned long long i0 = 0;
+            bool bad = false;
+            if ((reinterpret_cast<std::uintptr_t>(data) & 15u) == 0) {
+                const unsigned long long octs = ct.count / 8;
+                const uint4* q = reinterpret_cast<const uint4*>(data);
+                for (unsigned long long i = first; i < octs; i += stride) {
+                    const uint4 v = __ldg(q + i);
+                    const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        bad |= ((w[j] & 0x7C00u) == 0x7C00u) | ((w[j] & 0x7C000000u) == 0x7C000000u);
+                }
+                i0 = octs * 8;
+            }
+            for (unsigned long long i = i0 + first; i < ct.count; i += stride) bad |= (__ldg(data + i) & 0x7C00u) == 0x7C00u;
+            if (bad) found |= ct.bit;
+            continue;
+        }
+        const float* data = static_cast<const float*>(ct.data);
         unsigned long long i0 = 0;
         const bool aligned = (reinterpret_cast<std::uintptr_t>(data) & 15u) == 0;
         if (aligned) {
@@ -241,7 +298,7 @@ __device__ void check_tensors(const CheckList& list, unsigned long long first, u
     if (found) atomicOr(&status->flags, found);
 }
 
-template <int N>
+template <typename T, int N>
 __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanStatus* status) {
     if (blockIdx.x >= p.scan_blocks) {
         const unsigned long long first = static_cast<unsigned long long>(blockIdx.x - p.scan_blocks) * kThreads + threadIdx.x;
@@ -273,10 +330,10 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
         for (int n = 0; n < N; ++n) prod[n] = 1.0f;
         if (active && k < K - 1) {
             Token<N> cur;
-            if (t0 < t1) load_token<N>(p, bb * L + t0, d, cur);
+            if (t0 < t1) load_token<T, N>(p, bb * L + t0, d, cur);
             for (unsigned long long t = t0; t < t1; ++t) {
                 Token<N> nxt;
-                if (t + 1 < t1) load_token<N>(p, bb * L + t + 1, d, nxt);
+                if (t + 1 < t1) load_token<T, N>(p, bb * L + t + 1, d, nxt);
                 step_carry<N>(h, prod, a, cur);
                 cur = nxt;
             }
@@ -301,14 +358,14 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
     unsigned fail = 0;
     if (active && t0 < t1) {
         Token<N> cur;
-        load_token<N>(p, bb * L + t0, d, cur);
+        load_token<T, N>(p, bb * L + t0, d, cur);
         for (unsigned long long t = t0; t < t1; ++t) {
             Token<N> nxt;
-            if (t + 1 < t1) load_token<N>(p, bb * L + t + 1, d, nxt);
+            if (t + 1 < t1) load_token<T, N>(p, bb * L + t + 1, d, nxt);
             float y = 0.0f;
-            fail = step_out<N>(h, a, cur, p.has_d != 0, skip_d, y);
+            fail = step_out<N, std::is_same_v<T, __half>>(h, a, cur, p.has_d != 0, skip_d, y);
             if (fail) break;
-            p.y[(bb * L + t) * Dc + d] = y;
+            store_act(static_cast<T*>(p.y) + (bb * L + t) * Dc + d, y);
             cur = nxt;
         }
     }
@@ -332,31 +389,36 @@ __global__ void __launch_bounds__(kThreads) check_kernel(CheckList list, SaccSca
                   static_cast<unsigned long long>(gridDim.x) * kThreads, status);
 }
 
-// Last kernel of every call: poison every output on failure, then write done
-// (reference cuda/selective_scan.cu:238-244).
-__global__ void __launch_bounds__(kThreads) finalize_kernel(float* out, unsigned long long count, SaccScanStatus* status) {
+// Last kernel of every call: poison every output on failure (the FP32 quiet
+// NaN 0x7fc00000, or the FP16 one 0x7e00), then write done (reference
+// cuda/selective_scan.cu:238-244).
+template <typename W, unsigned kPoison>
+__global__ void __launch_bounds__(kThreads) finalize_kernel(W* out, unsigned long long count, SaccScanStatus* status) {
     const unsigned long long first = static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x;
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * kThreads;
     if (status->flags)
-        for (unsigned long long i = first; i < count; i += stride) out[i] = __int_as_float(0x7fc00000);
+        for (unsigned long long i = first; i < count; i += stride) out[i] = static_cast<W>(kPoison);
     if (first == 0) status->done = SACC_SCAN_DONE;
 }
 
-template <int N>
+template <typename T, int N>
 const void* scan_kernel_ptr() {
-    return reinterpret_cast<const void*>(scan_f32_kernel<N>);
+    return reinterpret_cast<const void*>(scan_f32_kernel<T, N>);
 }
 
-const void* pick_kernel(unsigned state) {
+template <typename T>
+const void* pick_kernel_t(unsigned state) {
     switch (state) {
-    case 1: return scan_kernel_ptr<1>();
-    case 2: return scan_kernel_ptr<2>();
-    case 4: return scan_kernel_ptr<4>();
-    case 8: return scan_kernel_ptr<8>();
-    case 16: return scan_kernel_ptr<16>();
-    default: return scan_kernel_ptr<32>();
+    case 1: return scan_kernel_ptr<T, 1>();
+    case 2: return scan_kernel_ptr<T, 2>();
+    case 4: return scan_kernel_ptr<T, 4>();
+    case 8: return scan_kernel_ptr<T, 8>();
+    case 16: return scan_kernel_ptr<T, 16>();
+    default: return scan_kernel_ptr<T, 32>();
     }
 }
+
+const void* pick_kernel(unsigned state, bool half) { return half ? pick_kernel_t<__half>(state) : pick_kernel_t<float>(state); }
 
 unsigned long long total_checked(const CheckList& l) {
     unsigned long long n = 0;
@@ -377,8 +439,9 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     p.u = s.u; p.delta = s.delta; p.a = s.a; p.b = s.b; p.c = s.c; p.d = s.d; p.y = s.y;
     p.length = s.length; p.channels = s.channels; p.lanes = s.lanes;
     p.a_shared = s.a_shared; p.c_full = s.c_full; p.has_d = s.has_d;
-    p.vec_b = (reinterpret_cast<std::uintptr_t>(s.b) & 15u) == 0;
-    p.vec_c = (reinterpret_cast<std::uintptr_t>(s.c) & 15u) == 0;
+    const std::uintptr_t vec_align = s.half ? 7u : 15u; // four values per load
+    p.vec_b = (reinterpret_cast<std::uintptr_t>(s.b) & vec_align) == 0;
+    p.vec_c = (reinterpret_cast<std::uintptr_t>(s.c) & vec_align) == 0;
     p.check = s.check;
     // Chunks: enough (lane, chunk) threads for ~4 warps per SM scheduler, at
     // least 4 tokens per chunk, at most 64 chunks; one chunk when lanes suffice.
@@ -395,7 +458,14 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     const unsigned extra = check_blocks(total_checked(s.check), sm_count);
     const size_t smem = K > 1 ? static_cast<size_t>(kThreads) * s.state * sizeof(float2) : 0;
     void* args[] = {&p, &status};
-    return cudaLaunchKernel(pick_kernel(s.state), dim3(p.scan_blocks + extra), dim3(kThreads), args, smem, stream);
+    const void* fn = pick_kernel(s.state, s.half);
+    if (smem > 48 * 1024) {
+        // Also set by the kernel loader; repeated here so that a call before
+        // sacc_scan_load_kernels still launches.
+        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaLaunchKernel(fn, dim3(p.scan_blocks + extra), dim3(kThreads), args, smem, stream);
 }
 
 cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
@@ -403,25 +473,36 @@ cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_c
     return cudaGetLastError();
 }
 
-cudaError_t launch_finalize(float* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
+cudaError_t launch_finalize(void* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream,
+                            bool half) {
     const unsigned long long want = (count + kThreads * 8ull - 1) / (kThreads * 8ull);
     const unsigned long long cap = 4ull * static_cast<unsigned long long>(sm_count);
     const unsigned blocks = static_cast<unsigned>(want < 1 ? 1 : want > cap ? cap : want);
-    finalize_kernel<<<blocks, kThreads, 0, stream>>>(out, count, status);
+    if (half)
+        finalize_kernel<unsigned short, 0x7e00u><<<blocks, kThreads, 0, stream>>>(static_cast<unsigned short*>(out), count, status);
+    else
+        finalize_kernel<unsigned, 0x7fc00000u><<<blocks, kThreads, 0, stream>>>(static_cast<unsigned*>(out), count, status);
     return cudaGetLastError();
 }
 
 cudaError_t load_scan_f32_kernels(std::string& report) {
     struct Entry { const char* name; const void* fn; size_t smem; };
     const Entry kernels[] = {
-        {"scan_f32_n1", scan_kernel_ptr<1>(), kThreads * 1 * sizeof(float2)},
-        {"scan_f32_n2", scan_kernel_ptr<2>(), kThreads * 2 * sizeof(float2)},
-        {"scan_f32_n4", scan_kernel_ptr<4>(), kThreads * 4 * sizeof(float2)},
-        {"scan_f32_n8", scan_kernel_ptr<8>(), kThreads * 8 * sizeof(float2)},
-        {"scan_f32_n16", scan_kernel_ptr<16>(), kThreads * 16 * sizeof(float2)},
-        {"scan_f32_n32", scan_kernel_ptr<32>(), kThreads * 32 * sizeof(float2)},
+        {"scan_f32_n1", scan_kernel_ptr<float, 1>(), kThreads * 1 * sizeof(float2)},
+        {"scan_f32_n2", scan_kernel_ptr<float, 2>(), kThreads * 2 * sizeof(float2)},
+        {"scan_f32_n4", scan_kernel_ptr<float, 4>(), kThreads * 4 * sizeof(float2)},
+        {"scan_f32_n8", scan_kernel_ptr<float, 8>(), kThreads * 8 * sizeof(float2)},
+        {"scan_f32_n16", scan_kernel_ptr<float, 16>(), kThreads * 16 * sizeof(float2)},
+        {"scan_f32_n32", scan_kernel_ptr<float, 32>(), kThreads * 32 * sizeof(float2)},
+        {"scan_f16io_n1", scan_kernel_ptr<__half, 1>(), kThreads * 1 * sizeof(float2)},
+        {"scan_f16io_n2", scan_kernel_ptr<__half, 2>(), kThreads * 2 * sizeof(float2)},
+        {"scan_f16io_n4", scan_kernel_ptr<__half, 4>(), kThreads * 4 * sizeof(float2)},
+        {"scan_f16io_n8", scan_kernel_ptr<__half, 8>(), kThreads * 8 * sizeof(float2)},
+        {"scan_f16io_n16", scan_kernel_ptr<__half, 16>(), kThreads * 16 * sizeof(float2)},
+        {"scan_f16io_n32", scan_kernel_ptr<__half, 32>(), kThreads * 32 * sizeof(float2)},
         {"check", reinterpret_cast<const void*>(check_kernel), 0},
-        {"finalize", reinterpret_cast<const void*>(finalize_kernel), 0},
+        {"finalize", reinterpret_cast<const void*>(finalize_kernel<unsigned, 0x7fc00000u>), 0},
+        {"finalize_f16", reinterpret_cast<const void*>(finalize_kernel<unsigned short, 0x7e00u>), 0},
     };
     for (const auto& k : kernels) {
         cudaFuncAttributes attr{};

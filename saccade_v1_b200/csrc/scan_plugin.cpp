@@ -2,7 +2,8 @@
 //
 // The reference registers three IPluginV3 plugins, saccade::SelectiveScan v2,
 // saccade::CrossScanExpand v1 and saccade::CrossScanMerge v1
-// (src/scan_trt_plugin.cpp:69-455).  TensorRT itself is not available on this
+// (src/scan_trt_plugin.cpp:69-455); saccade::SelectiveScan v3 is the same
+// scan with FP16 activations (u, delta, B, C, y) for FP16 engines.  TensorRT itself is not available on this
 // platform, so the plugin's logic lives here behind a C ABI whose calls map
 // one to one onto the IPluginV3 methods; a thin TensorRT adapter (see
 // INTEGRATION.md) translates TensorRT's descriptor and field types into these
@@ -97,8 +98,16 @@ struct SaccScanPlugin {
     sacc::Op op;
     std::int32_t has_d, height, width;
     unsigned long long bound_context = 0; // 0: kernels not loaded for any context
+    bool half = false;                    // SelectiveScan v3: FP16 activations
     int inputs() const { return op == sacc::Op::scan ? 5 + has_d : 1; }
     std::string prefix() const { return std::string(SACC_PLUGIN_NAMESPACE) + "::" + sacc::identity_of(op).name + ": "; }
+    // Data type of tensor `pos` (inputs, then y, then status).
+    int32_t type_at(int pos) const {
+        if (pos == inputs() + 1) return SACC_TENSOR_INT32;
+        if (!half) return SACC_TENSOR_FLOAT;
+        if (pos == inputs()) return SACC_TENSOR_HALF;                         // y
+        return (pos == 2 || pos == 5) ? SACC_TENSOR_FLOAT : SACC_TENSOR_HALF; // A and D stay FP32
+    }
 };
 
 namespace sacc {
@@ -126,12 +135,15 @@ int plugin_guard(F&& body) {
 }
 
 // Why the descriptors break the plugin contract, or "" (reference :299-341).
+const char* type_name(int32_t t) { return t == SACC_TENSOR_HALF ? "FP16" : t == SACC_TENSOR_INT32 ? "INT32" : "FP32"; }
+
 std::string check(const SaccScanPlugin& p, const SaccTensorDesc* in, const SaccTensorDesc* out, SaccScanShape& scan,
                   SaccCrossScanShape& cross) {
     for (int i = 0; i < p.inputs(); ++i)
-        if (in[i].type != SACC_TENSOR_FLOAT || in[i].format != SACC_FORMAT_LINEAR)
-            return "input " + std::to_string(i) + " is not linear FP32";
-    if (out[0].type != SACC_TENSOR_FLOAT || out[0].format != SACC_FORMAT_LINEAR) return "output 0 is not linear FP32";
+        if (in[i].type != p.type_at(i) || in[i].format != SACC_FORMAT_LINEAR)
+            return "input " + std::to_string(i) + " is not linear " + type_name(p.type_at(i));
+    if (out[0].type != p.type_at(p.inputs()) || out[0].format != SACC_FORMAT_LINEAR)
+        return std::string("output 0 is not linear ") + type_name(p.type_at(p.inputs()));
     if (out[1].type != SACC_TENSOR_INT32 || out[1].format != SACC_FORMAT_LINEAR || !equal(out[1], {2}))
         return "status output is not linear INT32[2]";
     for (int i = 0; i < p.inputs(); ++i)
@@ -192,8 +204,12 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
         if (out == nullptr) throw PluginError{SACC_EINVAL, "sacc_plugin_create: out is required"};
         *out = nullptr;
         Op op;
+        bool half = false;
         if (name && !std::strcmp(name, SACC_PLUGIN_SCAN_NAME) && version && !std::strcmp(version, SACC_PLUGIN_SCAN_VERSION))
             op = Op::scan;
+        else if (name && !std::strcmp(name, SACC_PLUGIN_SCAN_NAME) && version &&
+                 !std::strcmp(version, SACC_PLUGIN_SCAN_F16_VERSION))
+            op = Op::scan, half = true;
         else if (name && !std::strcmp(name, SACC_PLUGIN_EXPAND_NAME) && version &&
                  !std::strcmp(version, SACC_PLUGIN_EXPAND_VERSION))
             op = Op::expand;
@@ -231,7 +247,7 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
         if (op == Op::merge && (value[0] < 1 || value[1] < 1))
             throw PluginError{SACC_EINVAL, who + "height and width must be positive"};
         *out = new SaccScanPlugin{op, op == Op::scan ? value[0] : 1, op == Op::merge ? value[0] : 0,
-                                  op == Op::merge ? value[1] : 0, 0};
+                                  op == Op::merge ? value[1] : 0, 0, half};
     });
 }
 
@@ -259,8 +275,8 @@ int sacc_plugin_output_types(const SaccScanPlugin* p, const int32_t* in_types, i
         if (!p) throw PluginError{SACC_EINVAL, "sacc_plugin_output_types: plugin is required"};
         if (nb_in != p->inputs() || nb_out != 2 || !in_types || !out_types) fail(p, "input or output count");
         for (std::int32_t i = 0; i < nb_in; ++i)
-            if (in_types[i] != SACC_TENSOR_FLOAT) fail(p, "input " + std::to_string(i) + " is not FP32");
-        out_types[0] = SACC_TENSOR_FLOAT;
+            if (in_types[i] != p->type_at(i)) fail(p, "input " + std::to_string(i) + " is not " + type_name(p->type_at(i)));
+        out_types[0] = p->type_at(nb_in);
         out_types[1] = SACC_TENSOR_INT32;
     });
 }
@@ -288,7 +304,7 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
             if (n < 1 || n > 32 || (n & (n - 1)) != 0) fail(p, "state must be a power of two in [1, 32]");
             if (rows > 1 && rows != channels) fail(p, "A rows must be 1 or channels");
             if (width > 1 && width != n) fail(p, "C width must be 1 or state");
-            out[0] = SaccTensorDesc{3, {u.dims[0], u.dims[1], u.dims[2]}, SACC_TENSOR_FLOAT, SACC_FORMAT_LINEAR};
+            out[0] = SaccTensorDesc{3, {u.dims[0], u.dims[1], u.dims[2]}, p->type_at(nb_in), SACC_FORMAT_LINEAR};
             return;
         }
         case Op::expand: {
@@ -308,10 +324,11 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
     });
 }
 
-// Dense row-major FP32 everywhere except the INT32 status output (:163-167).
+// Dense row-major FP32 everywhere except the INT32 status output (:163-167);
+// v3: FP16 u, delta, B, C and y.
 int sacc_plugin_supports_format(const SaccScanPlugin* p, int32_t pos, const SaccTensorDesc* io, int32_t nb_in, int32_t nb_out) {
     if (!p || !io || nb_in != p->inputs() || nb_out != 2 || pos < 0 || pos >= nb_in + nb_out) return 0;
-    return io[pos].format == SACC_FORMAT_LINEAR && io[pos].type == (pos == nb_in + 1 ? SACC_TENSOR_INT32 : SACC_TENSOR_FLOAT);
+    return io[pos].format == SACC_FORMAT_LINEAR && io[pos].type == p->type_at(pos);
 }
 
 size_t sacc_plugin_workspace_size(const SaccScanPlugin*) { return 0; }
@@ -359,10 +376,18 @@ int sacc_plugin_enqueue(const SaccScanPlugin* p, const SaccTensorDesc* in_desc, 
         int rc = SACC_OK;
         switch (p->op) {
         case Op::scan: {
-            const SaccScanInputs ins{static_cast<const float*>(in[0]), static_cast<const float*>(in[1]),
-                                     static_cast<const float*>(in[2]), static_cast<const float*>(in[3]),
-                                     static_cast<const float*>(in[4]), p->has_d ? static_cast<const float*>(in[5]) : nullptr};
-            rc = sacc_selective_scan_f32(&scan, &ins, static_cast<float*>(out[0]), status, stream);
+            const auto* d = p->has_d ? static_cast<const float*>(in[5]) : nullptr;
+            if (p->half) {
+                const SaccScanInputsF16 ins{static_cast<const std::uint16_t*>(in[0]), static_cast<const std::uint16_t*>(in[1]),
+                                            static_cast<const float*>(in[2]), static_cast<const std::uint16_t*>(in[3]),
+                                            static_cast<const std::uint16_t*>(in[4]), d};
+                rc = sacc_selective_scan_f16(&scan, &ins, static_cast<std::uint16_t*>(out[0]), status, stream);
+            } else {
+                const SaccScanInputs ins{static_cast<const float*>(in[0]), static_cast<const float*>(in[1]),
+                                         static_cast<const float*>(in[2]), static_cast<const float*>(in[3]),
+                                         static_cast<const float*>(in[4]), d};
+                rc = sacc_selective_scan_f32(&scan, &ins, static_cast<float*>(out[0]), status, stream);
+            }
             break;
         }
         case Op::expand:

@@ -13,9 +13,10 @@ import ctypes
 from . import _lib
 
 FIELD_INT32, FIELD_OTHER = 1, 0
-TENSOR_FLOAT, TENSOR_INT32, TENSOR_OTHER = 0, 3, 99
+TENSOR_FLOAT, TENSOR_HALF, TENSOR_INT32, TENSOR_OTHER = 0, 1, 3, 99
 FORMAT_LINEAR, FORMAT_OTHER = 0, 99
 SCAN, EXPAND, MERGE = ("SelectiveScan", "2"), ("CrossScanExpand", "1"), ("CrossScanMerge", "1")
+SCAN_F16 = ("SelectiveScan", "3")  # FP16 u, delta, B, C, y; FP32 A, D
 
 
 class PluginError(ValueError):

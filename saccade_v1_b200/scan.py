@@ -98,6 +98,17 @@ def selective_scan_cuda(shape: SelectiveScanShape, u, delta, a, b, c, d, y, stat
                                      _stream_handle(stream)))
 
 
+def selective_scan_f16(shape: SelectiveScanShape, u, delta, a, b, c, d, y, status, stream=None) -> None:
+    """The same operator with FP16 activations (plugin SelectiveScan v3): u,
+    delta, b, c and y float16 tensors, a and d float32.  y is the FP32 path's
+    output on the widened inputs rounded to nearest FP16; an output FP16
+    cannot hold sets SACC_SCAN_OUTPUT_RANGE."""
+    L = _lib.load()
+    ins = _lib.ScanInputsF16(_ptr(u), _ptr(delta), _ptr(a), _ptr(b), _ptr(c), _ptr(d))
+    _check(L.sacc_selective_scan_f16(ctypes.byref(shape.c()), ctypes.byref(ins), _ptr(y), _ptr(status),
+                                     _stream_handle(stream)))
+
+
 @dataclass
 class CrossScanShape:
     batch: int = 0

@@ -4,8 +4,8 @@ that happen before any GPU work (reference src/scan_trt_plugin.cpp and its
 tests/scan_trt_tests.cpp contract group)."""
 import pytest
 
-from saccade_v1_b200.plugin import (EXPAND, FIELD_OTHER, FORMAT_LINEAR, FORMAT_OTHER, MERGE, SCAN, TENSOR_FLOAT, TENSOR_INT32,
-                                    TENSOR_OTHER, PluginError, ScanPlugin, TensorDesc)
+from saccade_v1_b200.plugin import (EXPAND, FIELD_OTHER, FORMAT_LINEAR, FORMAT_OTHER, MERGE, SCAN, SCAN_F16, TENSOR_FLOAT,
+                                    TENSOR_HALF, TENSOR_INT32, TENSOR_OTHER, PluginError, ScanPlugin, TensorDesc)
 
 
 def test_creator_accepts_exactly_the_advertised_fields():
@@ -35,8 +35,8 @@ def test_creator_rejections(fields, msg):
 def test_merge_creator_rejections_and_unknown_plugin():
     with pytest.raises(PluginError, match="height and width must be positive"):
         ScanPlugin.create(*MERGE, [("height", 0), ("width", 4)])
-    with pytest.raises(PluginError, match="plugin creator not registered: saccade::SelectiveScan v3"):
-        ScanPlugin.create("SelectiveScan", "3", [("has_d", 1)])
+    with pytest.raises(PluginError, match="plugin creator not registered: saccade::SelectiveScan v4"):
+        ScanPlugin.create("SelectiveScan", "4", [("has_d", 1)])
 
 
 def test_output_types_and_shapes():
@@ -86,3 +86,39 @@ def test_enqueue_rejects_before_any_gpu_work():
         p.enqueue(descs, outs, ptrs, [0x9000, 0xA000], 0x5EED)
     q = p.clone()
     assert q.fields() == {"has_d": 1}
+
+
+H, F, I = TENSOR_HALF, TENSOR_FLOAT, TENSOR_INT32
+
+
+@pytest.mark.parametrize("has_d", [0, 1])
+def test_fp16_version_types_and_formats(has_d):
+    """SelectiveScan v3: the same creator fields and shape rules as v2, FP16 u,
+    delta, B, C and y, FP32 A and D, INT32 status."""
+    p = ScanPlugin.create(*SCAN_F16, [("has_d", has_d)])
+    assert p.fields() == {"has_d": has_d}
+    ins = [H, H, F, H, H] + [F] * has_d
+    assert p.output_types(ins) == [H, I]
+    with pytest.raises(PluginError, match="input 0 is not FP16"):
+        p.output_types([F] + ins[1:])
+    with pytest.raises(PluginError, match="input 2 is not FP32"):
+        p.output_types(ins[:2] + [H] + ins[3:])
+    n = len(ins)
+    io = [TensorDesc.of((1,), t) for t in ins] + [TensorDesc.of((1,), H), TensorDesc.of((2,), I)]
+    assert all(p.supports_format(i, io, n) for i in range(n + 2))
+    for pos, wrong in [(0, F), (2, H), (n, F), (n + 1, H)] + ([(5, H)] if has_d else []):
+        bad = list(io)
+        bad[pos] = TensorDesc.of((1,), wrong)
+        assert not p.supports_format(pos, bad, n), pos
+    dims = [(4, 240, 256), (4, 240, 256), (1, 16), (4, 240, 16), (4, 240, 1)] + [(256,)] * has_d
+    assert p.output_shapes(dims) == [(4, 240, 256), (2,)]
+    assert p.workspace_size() == 0
+
+
+def test_fp16_version_enqueue_rejects_fp32_descriptors():
+    p = ScanPlugin.create(*SCAN_F16, [("has_d", 1)])
+    dims = [(4, 9, 8), (4, 9, 8), (1, 4), (4, 9, 4), (4, 9, 1), (8,)]
+    descs = [TensorDesc.of(d) for d in dims]
+    outs = [TensorDesc.of((4, 9, 8), H), TensorDesc.of((2,), I)]
+    with pytest.raises(PluginError, match="kernels are not loaded|input 0 is not linear FP16|explicit non-default stream"):
+        p.enqueue(descs, outs, [0x1000] * 6, [0x2000, 0x3000], 0x5EED)

@@ -16,7 +16,8 @@ if not torch.cuda.is_available():
 
 import gpu_util as gu  # noqa: E402
 import saccade_v1_b200 as sb  # noqa: E402
-from saccade_v1_b200.plugin import EXPAND, MERGE, SCAN, TENSOR_INT32, PluginError, ScanPlugin, TensorDesc  # noqa: E402
+from saccade_v1_b200.plugin import (EXPAND, MERGE, SCAN, SCAN_F16, TENSOR_FLOAT, TENSOR_HALF, TENSOR_INT32,  # noqa: E402
+                                    PluginError, ScanPlugin, TensorDesc)
 
 
 def descs_for(k):
@@ -96,3 +97,37 @@ def test_plugins_chain_expand_scan_merge():
     k2.u = oracle.cross_scan_expand(x, 1, C, H, W)
     y2, _ = gu.run_f32(k2)
     assert np.array_equal(y.cpu().numpy().view(np.uint32), y2.view(np.uint32))
+
+
+@pytest.mark.parametrize("bad", [False, True])
+def test_fp16_plugin_enqueue_is_bitwise_the_direct_api(bad):
+    """SelectiveScan v3 (FP16 u, delta, B, C, y; FP32 A, D) enqueues the same
+    bits and status words as sacc_selective_scan_f16."""
+    k = random_case(Shape(4, 240, 256, 16, 1, 1, True), 0x5eed0610)
+    if bad:
+        k.delta[17] = np.inf
+    p = ScanPlugin.create(*SCAN_F16, [("has_d", 1)])
+    p.bind()
+    s = gu.stream()
+    sh = sb.SelectiveScanShape(4, 240, 256, 16, 1, 1, True)
+    with torch.cuda.stream(s):
+        h = lambda x: torch.from_numpy(x).cuda().half()
+        f = lambda x: torch.from_numpy(x).cuda()
+        ins = [h(k.u), h(k.delta), f(k.a), h(k.b), h(k.c), f(k.d)]
+        y = torch.empty(k.u.size, dtype=torch.float16, device="cuda")
+        st = gu.new_status()
+        ind, outd = descs_for(k)
+        for i in (0, 1, 3, 4):
+            ind[i].type = TENSOR_HALF
+        outd[0].type = TENSOR_HALF
+        p.enqueue(ind, outd, [t.data_ptr() for t in ins], [y.data_ptr(), st.data_ptr()], s)
+        y2 = torch.empty_like(y)
+        st2 = gu.new_status()
+        sb.selective_scan_f16(sh, *ins, y2, st2, stream=s)
+    s.synchronize()
+    assert gu.status_words(st) == gu.status_words(st2)
+    assert (gu.status_words(st)[0] != 0) == bad
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    ind[0].type = TENSOR_FLOAT
+    with pytest.raises(PluginError, match="input 0 is not linear FP16"):
+        p.enqueue(ind, outd, [t.data_ptr() for t in ins], [y.data_ptr(), st.data_ptr()], s)

@@ -111,7 +111,12 @@ cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);
 cudaError_t read_step_fault(unsigned* out, bool clear);
-cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs = nullptr);
+// `scratch` (optional, 16-byte aligned): lets few-unit long-sequence calls run
+// the chunk-parallel scan as one fused launch; bulk_scan_scratch_bytes() says
+// how much this call would use (0: none).
+cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs = nullptr,
+                             void* scratch = nullptr, std::size_t scratch_bytes = 0);
+std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
 cudaError_t read_bulk_fault(unsigned* out, bool clear);

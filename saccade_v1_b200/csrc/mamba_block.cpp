@@ -27,8 +27,25 @@ namespace sacc {
 namespace {
 
 struct Layout {
-    std::size_t r, wn, wx, xz, u, dbc, delta, y, total;
+    std::size_t r, wn, wx, xz, u, dbc, delta, y, scan, scan_bytes, total;
 };
+
+// Batch rows per scan call, so that each call stays within the int32
+// element capacity.
+std::uint64_t scan_rows(const SaccMambaBlockArgs& a) {
+    const std::uint64_t per_seq = a.length * a.d_inner;
+    std::uint64_t chunk = a.batch;
+    while (chunk > 1 && chunk * per_seq * 2 > kMaxElements) chunk = (chunk + 1) / 2;
+    return chunk;
+}
+
+// The scan's arguments for `nb` rows of the block (pointers left null).
+SaccScanExArgs scan_shape(const SaccMambaBlockArgs& a, std::uint64_t nb) {
+    SaccScanExArgs s{};
+    s.batch = nb; s.length = a.length; s.channels = a.d_inner; s.state = a.d_state; s.groups = 1; s.a_rows = a.d_inner;
+    s.c_width = a.d_state; s.layout = SACC_LAYOUT_BLD; s.dtype = a.dtype; s.delta_softplus = 1; s.nseq = 0;
+    return s;
+}
 
 std::size_t align256(std::size_t v) { return (v + 255) & ~std::size_t(255); }
 
@@ -50,6 +67,9 @@ Layout plan(const SaccMambaBlockArgs& a) {
     l.dbc = take(M * (R + 2 * N) * e);
     l.delta = take(M * D * e);
     l.y = take(M * D * e);
+    // Scratch of the scan's fused chunk-parallel mode (few long sequences).
+    l.scan_bytes = bulk_scan_scratch_bytes(scan_shape(a, a.batch < scan_rows(a) ? a.batch : scan_rows(a)));
+    l.scan = l.scan_bytes ? take(l.scan_bytes) : 0;
     l.total = off;
     return l;
 }
@@ -117,22 +137,19 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
     // read in place through their row pitches; chunked by batch so that each
     // call stays within the int32 element capacity.
     const RowStrides pitch{2 * D, W, W};
-    const std::uint64_t per_seq = a.length * D;
-    std::uint64_t chunk = a.batch;
-    while (chunk > 1 && chunk * per_seq * 2 > kMaxElements) chunk = (chunk + 1) / 2;
+    const std::uint64_t chunk = scan_rows(a);
     for (std::uint64_t b0 = 0; b0 < a.batch; b0 += chunk) {
         const std::uint64_t nb = (a.batch - b0 < chunk) ? a.batch - b0 : chunk;
         const std::size_t tok = b0 * a.length;
-        SaccScanExArgs s{};
-        s.batch = nb; s.length = a.length; s.channels = D; s.state = N; s.groups = 1; s.a_rows = D; s.c_width = N;
-        s.layout = SACC_LAYOUT_BLD; s.dtype = dt_; s.delta_softplus = 1; s.nseq = 0;
+        SaccScanExArgs s = scan_shape(a, nb);
         s.u = at(u, tok * D); s.delta = at(delta, tok * D);
         s.z = at(xz, tok * 2 * D + D);
         s.b = at(dbc, tok * W + R); s.c = at(dbc, tok * W + R + N);
         s.a = a.a; s.d = a.d; s.delta_bias = a.dt_bias;
         s.y = static_cast<unsigned char*>(y) + tok * D * e;
         if (!bulk_eligible(s, &pitch)) return cudaErrorInvalidValue; // shapes are checked by the caller
-        if ((err = launch_scan_bulk(s, stream, &pitch)) != cudaSuccess) return err;
+        if ((err = launch_scan_bulk(s, stream, &pitch, l.scan_bytes ? ws + l.scan : nullptr, l.scan_bytes)) != cudaSuccess)
+            return err;
     }
 
     // out_proj + residual.

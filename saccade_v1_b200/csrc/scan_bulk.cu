@@ -50,12 +50,13 @@ constexpr int kT = 32;      // tokens per chunk
 constexpr int kStages = 2;
 constexpr int kN = 16;
 constexpr int kMinBlocks = 4; // four CTAs per SM: 128 registers per thread
+constexpr int kMaxFusedParts = 32;
 
 // One item of work: 128 channels of one row (or packed sequence) over the
 // chunk range of one part, with the tensor-map coordinates of the unit.
 struct Item {
     unsigned long long b, d0, tok0, len;
-    int c0, c1, part, row0, bb, brow0, crow0;
+    int c0, c1, part, pass, row0, bb, brow0, crow0;
 };
 
 // The producer's position in a CTA's list of (item, chunk) loads.
@@ -100,7 +101,9 @@ struct BulkParams {
     int a_shared, c_full, has_d, softplus, nchunks;
     int parts;                   // chunk ranges per unit (> 1: split launch, cooperative, or chunk-parallel phases)
     int phase;                   // 0 one pass; chunk-parallel: 1 local pass (parts from zero), 2 final pass
+    int passes;                  // 2: fused chunk-parallel launch (pass 0 local, pass 1 final, one CTA per part)
     unsigned long long item0;    // first item of this launch (the final pass starts at part 1)
+    float* scratch;              // fused mode: per (unit, part) 17 x 128 floats (S, sum of Delta), then the flags
 };
 
 
@@ -271,7 +274,13 @@ __device__ __forceinline__ Item item_at(const BulkParams& p, unsigned long long 
     // below 2^31 (64-bit divisions would sit on every CTA's start-up path).
     const unsigned long long D = p.channels, L = p.length;
     const unsigned tiles = static_cast<unsigned>(D / kLanes), units = static_cast<unsigned>(p.units);
-    const unsigned it32 = static_cast<unsigned>(it);
+    unsigned it32 = static_cast<unsigned>(it);
+    w.pass = 0;
+    if (p.passes > 1) {
+        const unsigned per_pass = units * static_cast<unsigned>(p.parts);
+        w.pass = static_cast<int>(it32 / per_pass);
+        it32 %= per_pass;
+    }
     const unsigned u = it32 % units;
     w.part = static_cast<int>(it32 / units);
     w.b = u / tiles;
@@ -291,6 +300,9 @@ __device__ __forceinline__ Item item_at(const BulkParams& p, unsigned long long 
     const int nch = (!kBDL && p.cu) ? static_cast<int>((w.len + kT - 1) / kT) : p.nchunks;
     w.c0 = p.parts == 1 ? 0 : static_cast<int>(static_cast<unsigned>(w.part * nch) / static_cast<unsigned>(p.parts));
     w.c1 = p.parts == 1 ? nch : static_cast<int>(static_cast<unsigned>((w.part + 1) * nch) / static_cast<unsigned>(p.parts));
+    // Fused mode: part 0's local pass is final (no second pass), the last
+    // part's local pass is not needed (no part after it).
+    if (p.passes > 1 && (w.pass == 1 ? w.part == 0 : w.part + 1 == p.parts)) w.c1 = w.c0;
     w.row0 = kBDL ? static_cast<int>(w.b * D + w.d0) : static_cast<int>(w.d0);
     w.bb = (!kBDL && p.cu) ? 0 : static_cast<int>(w.b);
     w.brow0 = kBDL ? static_cast<int>((w.b * p.groups + g) * kN) : static_cast<int>(g * kN);
@@ -303,7 +315,7 @@ __device__ __forceinline__ Item item_at(const BulkParams& p, unsigned long long 
 template <bool kBDL, bool kFullC>
 __device__ __forceinline__ void cursor_next(Cursor& c, const BulkParams& p) {
     if (++c.chunk < c.w.c1) return;
-    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts);
+    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts) * p.passes;
     for (c.it += gridDim.x; c.it < items; c.it += gridDim.x) {
         c.w = item_at<kBDL, kFullC>(p, c.it);
         if (c.w.c1 > c.w.c0) {
@@ -410,7 +422,57 @@ __device__ __forceinline__ unsigned long long flag_acquire(const unsigned long l
     return v;
 }
 
-// With kLoop each CTA walks items blockIdx.x, blockIdx.x + gridDim.x, ... (a
+// Fused chunk-parallel mode (scratch): flag of part k of w's unit, after the
+// units x parts x 17 x 128 floats of the (state, sum of Delta) records.
+__device__ __forceinline__ unsigned long long* fused_flag(const BulkParams& p, const Item& w, int k) {
+    const unsigned long long unit = w.b * (p.channels / kLanes) + w.d0 / kLanes;
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(p.scratch + p.units * p.parts * (kN + 1) * kLanes);
+    return flags + unit * p.parts + k;
+}
+
+// The true initial state of part w.part >= 1 from the local records of parts
+// 0 .. part - 1: H_1 = S_0, H_{j+1} = exp2(a sum Delta_j) H_j + S_j (the
+// recurrence is linear in h, and a part's per-token decays multiply to one
+// exponential of the summed exponents).  Thread j < part first waits (bounded)
+// for part j's flag; false when a wait ran out.  Records are loaded two
+// parts at a time.
+__device__ __forceinline__ bool fused_prefix(const BulkParams& p, const Item& w, int tid, const float (&a)[kN], float (&h)[kN]) {
+    bool ready = true;
+    if (tid < w.part) {
+        const unsigned long long* f = fused_flag(p, w, tid);
+        ready = false;
+        for (std::uint32_t i = 0; i < (1u << 24); ++i) {
+            if (flag_acquire(f) == p.epoch) {
+                ready = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!__syncthreads_and(ready)) return false;
+    const unsigned long long unit = w.b * (p.channels / kLanes) + w.d0 / kLanes;
+    const float* rec = p.scratch + unit * p.parts * (kN + 1) * kLanes + tid;
+#pragma unroll
+    for (int n = 0; n < kN; ++n) h[n] = __ldcg(rec + n * kLanes); // S_0: part 0 ran from h0
+    constexpr int kBatch = 2;
+    for (int j0 = 1; j0 < w.part; j0 += kBatch) {
+        float sv[kBatch][kN + 1];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+            if (j0 + q < w.part)
+#pragma unroll
+                for (int n = 0; n <= kN; ++n) sv[q][n] = __ldcg(rec + ((j0 + q) * (kN + 1) + n) * kLanes);
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+            if (j0 + q < w.part)
+#pragma unroll
+                for (int n = 0; n < kN; ++n) h[n] = fmaf(fast_exp2(sv[q][kN] * a[n]), h[n], sv[q][n]);
+    }
+    return true;
+}
+
+// kMode 0: one item per CTA; 1 (split launch) and 2 (fused chunk-parallel
+// launch, kLoop below) walk a list.  With kLoop each CTA walks items blockIdx.x, blockIdx.x + gridDim.x, ... (a
 // one-wave grid for split launches: parts > 1, cooperative so that every CTA
 // is resident, an item's part k waiting on part k - 1 of the same unit one
 // round earlier); without it a CTA takes exactly its own item (plain and
@@ -418,7 +480,7 @@ __device__ __forceinline__ unsigned long long flag_acquire(const unsigned long l
 // faster on one-chunk items).  Thread 0 keeps kStages chunk loads in
 // flight along the CTA's whole list, so the next item's first chunks arrive
 // while the current item computes.
-template <typename T, bool kBDL, bool kHasZ, bool kFullC, bool kLoop>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode>
 __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
                                                                   const __grid_constant__ CUtensorMap tm_d,
                                                                   const __grid_constant__ CUtensorMap tm_z,
@@ -433,7 +495,8 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     const unsigned long long D = p.channels;
     const int cw = kFullC ? kN : 1;
     const std::uint32_t c_bytes = static_cast<std::uint32_t>(cw) * kT * sizeof(T);
-    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts);
+    constexpr bool kLoop = kMode != 0;
+    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts) * (kMode == 2 ? 2u : 1u);
 
     if (tid == 0) {
         prefetch_tensor_map(&tm_u);
@@ -478,9 +541,18 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         const float dskip = p.has_d ? p.d[d] : 0.0f;
         const float bias = p.bias ? p.bias[d] : 0.0f;
         float dtsum = 0.0f; // sum of Delta over the part (chunk-parallel local pass)
+        if (kMode == 2 && w.c1 == w.c0) continue; // a pass the fused mode skips
         if (w.part == 0) {
 #pragma unroll
             for (int n = 0; n < kN; ++n) h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
+        } else if (kMode == 2) {
+            if (w.pass == 0) {
+#pragma unroll
+                for (int n = 0; n < kN; ++n) h[n] = 0.0f; // local pass from zero
+            } else if (!fused_prefix(p, w, tid, a, h)) {
+                fault = true;
+                break;
+            }
         } else if (p.phase == 1) {
 #pragma unroll
             for (int n = 0; n < kN; ++n) h[n] = 0.0f; // local pass: from zero, corrected by the final pass
@@ -552,14 +624,16 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                                                  static_cast<unsigned long long>(chunk) * kT,
                                              p.zld, d, tid, q, valid - q * 8, blk);
                 float out[8];
-                scan_block8<kFullC, kHasZ, true, !kLoop>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out, dtsum);
+                scan_block8<kFullC, kHasZ, true, kMode != 1>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out,
+                                                            dtsum);
                 if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
                 else store_block_bld<T>(sm.y, tid, q, out);
             }
             fence_async_shared();
             __syncthreads();
             const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
-            const bool write_y = !(p.phase == 1 && w.part > 0); // local-pass outputs are not final
+            // Local-pass outputs (parts after the first) are not final.
+            const bool write_y = !((p.phase == 1 || (kMode == 2 && w.pass == 0)) && w.part > 0);
             const bool tail = !kBDL && p.cu && valid < kT;
             if (tail && write_y) {
                 // A packed sequence's partial last chunk: a tile store would also
@@ -583,7 +657,23 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             }
         }
         if (fault) break;
-        if (p.phase == 1) {
+        if (kMode == 2) {
+            if (w.pass == 0) {
+                // Local pass: the part's end state and its sum of Delta to the
+                // scratch, then this part's flag.
+                float* out = p.scratch + (static_cast<unsigned long long>(w.b * (D / kLanes) + w.d0 / kLanes) * p.parts + w.part) *
+                                             (kN + 1) * kLanes + tid;
+#pragma unroll
+                for (int n = 0; n < kN; ++n) out[n * kLanes] = h[n];
+                out[kN * kLanes] = dtsum;
+                __threadfence();
+                __syncthreads();
+                if (tid == 0) flag_release(fused_flag(p, w, w.part), p.epoch);
+            } else if (p.h_final && w.part + 1 == p.parts) {
+#pragma unroll
+                for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
+            }
+        } else if (p.phase == 1) {
             // Local pass: the part's end state and its sum of Delta go to the
             // next part's first outputs for the combine (the last part's are
             // not needed).
@@ -655,9 +745,9 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, bool kBDL, bool kHasZ, bool kFullC, bool kLoop>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode>
 struct Variant {
-    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kLoop>); }
+    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kMode>); }
     static cudaError_t prepare() {
         static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                                static_cast<int>(smem_bytes<T, kBDL && kHasZ>()));
@@ -706,25 +796,30 @@ struct Pick {
 };
 
 template <typename T, bool kBDL, bool kHasZ, bool kFullC>
-Pick make_pick(bool loop) {
-    if (loop) {
-        using V = Variant<T, kBDL, kHasZ, kFullC, true>;
+Pick make_pick(int mode) {
+    if (mode == 1) {
+        using V = Variant<T, kBDL, kHasZ, kFullC, 1>;
         return {V::fn(), V::smem(), &V::prepare};
     }
-    using V = Variant<T, kBDL, kHasZ, kFullC, false>;
+    if (mode == 2) {
+        using V = Variant<T, kBDL, kHasZ, kFullC, 2>;
+        return {V::fn(), V::smem(), &V::prepare};
+    }
+    using V = Variant<T, kBDL, kHasZ, kFullC, 0>;
     return {V::fn(), V::smem(), &V::prepare};
 }
 
 template <typename T, bool kBDL>
-Pick pick_z(bool z, bool full_c, bool loop) {
-    if (z) return full_c ? make_pick<T, kBDL, true, true>(loop) : make_pick<T, kBDL, true, false>(loop);
-    return full_c ? make_pick<T, kBDL, false, true>(loop) : make_pick<T, kBDL, false, false>(loop);
+Pick pick_z(bool z, bool full_c, int mode) {
+    if (z) return full_c ? make_pick<T, kBDL, true, true>(mode) : make_pick<T, kBDL, true, false>(mode);
+    return full_c ? make_pick<T, kBDL, false, true>(mode) : make_pick<T, kBDL, false, false>(mode);
 }
 
-Pick pick(int dtype, bool bdl, bool z, bool full_c, bool loop) {
+// mode 0: one item per CTA; 1: split launch; 2: fused chunk-parallel launch.
+Pick pick(int dtype, bool bdl, bool z, bool full_c, int mode) {
     if (dtype == SACC_DTYPE_BF16)
-        return bdl ? pick_z<__nv_bfloat16, true>(z, full_c, loop) : pick_z<__nv_bfloat16, false>(z, full_c, loop);
-    return bdl ? pick_z<__half, true>(z, full_c, loop) : pick_z<__half, false>(z, full_c, loop);
+        return bdl ? pick_z<__nv_bfloat16, true>(z, full_c, mode) : pick_z<__nv_bfloat16, false>(z, full_c, mode);
+    return bdl ? pick_z<__half, true>(z, full_c, mode) : pick_z<__half, false>(z, full_c, mode);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
@@ -792,6 +887,26 @@ int chunk_parts(unsigned long long units, unsigned long long sms, int nchunks, u
     return k >= 3 ? static_cast<int>(k) : 0; // two passes over 2/K of the sequence: below 3 parts no gain
 }
 
+// Parts for the fused chunk-parallel mode (one cooperative launch with a
+// scratch buffer for the parts' records, so parts of one chunk are allowed
+// and any L): launches that leave most SMs idle (units at most a quarter of
+// the SMs), K = as many whole-chunk parts as resident CTAs allow (at most 32),
+// when two passes over the longest part plus about one chunk of hand-off
+// beat the sequential walk; 0 when the mode does not apply.
+int fused_parts(unsigned long long units, unsigned long long sms, unsigned long long wave, int nchunks) {
+    if (units == 0 || units * 4 > sms || nchunks < 4) return 0;
+    unsigned long long k = wave / units;
+    if (k > static_cast<unsigned long long>(nchunks)) k = static_cast<unsigned long long>(nchunks);
+    if (k > static_cast<unsigned long long>(kMaxFusedParts)) k = kMaxFusedParts;
+    if (k < 2) return 0;
+    const unsigned long long longest = (static_cast<unsigned long long>(nchunks) + k - 1) / k;
+    return 2 * longest + 1 < static_cast<unsigned long long>(nchunks) ? static_cast<int>(k) : 0;
+}
+
+std::size_t fused_scratch_bytes(unsigned long long units, int parts) {
+    return static_cast<std::size_t>(units) * static_cast<std::size_t>(parts) * ((kN + 1) * kLanes * sizeof(float) + 8);
+}
+
 // A value no earlier split launch of this process used, never zero: the
 // hand-off flags in the output are compared against it.
 unsigned long long next_epoch() {
@@ -844,7 +959,30 @@ bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
     return rows <= 0x7fffffffull && tokens <= 0x7fffffffull && a.batch * a.groups * kN <= 0x7fffffffull;
 }
 
-cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs) {
+namespace {
+// Parts of the fused chunk-parallel mode for this call on the current device
+// (0: it does not apply), and the variant it would use.
+int fused_plan(const SaccScanExArgs& a, Pick& k) {
+    if (a.cu_seqlens != nullptr) return 0;
+    const bool bdl = a.layout == SACC_LAYOUT_BDL;
+    k = pick(a.dtype, bdl, a.z != nullptr, a.c_width != 1, 2);
+    if (k.prepare() != cudaSuccess) return 0;
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned long long units = a.batch * (a.channels / kLanes);
+    return fused_parts(units, static_cast<unsigned long long>(sms), resident_ctas(k),
+                       static_cast<int>((a.length + kT - 1) / kT));
+}
+} // namespace
+
+std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a) {
+    Pick k{};
+    const int parts = fused_plan(a, k);
+    return parts ? fused_scratch_bytes(a.batch * (a.channels / kLanes), parts) : 0;
+}
+
+cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs, void* scratch,
+                             std::size_t scratch_bytes) {
     const RowStrides dense{0, 0, 0};
     if (!rs) rs = &dense;
     const bool bdl = a.layout == SACC_LAYOUT_BDL;
@@ -890,6 +1028,32 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     // launches that fit one wave or gain nothing from a split: one item per CTA.
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    p.passes = 1;
+    if (scratch != nullptr) {
+        Pick fk{};
+        const int fused = fused_plan(a, fk);
+        if (fused && scratch_bytes >= fused_scratch_bytes(p.units, fused) &&
+            (reinterpret_cast<std::uintptr_t>(scratch) & 15u) == 0) {
+            // Few units over long sequences, with scratch: every part's local
+            // pass, hand-off and final pass in one cooperative launch (every
+            // CTA resident: a part waits on the flags of the parts before it).
+            p.parts = fused;
+            p.passes = 2;
+            p.scratch = static_cast<float*>(scratch);
+            p.epoch = next_epoch();
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(static_cast<unsigned>(p.units * fused));
+            cfg.blockDim = dim3(kLanes);
+            cfg.dynamicSmemBytes = fk.smem;
+            cfg.stream = stream;
+            cudaLaunchAttribute attrs[2]{};
+            attrs[0].id = cudaLaunchAttributeCooperative;
+            attrs[0].val.cooperative = 1;
+            cfg.attrs = attrs;
+            cfg.numAttrs = 1;
+            return cudaLaunchKernelExC(&cfg, fk.fn, args);
+        }
+    }
     const int chunked = p.cu ? 0 : chunk_parts(p.units, static_cast<unsigned long long>(sms), p.nchunks, L);
     if (chunked) {
         // Few units over long sequences: the chunk-parallel passes (stream

@@ -6,6 +6,10 @@ multiply :235, add :248) plus BASELINE's RMSNorm prologue (not in the
 reference), computing in float64 and rounding to the activation dtype exactly
 where the device pipeline stores an activation (x_in, z, u, dt, B, C, delta,
 y, out), so that the comparison measures arithmetic, not storage choices.
+(For dt_rank 8 or 16 the device forms delta inside the scan in FP32 and does
+not store it, except in its fused chunk-parallel mode; the oracle still rounds
+delta there, a perturbation below half an FP16 / BF16 ulp of delta that the
+tests' 1e-3 + 1e-2 |ref| tolerance covers.)
 The scan itself is the C oracle (oracle/scan_oracle.c), pinned to the
 reference build.
 """

@@ -111,12 +111,22 @@ cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);
 cudaError_t read_step_fault(unsigned* out, bool clear);
+// delta formed inside the scan as dt (rows of pitch `ld` elements, `rank`
+// columns) x w^T (w: channels x rank), for rank 8 or 16 with the (B, L, D)
+// layout, a gate and a full-width C (the block's small dt_proj).
+struct DtFusion {
+    const void* dt;
+    unsigned long long ld;
+    const void* w;
+    int rank;
+};
+bool dt_fusable(const SaccScanExArgs& a, const DtFusion& f);
 // `scratch` (optional, 16-byte aligned): lets few-unit long-sequence calls run
 // the chunk-parallel scan as one fused launch; bulk_scan_scratch_bytes() says
 // how much this call would use (0: none).
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs = nullptr,
-                             void* scratch = nullptr, std::size_t scratch_bytes = 0);
-std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a);
+                             void* scratch = nullptr, std::size_t scratch_bytes = 0, const DtFusion* dtf = nullptr);
+std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf = nullptr);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
 cudaError_t read_bulk_fault(unsigned* out, bool clear);

@@ -28,6 +28,7 @@ namespace {
 
 struct Layout {
     std::size_t r, wn, wx, xz, u, dbc, delta, y, scan, scan_bytes, total;
+    bool fuse_dt; // dt_proj inside the scan
 };
 
 // Batch rows per scan call, so that each call stays within the int32
@@ -38,6 +39,10 @@ std::uint64_t scan_rows(const SaccMambaBlockArgs& a) {
     while (chunk > 1 && chunk * per_seq * 2 > kMaxElements) chunk = (chunk + 1) / 2;
     return chunk;
 }
+
+// dt_proj inside the scan (delta = dt W_dt^T formed per token in FP32, no
+// GEMM launch and no delta tensor) for the small ranks the scan supports.
+bool dt_rank_fusable(const SaccMambaBlockArgs& a) { return a.dt_rank == 8 || a.dt_rank == 16; }
 
 // The scan's arguments for `nb` rows of the block (pointers left null).
 SaccScanExArgs scan_shape(const SaccMambaBlockArgs& a, std::uint64_t nb) {
@@ -65,10 +70,13 @@ Layout plan(const SaccMambaBlockArgs& a) {
     l.xz = take(M * 2 * D * e);
     l.u = take(M * D * e);
     l.dbc = take(M * (R + 2 * N) * e);
-    l.delta = take(M * D * e);
-    l.y = take(M * D * e);
-    // Scratch of the scan's fused chunk-parallel mode (few long sequences).
+    // Scratch of the scan's fused chunk-parallel mode (few long sequences);
+    // that latency-bound launch runs without the in-scan dt_proj (measured
+    // slower with it), every other scan forms delta itself for rank 8 / 16.
     l.scan_bytes = bulk_scan_scratch_bytes(scan_shape(a, a.batch < scan_rows(a) ? a.batch : scan_rows(a)));
+    l.fuse_dt = dt_rank_fusable(a) && l.scan_bytes == 0;
+    l.delta = l.fuse_dt ? 0 : take(M * D * e);
+    l.y = take(M * D * e);
     l.scan = l.scan_bytes ? take(l.scan_bytes) : 0;
     l.total = off;
     return l;
@@ -130,8 +138,11 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
         w_x = wx;
     }
     if ((err = launch_gemm(gemm_args(dt_, M, W, D, u, D, w_x, D, dbc, W), stream)) != cudaSuccess) return err;
-    // dt_proj on the dt columns (bias added inside the scan, before softplus).
-    if ((err = launch_gemm(gemm_args(dt_, M, D, R, dbc, W, a.w_dt, R, delta, D), stream)) != cudaSuccess) return err;
+    // dt_proj on the dt columns (bias added inside the scan, before softplus);
+    // for rank 8 / 16 the scan forms delta itself.
+    const bool fuse_dt = l.fuse_dt;
+    if (!fuse_dt && (err = launch_gemm(gemm_args(dt_, M, D, R, dbc, W, a.w_dt, R, delta, D), stream)) != cudaSuccess)
+        return err;
 
     // Selective scan with D skip and SiLU(z) gate, (B, L, D) layout, z / B / C
     // read in place through their row pitches; chunked by batch so that each
@@ -142,13 +153,17 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
         const std::uint64_t nb = (a.batch - b0 < chunk) ? a.batch - b0 : chunk;
         const std::size_t tok = b0 * a.length;
         SaccScanExArgs s = scan_shape(a, nb);
-        s.u = at(u, tok * D); s.delta = at(delta, tok * D);
+        s.u = at(u, tok * D);
+        s.delta = fuse_dt ? at(dbc, tok * W) : at(delta, tok * D);
         s.z = at(xz, tok * 2 * D + D);
         s.b = at(dbc, tok * W + R); s.c = at(dbc, tok * W + R + N);
         s.a = a.a; s.d = a.d; s.delta_bias = a.dt_bias;
         s.y = static_cast<unsigned char*>(y) + tok * D * e;
         if (!bulk_eligible(s, &pitch)) return cudaErrorInvalidValue; // shapes are checked by the caller
-        if ((err = launch_scan_bulk(s, stream, &pitch, l.scan_bytes ? ws + l.scan : nullptr, l.scan_bytes)) != cudaSuccess)
+        const DtFusion dtf{at(dbc, tok * W), W, a.w_dt, static_cast<int>(R)};
+        if (fuse_dt && !dt_fusable(s, dtf)) return cudaErrorInvalidValue;
+        if ((err = launch_scan_bulk(s, stream, &pitch, l.scan_bytes ? ws + l.scan : nullptr, l.scan_bytes,
+                                    fuse_dt ? &dtf : nullptr)) != cudaSuccess)
             return err;
     }
 

@@ -104,6 +104,7 @@ struct BulkParams {
     int passes;                  // 2: fused chunk-parallel launch (pass 0 local, pass 1 final, one CTA per part)
     unsigned long long item0;    // first item of this launch (the final pass starts at part 1)
     float* scratch;              // fused mode: per (unit, part) 17 x 128 floats (S, sum of Delta), then the flags
+    const void* wdt;             // kR > 0: W_dt (channels x kR); delta = dt rows (tensor map td) x W_dt^T in the scan
 };
 
 
@@ -193,6 +194,43 @@ __device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T*
     }
 }
 
+// (B, L, D) with delta formed in the scan: the chunk's dt rows sit token-major
+// in `dt` ([32][kR]); delta of token t is dt[t] . W_dt[d] (FP32; `wrow` the
+// lane's W_dt row, re-read from L1 for every 8 tokens so that it holds no
+// registers across the scan).  Every lane reads the same dt values (broadcast).
+template <typename T, int kR>
+__device__ __forceinline__ void delta_from_dt(const T* dt, const T* wrow, int q, Block8& blk) {
+    float wd[kR];
+#pragma unroll
+    for (int v = 0; v < kR / 8; ++v) {
+        const uint4 w8 = __ldg(reinterpret_cast<const uint4*>(wrow) + v);
+        const std::uint32_t ww[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack2<T>(ww[i]);
+            wd[8 * v + 2 * i] = f.x;
+            wd[8 * v + 2 * i + 1] = f.y;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint4* row = reinterpret_cast<const uint4*>(dt + (q * 8 + j) * kR);
+        float acc = 0.0f;
+#pragma unroll
+        for (int v = 0; v < kR / 8; ++v) {
+            const uint4 w8 = row[v];
+            const std::uint32_t ww[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = unpack2<T>(ww[i]);
+                acc = fmaf(f.x, wd[8 * v + 2 * i], acc);
+                acc = fmaf(f.y, wd[8 * v + 2 * i + 1], acc);
+            }
+        }
+        blk.x[j] = acc;
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const float (&out)[8]) {
 #pragma unroll
@@ -203,11 +241,20 @@ __device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const floa
 // x = token, y = row (b * D + d).  (B, L, D): 3D maps (channel, token, batch),
 // so that a chunk past the end of a sequence reads zeros instead of the next
 // sequence; a packed varlen sequence reads whatever follows it, unused.
-template <typename T, bool kBDL, bool kHasZ>
+template <typename T, bool kBDL, bool kHasZ, int kR = 0>
 __device__ __forceinline__ void issue_chunk(Smem<T, kBDL && kHasZ>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
                                             std::uint32_t c_bytes, const CUtensorMap* tu, const CUtensorMap* td,
                                             const CUtensorMap* tz, const CUtensorMap* tb, const CUtensorMap* tc) {
     constexpr std::uint32_t tile = kLanes * kT * sizeof(T), btile = kN * kT * sizeof(T);
+    if constexpr (kR > 0) {
+        // (B, L, D), delta formed in the scan: the chunk's dt rows instead of a delta tile.
+        mbar_arrive_expect_tx(&sm.full[s], tile + kR * kT * sizeof(T) + btile + c_bytes);
+        tma_load_3d(sm.u[s], tu, &sm.full[s], row0, t0, bb);
+        tma_load_3d(sm.dl[s], td, &sm.full[s], 0, t0, bb);
+        tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
+        tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
+        return;
+    }
     mbar_arrive_expect_tx(&sm.full[s], tile * (kBDL && kHasZ ? 3u : 2u) + btile + c_bytes);
     if (kBDL) {
         tma_load_2d(sm.u[s], tu, &sm.full[s], t0, row0);
@@ -480,7 +527,7 @@ __device__ __forceinline__ bool fused_prefix(const BulkParams& p, const Item& w,
 // faster on one-chunk items).  Thread 0 keeps kStages chunk loads in
 // flight along the CTA's whole list, so the next item's first chunks arrive
 // while the current item computes.
-template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode, int kR>
 __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
                                                                   const __grid_constant__ CUtensorMap tm_d,
                                                                   const __grid_constant__ CUtensorMap tm_z,
@@ -518,8 +565,8 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             cursor_next<kBDL, kFullC>(c, p); // to the first chunk of the first item with chunks
         }
         for (int s = 0; s < kStages && c.more; ++s) {
-            issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
-                                        c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+            issue_chunk<T, kBDL, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
+                                            c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
             cursor_next<kBDL, kFullC>(c, p);
         }
     }
@@ -540,6 +587,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         for (int n = 0; n < kN; ++n) a[n] = arow[n] * kLog2e;
         const float dskip = p.has_d ? p.d[d] : 0.0f;
         const float bias = p.bias ? p.bias[d] : 0.0f;
+        const T* wrow = kR > 0 ? static_cast<const T*>(p.wdt) + d * (kR > 0 ? kR : 1) : nullptr;
         float dtsum = 0.0f; // sum of Delta over the part (chunk-parallel local pass)
         if (kMode == 2 && w.c1 == w.c0) continue; // a pass the fused mode skips
         if (w.part == 0) {
@@ -619,10 +667,13 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                 if constexpr (kBDL)
                     load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
                 else
+                {
                     load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], static_cast<const T*>(p.zg),
                                              static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
                                                  static_cast<unsigned long long>(chunk) * kT,
                                              p.zld, d, tid, q, valid - q * 8, blk);
+                    if constexpr (kR > 0) delta_from_dt<T, kR>(sm.dl[s], wrow, q, blk);
+                }
                 float out[8];
                 scan_block8<kFullC, kHasZ, true, kMode != 1>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out,
                                                             dtsum);
@@ -650,8 +701,8 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                 Cursor& c = sm.next;
                 if (c.more) {
                     // Stage s is free again: the chunk kStages ahead in this CTA's list.
-                    issue_chunk<T, kBDL, kHasZ>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
-                                                c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+                    issue_chunk<T, kBDL, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
+                                                    c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
                     cursor_next<kBDL, kFullC>(c, p);
                 }
             }
@@ -745,9 +796,9 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode>
+template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode, int kR = 0>
 struct Variant {
-    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kMode>); }
+    static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kMode, kR>); }
     static cudaError_t prepare() {
         static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                                static_cast<int>(smem_bytes<T, kBDL && kHasZ>()));
@@ -820,6 +871,33 @@ Pick pick(int dtype, bool bdl, bool z, bool full_c, int mode) {
     if (dtype == SACC_DTYPE_BF16)
         return bdl ? pick_z<__nv_bfloat16, true>(z, full_c, mode) : pick_z<__nv_bfloat16, false>(z, full_c, mode);
     return bdl ? pick_z<__half, true>(z, full_c, mode) : pick_z<__half, false>(z, full_c, mode);
+}
+
+// The variants that form delta in the scan from dt rows of rank kR (the
+// block's (B, L, D) layout with a gate and a full-width C).
+template <typename T, int kR>
+Pick make_pick_dt(int mode) {
+    if (mode == 1) {
+        using V = Variant<T, false, true, true, 1, kR>;
+        return {V::fn(), V::smem(), &V::prepare};
+    }
+    if (mode == 2) {
+        using V = Variant<T, false, true, true, 2, kR>;
+        return {V::fn(), V::smem(), &V::prepare};
+    }
+    using V = Variant<T, false, true, true, 0, kR>;
+    return {V::fn(), V::smem(), &V::prepare};
+}
+
+Pick pick_dt(int dtype, int rank, int mode) {
+    if (dtype == SACC_DTYPE_BF16) return rank == 8 ? make_pick_dt<__nv_bfloat16, 8>(mode) : make_pick_dt<__nv_bfloat16, 16>(mode);
+    return rank == 8 ? make_pick_dt<__half, 8>(mode) : make_pick_dt<__half, 16>(mode);
+}
+
+// The variant for this call and mode.
+Pick pick_for(const SaccScanExArgs& a, const DtFusion* dtf, int mode) {
+    if (dtf) return pick_dt(a.dtype, dtf->rank, mode);
+    return pick(a.dtype, a.layout == SACC_LAYOUT_BDL, a.z != nullptr, a.c_width != 1, mode);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
@@ -962,10 +1040,9 @@ bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
 namespace {
 // Parts of the fused chunk-parallel mode for this call on the current device
 // (0: it does not apply), and the variant it would use.
-int fused_plan(const SaccScanExArgs& a, Pick& k) {
+int fused_plan(const SaccScanExArgs& a, const DtFusion* dtf, Pick& k) {
     if (a.cu_seqlens != nullptr) return 0;
-    const bool bdl = a.layout == SACC_LAYOUT_BDL;
-    k = pick(a.dtype, bdl, a.z != nullptr, a.c_width != 1, 2);
+    k = pick_for(a, dtf, 2);
     if (k.prepare() != cudaSuccess) return 0;
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -975,16 +1052,23 @@ int fused_plan(const SaccScanExArgs& a, Pick& k) {
 }
 } // namespace
 
-std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a) {
+bool dt_fusable(const SaccScanExArgs& a, const DtFusion& f) {
+    return (f.rank == 8 || f.rank == 16) && a.layout == SACC_LAYOUT_BLD && a.cu_seqlens == nullptr && a.z != nullptr &&
+           a.c_width == kN && f.dt != nullptr && f.w != nullptr && aligned16(f.dt) && aligned16(f.w) &&
+           f.ld >= static_cast<unsigned long long>(f.rank) && f.ld % 8 == 0;
+}
+
+std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf) {
     Pick k{};
-    const int parts = fused_plan(a, k);
+    const int parts = fused_plan(a, dtf, k);
     return parts ? fused_scratch_bytes(a.batch * (a.channels / kLanes), parts) : 0;
 }
 
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs, void* scratch,
-                             std::size_t scratch_bytes) {
+                             std::size_t scratch_bytes, const DtFusion* dtf) {
     const RowStrides dense{0, 0, 0};
     if (!rs) rs = &dense;
+    if (dtf && !dt_fusable(a, *dtf)) return cudaErrorInvalidValue;
     const bool bdl = a.layout == SACC_LAYOUT_BDL;
     const unsigned long long cw = a.c_width, B = a.batch, D = a.channels, L = a.length, G = a.groups;
     const CUtensorMapDataType dt = a.dtype == SACC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -999,7 +1083,10 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
              make_map_2d(&tb, dt, a.b, L, B * G * kN, L * 2, kT, kN, CU_TENSOR_MAP_SWIZZLE_NONE) &&
              make_map_2d(&tc, dt, a.c, L, B * G * cw, L * 2, kT, static_cast<unsigned>(cw), CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
-        ok = make_map_3d(&tu, dt, a.u, D, L, B, kLanes, kT) && make_map_3d(&td, dt, a.delta, D, L, B, kLanes, kT) &&
+        ok = make_map_3d(&tu, dt, a.u, D, L, B, kLanes, kT) &&
+             (dtf ? make_map_3d(&td, dt, dtf->dt, static_cast<unsigned long long>(dtf->rank), L, B,
+                                static_cast<unsigned>(dtf->rank), kT, dtf->ld)
+                  : make_map_3d(&td, dt, a.delta, D, L, B, kLanes, kT)) &&
              make_map_3d(&tz, dt, a.z ? a.z : a.u, D, L, B, kLanes, kT, a.z ? rs->z : 0) &&
              make_map_3d(&ty, dt, a.y, D, L, B, kLanes, kT) && make_map_3d(&tb, dt, a.b, G * kN, L, B, kN, kT, rs->b) &&
              make_map_3d(&tc, dt, a.c, G * cw, L, B, static_cast<unsigned>(cw), kT, rs->c);
@@ -1014,11 +1101,12 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     p.y = a.y;
     p.zg = a.z;
     p.zld = rs->z ? rs->z : D;
+    p.wdt = dtf ? dtf->w : nullptr;
     const unsigned long long rows = a.cu_seqlens ? static_cast<unsigned long long>(a.nseq) : B; // sequences
     p.units = rows * (D / kLanes);
     p.parts = 1;
     p.epoch = 0;
-    const Pick loop = pick(a.dtype, bdl, a.z != nullptr, cw != 1, true);
+    const Pick loop = pick_for(a, dtf, 1);
     cudaError_t attr = loop.prepare();
     if (attr != cudaSuccess) return attr;
     const unsigned long long wave = resident_ctas(loop);
@@ -1031,7 +1119,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     p.passes = 1;
     if (scratch != nullptr) {
         Pick fk{};
-        const int fused = fused_plan(a, fk);
+        const int fused = fused_plan(a, dtf, fk);
         if (fused && scratch_bytes >= fused_scratch_bytes(p.units, fused) &&
             (reinterpret_cast<std::uintptr_t>(scratch) & 15u) == 0) {
             // Few units over long sequences, with scratch: every part's local
@@ -1058,7 +1146,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     if (chunked) {
         // Few units over long sequences: the chunk-parallel passes (stream
         // ordered, no workspace: the hand-offs live in y like the split's).
-        const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
+        const Pick one = pick_for(a, dtf, 0);
         if ((attr = one.prepare()) != cudaSuccess) return attr;
         p.parts = chunked;
         p.phase = 1;
@@ -1079,7 +1167,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
     }
     p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks, L);
     if (p.parts == 1) {
-        const Pick one = pick(a.dtype, bdl, a.z != nullptr, cw != 1, false);
+        const Pick one = pick_for(a, dtf, 0);
         if ((attr = one.prepare()) != cudaSuccess) return attr;
         return launch_pdl(one.fn, dim3(static_cast<unsigned>(p.units)), dim3(kLanes), one.smem, stream, args);
     }

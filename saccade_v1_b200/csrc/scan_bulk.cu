@@ -752,6 +752,263 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
     if (tid == 0) bulk_wait<0>();
 }
 
+// ------------------------------------------------------------ quad variant
+// Four threads per lane, four of the 16 states each, for launches that leave
+// the SMs mostly empty (few units; the fused chunk-parallel launch): 16 warps
+// per CTA instead of 4, so a lane's per-token dependency chain is spread over
+// four threads.  Thread q of a lane forms Delta for tokens q and q + 4 of every
+// eight and the four threads exchange them by shuffles; the partial sums
+// C_n h_n of the four state quarters meet by two xor shuffles; thread q
+// stores tokens q and q + 4.  (B, L, D) layout with a full-width C, dense rows
+// or packed varlen sequences; modes 0 (one item per CTA) and 2 (fused
+// chunk-parallel, with scratch).
+constexpr int kQ = 4;         // threads per lane
+constexpr int kQS = kN / kQ;  // states per thread
+
+// quad form of fused_prefix: this thread's kQS states of the lane.
+__device__ __forceinline__ bool quad_prefix(const BulkParams& p, const Item& w, int tid, int li, int n0, const float (&a)[kQS],
+                                            float (&h)[kQS]) {
+    bool ready = true;
+    if (tid < w.part) {
+        const unsigned long long* f = fused_flag(p, w, tid);
+        ready = false;
+        for (std::uint32_t i = 0; i < (1u << 24); ++i) {
+            if (flag_acquire(f) == p.epoch) {
+                ready = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!__syncthreads_and(ready)) return false;
+    const unsigned long long unit = w.b * (p.channels / kLanes) + w.d0 / kLanes;
+    const float* rec = p.scratch + unit * p.parts * (kN + 1) * kLanes + li;
+#pragma unroll
+    for (int n = 0; n < kQS; ++n) h[n] = __ldcg(rec + (n0 + n) * kLanes); // S_0
+    constexpr int kBatch = 2;
+    for (int j0 = 1; j0 < w.part; j0 += kBatch) {
+        float sv[kBatch][kQS + 1];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            if (j0 + b < w.part) {
+                const float* r = rec + static_cast<unsigned long long>(j0 + b) * (kN + 1) * kLanes;
+#pragma unroll
+                for (int n = 0; n < kQS; ++n) sv[b][n] = __ldcg(r + (n0 + n) * kLanes);
+                sv[b][kQS] = __ldcg(r + kN * kLanes);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b)
+            if (j0 + b < w.part)
+#pragma unroll
+                for (int n = 0; n < kQS; ++n) h[n] = fmaf(fast_exp2(sv[b][kQS] * a[n]), h[n], sv[b][n]);
+    }
+    return true;
+}
+
+template <typename T, bool kHasZ, int kMode, int kR>
+__global__ void __launch_bounds__(kLanes * kQ, 2) quad_kernel(const __grid_constant__ CUtensorMap tm_u,
+                                                             const __grid_constant__ CUtensorMap tm_d,
+                                                             const __grid_constant__ CUtensorMap tm_z,
+                                                             const __grid_constant__ CUtensorMap tm_b,
+                                                             const __grid_constant__ CUtensorMap tm_c,
+                                                             const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
+    pdl_wait();
+    extern __shared__ unsigned char smem_raw[];
+    auto& sm = *reinterpret_cast<Smem<T, false>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    const int tid = threadIdx.x, li = tid / kQ, q = tid % kQ, n0 = q * kQS;
+    const int quad0 = (tid & 31) & ~(kQ - 1); // this quad's first lane in the warp
+    const unsigned long long D = p.channels;
+    const std::uint32_t c_bytes = kN * kT * sizeof(T);
+    constexpr bool kLoop = kMode != 0;
+    const unsigned long long items = p.units * static_cast<unsigned long long>(p.parts) * (kMode == 2 ? 2u : 1u);
+
+    if (tid == 0) {
+        prefetch_tensor_map(&tm_u);
+        prefetch_tensor_map(&tm_d);
+        prefetch_tensor_map(&tm_b);
+        prefetch_tensor_map(&tm_c);
+        prefetch_tensor_map(&tm_y);
+        for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
+        fence_barrier_init();
+        Cursor& c = sm.next;
+        c.more = 1;
+        c.it = blockIdx.x + p.item0;
+        if (c.it >= items) {
+            c.more = 0;
+        } else {
+            c.w = item_at<false, true>(p, c.it);
+            c.chunk = c.w.c0 - 1;
+            cursor_next<false, true>(c, p);
+        }
+        for (int s = 0; s < kStages && c.more; ++s) {
+            issue_chunk<T, false, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
+                                             c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+            cursor_next<false, true>(c, p);
+        }
+    }
+    __syncthreads();
+
+    bool fault = false;
+    int gc = 0;
+    const unsigned long long first = blockIdx.x + p.item0;
+    const unsigned long long it_end = kLoop ? items : first + 1ull;
+    for (unsigned long long it = first; it < it_end && (!kLoop || !fault); it += kLoop ? gridDim.x : 1u) {
+        const Item w = item_at<false, true>(p, it);
+        if (kMode == 2 && w.c1 == w.c0) continue; // a pass the fused mode skips
+        const unsigned long long d = w.d0 + li, lane = w.b * D + d;
+        float a[kQS], h[kQS];
+        const float* arow = p.a + (p.a_shared ? 0 : d * kN) + n0;
+#pragma unroll
+        for (int n = 0; n < kQS; ++n) a[n] = arow[n] * kLog2e;
+        const float dskip = p.has_d ? p.d[d] : 0.0f;
+        const float bias = p.bias ? p.bias[d] : 0.0f;
+        const T* wrow = kR > 0 ? static_cast<const T*>(p.wdt) + d * (kR > 0 ? kR : 1) : nullptr;
+        float dtsum = 0.0f;
+        if (w.part == 0) {
+#pragma unroll
+            for (int n = 0; n < kQS; ++n) h[n] = p.h0 ? p.h0[lane * kN + n0 + n] : 0.0f;
+        } else if (w.pass == 0) {
+#pragma unroll
+            for (int n = 0; n < kQS; ++n) h[n] = 0.0f; // fused local pass from zero
+        } else if (!quad_prefix(p, w, tid, li, n0, a, h)) {
+            fault = true;
+            break;
+        }
+
+        for (int chunk = w.c0; chunk < w.c1; ++chunk, ++gc) {
+            const int s = gc % kStages;
+            const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((gc / kStages) & 1));
+            if (tid == 0) bulk_wait_read<0>();
+            if (!__syncthreads_and(ok)) {
+                fault = true;
+                break;
+            }
+            for (int i = tid; i < kN * kT; i += kLanes * kQ) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
+            for (int i = tid; i < kN * kT; i += kLanes * kQ) sm.bc[i / kN][kN + i % kN] = to_f32(sm.craw[s][i]);
+            __syncthreads();
+
+            const unsigned long long left = w.len - static_cast<unsigned long long>(chunk) * kT;
+            const int valid = static_cast<int>(left < kT ? left : kT);
+            const int blocks8 = (valid + 7) / 8;
+            const unsigned long long zrow0 = static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
+                                             static_cast<unsigned long long>(chunk) * kT;
+#pragma unroll 1
+            for (int qb = 0; qb < blocks8; ++qb) {
+                const int count = valid - qb * 8;
+                float u8[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) u8[j] = to_f32(sm.u[s][(qb * 8 + j) * kLanes + li]);
+                // Delta of tokens q and q + 4.
+                float dtq[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int t = qb * 8 + q + 4 * e;
+                    float x;
+                    if constexpr (kR > 0) {
+                        const uint4* row = reinterpret_cast<const uint4*>(sm.dl[s] + t * kR);
+                        const uint4* wr = reinterpret_cast<const uint4*>(wrow);
+                        float acc = 0.0f;
+#pragma unroll
+                        for (int v = 0; v < kR / 8; ++v) {
+                            const uint4 d8 = row[v], w8 = __ldg(wr + v);
+                            const std::uint32_t dd[4] = {d8.x, d8.y, d8.z, d8.w}, ww[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float2 fd = unpack2<T>(dd[i]), fw = unpack2<T>(ww[i]);
+                                acc = fmaf(fd.x, fw.x, acc);
+                                acc = fmaf(fd.y, fw.y, acc);
+                            }
+                        }
+                        x = acc;
+                    } else {
+                        x = to_f32(sm.dl[s][t * kLanes + li]);
+                    }
+                    const float v = x + bias;
+                    dtq[e] = p.softplus ? softplus_poly(v) : v;
+                }
+                float yp[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float dt = __shfl_sync(0xffffffffu, dtq[j / 4], quad0 + (j % 4));
+                    yp[j] = 0.0f;
+                    if (j < count) { // tokens past the end stay out of the state
+                        dtsum += dt;
+                        const float du = dt * u8[j];
+                        const float4 bq = *reinterpret_cast<const float4*>(&sm.bc[qb * 8 + j][n0]);
+                        const float4 cq = *reinterpret_cast<const float4*>(&sm.bc[qb * 8 + j][kN + n0]);
+                        const float bb[4] = {bq.x, bq.y, bq.z, bq.w}, cc[4] = {cq.x, cq.y, cq.z, cq.w};
+                        float acc[4];
+#pragma unroll
+                        for (int n = 0; n < kQS; ++n) {
+                            h[n] = fmaf(fast_exp2(dt * a[n]), h[n], du * bb[n]);
+                            acc[n] = cc[n] * h[n];
+                        }
+                        yp[j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    yp[j] += __shfl_xor_sync(0xffffffffu, yp[j], 1);
+                    yp[j] += __shfl_xor_sync(0xffffffffu, yp[j], 2);
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int j = q + 4 * e, t = qb * 8 + j;
+                    float y = 0.0f;
+                    if (j < count) {
+                        y = fmaf(dskip, u8[j], yp[j]);
+                        if constexpr (kHasZ)
+                            y *= silu(to_f32(static_cast<const T*>(p.zg)[(zrow0 + static_cast<unsigned long long>(t)) * p.zld + d]));
+                    }
+                    sm.y[t * kLanes + li] = from_f32<T>(y);
+                }
+            }
+            fence_async_shared();
+            __syncthreads();
+            const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
+            const bool write_y = !(kMode == 2 && w.pass == 0 && w.part > 0); // local-pass outputs are not final
+            const bool tail = p.cu && valid < kT;
+            if (tail && write_y) {
+                T* yg = static_cast<T*>(p.y);
+                for (int t = q; t < valid; t += kQ) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + li];
+            }
+            if (tid == 0) {
+                if (!tail && write_y) tma_store_3d(&tm_y, sm.y, w.row0, tc0, w.bb);
+                bulk_commit();
+                Cursor& c = sm.next;
+                if (c.more) {
+                    issue_chunk<T, false, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
+                                                     c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+                    cursor_next<false, true>(c, p);
+                }
+            }
+        }
+        if (fault) break;
+        if (kMode == 2 && w.pass == 0) {
+            float* rec = p.scratch + (static_cast<unsigned long long>(w.b * (D / kLanes) + w.d0 / kLanes) * p.parts + w.part) *
+                                         (kN + 1) * kLanes + li;
+#pragma unroll
+            for (int n = 0; n < kQS; ++n) rec[(n0 + n) * kLanes] = h[n];
+            if (q == 0) rec[kN * kLanes] = dtsum;
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) flag_release(fused_flag(p, w, w.part), p.epoch);
+        } else if (p.h_final && w.part + 1 == p.parts) {
+#pragma unroll
+            for (int n = 0; n < kQS; ++n) p.h_final[lane * kN + n0 + n] = h[n];
+        }
+    }
+    if (fault) {
+        if (tid == 0) {
+            atomicOr(&g_bulk_fault, 1u);
+            for (int s = 0; s < kStages; ++s) (void)mbar_wait_bounded(&sm.full[s], 0u, 1u << 16);
+        }
+        return;
+    }
+    if (tid == 0) bulk_wait<0>();
+}
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -893,6 +1150,43 @@ Pick pick_dt(int dtype, int rank, int mode) {
     if (dtype == SACC_DTYPE_BF16) return rank == 8 ? make_pick_dt<__nv_bfloat16, 8>(mode) : make_pick_dt<__nv_bfloat16, 16>(mode);
     return rank == 8 ? make_pick_dt<__half, 8>(mode) : make_pick_dt<__half, 16>(mode);
 }
+
+template <typename T, bool kHasZ, int kMode, int kR>
+struct QuadVariant {
+    static const void* fn() { return reinterpret_cast<const void*>(quad_kernel<T, kHasZ, kMode, kR>); }
+    static cudaError_t prepare() {
+        static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                               static_cast<int>(smem_bytes<T, false>()));
+        return status;
+    }
+    static size_t smem() { return smem_bytes<T, false>(); }
+};
+
+template <typename T, bool kHasZ, int kR>
+Pick make_pick_quad(int mode) {
+    if (mode == 2) {
+        using V = QuadVariant<T, kHasZ, 2, kR>;
+        return {V::fn(), V::smem(), &V::prepare};
+    }
+    using V = QuadVariant<T, kHasZ, 0, kR>;
+    return {V::fn(), V::smem(), &V::prepare};
+}
+
+template <typename T>
+Pick pick_quad_t(bool z, int rank, int mode) {
+    if (rank == 8) return make_pick_quad<T, true, 8>(mode);
+    if (rank == 16) return make_pick_quad<T, true, 16>(mode);
+    return z ? make_pick_quad<T, true, 0>(mode) : make_pick_quad<T, false, 0>(mode);
+}
+
+// The four-threads-per-lane variant ((B, L, D), full-width C; modes 0 and 2).
+Pick pick_quad(const SaccScanExArgs& a, const DtFusion* dtf, int mode) {
+    const int rank = dtf ? dtf->rank : 0;
+    return a.dtype == SACC_DTYPE_BF16 ? pick_quad_t<__nv_bfloat16>(a.z != nullptr, rank, mode)
+                                      : pick_quad_t<__half>(a.z != nullptr, rank, mode);
+}
+
+bool quad_eligible(const SaccScanExArgs& a) { return a.layout == SACC_LAYOUT_BLD && a.c_width == kN; }
 
 // The variant for this call and mode.
 Pick pick_for(const SaccScanExArgs& a, const DtFusion* dtf, int mode) {
@@ -1042,7 +1336,7 @@ namespace {
 // (0: it does not apply), and the variant it would use.
 int fused_plan(const SaccScanExArgs& a, const DtFusion* dtf, Pick& k) {
     if (a.cu_seqlens != nullptr) return 0;
-    k = pick_for(a, dtf, 2);
+    k = quad_eligible(a) ? pick_quad(a, dtf, 2) : pick_for(a, dtf, 2);
     if (k.prepare() != cudaSuccess) return 0;
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1131,7 +1425,7 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
             p.epoch = next_epoch();
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(static_cast<unsigned>(p.units * fused));
-            cfg.blockDim = dim3(kLanes);
+            cfg.blockDim = dim3(quad_eligible(a) ? kLanes * kQ : kLanes);
             cfg.dynamicSmemBytes = fk.smem;
             cfg.stream = stream;
             cudaLaunchAttribute attrs[2]{};
@@ -1166,6 +1460,12 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
         return launch_pdl(one.fn, dim3(static_cast<unsigned>(p.units * (chunked - 1))), dim3(kLanes), one.smem, stream, args);
     }
     p.parts = p.cu ? 1 : split_parts(p.units, wave, p.nchunks, L);
+    if (p.parts == 1 && quad_eligible(a) && p.units <= 2ull * static_cast<unsigned long long>(sms)) {
+        // Few units (at most two CTAs per SM): four threads per lane.
+        const Pick qk = pick_quad(a, dtf, 0);
+        if ((attr = qk.prepare()) != cudaSuccess) return attr;
+        return launch_pdl(qk.fn, dim3(static_cast<unsigned>(p.units)), dim3(kLanes * kQ), qk.smem, stream, args);
+    }
     if (p.parts == 1) {
         const Pick one = pick_for(a, dtf, 0);
         if ((attr = one.prepare()) != cudaSuccess) return attr;

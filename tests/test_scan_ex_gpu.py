@@ -346,9 +346,10 @@ def test_bulk_split_launch_bitwise_equals_unsplit(layout):
         hf = torch.empty(B, D, N, device="cuda")
         y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
         ys, hs = [], []
-        for b0 in range(0, B, 8):
-            sl = slice(b0, b0 + 8)
-            hfi = torch.empty(8, D, N, device="cuda")
+        rows = 32  # 384 units: one wave of the one-thread-per-lane kernel, not split (the four-thread kernel takes <= 296)
+        for b0 in range(0, B, rows):
+            sl = slice(b0, b0 + rows)
+            hfi = torch.empty(rows, D, N, device="cuda")
             ys.append(sb.selective_scan_ex(u[sl].contiguous(), dl[sl].contiguous(), A, bm[sl].contiguous(), cm[sl].contiguous(),
                                            D=Dv, z=z[sl].contiguous(), delta_bias=bias, h0=h0[sl].contiguous(), h_final=hfi,
                                            layout=layout, stream=s))
@@ -433,4 +434,26 @@ def test_bulk_chunk_parallel_close_to_one_pass(layout):
     y10, hf10 = gpu_run(rep, "bf16", layout, h0=np.concatenate([h0] * 10), want_final=True)
     np.testing.assert_allclose(hf, hf10[:B], rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(y, y10[:B], rtol=8e-3, atol=1e-4)
+    assert ctypes_fault() == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_four_thread_kernel_close_to_one_thread(dt):
+    """Few units run four threads per lane (state quarters, shuffled Delta and
+    partial sums); the same rows inside a batch large enough for the
+    one-thread-per-lane kernel agree to FP32 rounding in the states and to one
+    16-bit rounding step in the outputs.  (B, L, D), gate, h0 / h_final, a
+    ragged last chunk."""
+    B, L, D, N = 4, 200, 256, 16
+    t = long_memory(make(91, B, L, D, N, 1, "BLD", dt))
+    h0 = (np.random.default_rng(92).standard_normal((B, D, N)) * 0.5).astype(np.float32)
+    y, hf = gpu_run(t, dt, "BLD", h0=h0, want_final=True)
+    rep = dict(t)
+    for k in ("u", "delta", "z", "b", "c"):
+        rep[k] = np.concatenate([t[k]] * 80)  # 640 units of 128 channels
+    y80, hf80 = gpu_run(rep, dt, "BLD", h0=np.concatenate([h0] * 80), want_final=True)
+    np.testing.assert_allclose(hf, hf80[:B], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(y, y80[:B], rtol=8e-3, atol=1e-4)
+    ref, hr, _ = oracle_run(t, "BLD", h0=h0, want_final=True)
+    check_16bit(f"quad_{dt}", y, ref)
     assert ctypes_fault() == 0

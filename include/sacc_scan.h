@@ -139,6 +139,12 @@ const char* sacc_scan_identity(void);
  * *out (synchronous with the device), clearing it when `clear` is non-zero.
  * 0 means no kernel has ever given up waiting. */
 int sacc_scan_fault(uint32_t* out, int clear);
+/* Diagnostics: enqueues one CTA that waits, with the scan kernels' own wait
+ * helpers, on a hand-off flag nothing sets and on an mbarrier nothing arrives
+ * at, `limit` polls each (1 .. 2^20); both waits run out, the kernel sets bit 0
+ * of the fault word and returns, and the context stays usable.  For testing
+ * the failure path without a GPU fault. */
+int sacc_scan_wait_probe(uint32_t limit, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------
  * Extended scan (no counterpart in the reference, whose contract has zero

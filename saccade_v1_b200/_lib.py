@@ -28,6 +28,7 @@ EXPORTS = (
     "sacc_scan_identity",
     "sacc_selective_scan_ex",
     "sacc_scan_fault",
+    "sacc_scan_wait_probe",
     "sacc_selective_scan_step",
     "sacc_gemm",
     "sacc_mamba_block_workspace",
@@ -160,6 +161,8 @@ def load() -> ctypes.CDLL:
     L.sacc_selective_scan_ex.restype = i
     L.sacc_scan_fault.argtypes = [ctypes.POINTER(ctypes.c_uint32), i]
     L.sacc_scan_fault.restype = i
+    L.sacc_scan_wait_probe.argtypes = [ctypes.c_uint32, vp]
+    L.sacc_scan_wait_probe.restype = i
     L.sacc_selective_scan_step.argtypes = [ctypes.POINTER(ScanStepArgs), vp]
     L.sacc_selective_scan_step.restype = i
     L.sacc_gemm.argtypes = [ctypes.POINTER(GemmArgs), vp]

@@ -352,6 +352,15 @@ int sacc_scan_fault(uint32_t* out, int clear) {
     });
 }
 
+int sacc_scan_wait_probe(uint32_t limit, cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "sacc_scan_wait_probe";
+        require_stream(api, stream);
+        if (limit == 0 || limit > (1u << 20)) reject(api, "limit must be in [1, 2^20] polls");
+        CK(launch_wait_probe(limit, stream));
+    });
+}
+
 int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream) {
     return guarded([&] {
         constexpr const char* api = "selective_scan_ex";

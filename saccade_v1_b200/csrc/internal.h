@@ -130,6 +130,8 @@ std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
 cudaError_t read_bulk_fault(unsigned* out, bool clear);
+// One CTA whose bounded waits (a flag, an mbarrier) run out after `limit` polls.
+cudaError_t launch_wait_probe(std::uint32_t limit, cudaStream_t stream);
 
 // Loads every kernel (cudaFuncGetAttributes) and sets shared-memory limits;
 // appends one report line per kernel.

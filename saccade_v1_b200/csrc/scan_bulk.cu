@@ -1009,6 +1009,30 @@ __global__ void __launch_bounds__(kLanes * kQ, 2) quad_kernel(const __grid_const
     if (tid == 0) bulk_wait<0>();
 }
 
+// ------------------------------------------------------------ wait probe
+// Diagnostics for the bounded waits: one CTA waits on a hand-off flag that
+// nothing sets and on an mbarrier nothing arrives at, with the scan kernels'
+// own wait helpers, `limit` polls each; on time-out it sets the fault word,
+// as the scan kernels do, and returns (the context stays usable).
+__device__ unsigned long long g_probe_flag; // never written
+
+__global__ void wait_probe_kernel(std::uint32_t limit) {
+    __shared__ alignas(8) std::uint64_t bar;
+    if (threadIdx.x != 0) return;
+    bool ok = false;
+    for (std::uint32_t i = 0; i < limit; ++i) {
+        if (flag_acquire(&g_probe_flag) == 1ull) {
+            ok = true;
+            break;
+        }
+        __nanosleep(128);
+    }
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    const bool arrived = mbar_wait_bounded(&bar, 0u, limit);
+    if (!ok || !arrived) atomicOr(&g_bulk_fault, 1u);
+}
+
 // ---------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1508,6 +1532,11 @@ cudaError_t load_scan_bulk_kernels(std::string& report) {
                           " dynamic_shared_bytes=" + std::to_string(k.smem) + "\n";
             }
     return cudaSuccess;
+}
+
+cudaError_t launch_wait_probe(std::uint32_t limit, cudaStream_t stream) {
+    wait_probe_kernel<<<1, 32, 0, stream>>>(limit);
+    return cudaGetLastError();
 }
 
 cudaError_t read_bulk_fault(unsigned* out, bool clear) {

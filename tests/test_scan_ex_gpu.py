@@ -457,3 +457,25 @@ def test_four_thread_kernel_close_to_one_thread(dt):
     ref, hr, _ = oracle_run(t, "BLD", h0=h0, want_final=True)
     check_16bit(f"quad_{dt}", y, ref)
     assert ctypes_fault() == 0
+
+
+def test_bounded_waits_report_a_fault_and_leave_the_context_usable():
+    """A wait that runs out (a flag nothing sets, an mbarrier nothing arrives
+    at, polled with the scan kernels' helpers) sets the fault word instead of
+    hanging; the next scan runs normally on the same context."""
+    import ctypes
+
+    from saccade_v1_b200 import _lib
+    L = _lib.load()
+    v = ctypes.c_uint32(0)
+    assert L.sacc_scan_fault(ctypes.byref(v), 1) == 0  # clear
+    s = torch.cuda.Stream()
+    assert L.sacc_scan_wait_probe(1000, s.cuda_stream) == 0, _lib.last_error()
+    s.synchronize()
+    assert L.sacc_scan_fault(ctypes.byref(v), 1) == 0 and v.value & 1
+    assert L.sacc_scan_wait_probe(0, s.cuda_stream) == _lib.SACC_EINVAL
+    t = make(95, 2, 96, 256, 16, 1, "BLD", "bf16")
+    y, _ = gpu_run(t, "bf16", "BLD")
+    ref, _, _ = oracle_run(t, "BLD")
+    check_16bit("after_probe", y, ref)
+    assert ctypes_fault() == 0

@@ -138,6 +138,22 @@ __device__ __forceinline__ std::uint32_t pack2<__half>(float lo, float hi) {
     return w;
 }
 
+// A lane's 16 FP32 values (a row of A, h0 or h_final) as four 16-byte accesses
+// (rows are 64-byte aligned: the launcher checks the base pointers).
+__device__ __forceinline__ void load16(const float* src, float (&v)[16], float scale = 1.0f) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(src) + k);
+        v[4 * k] = q.x * scale; v[4 * k + 1] = q.y * scale; v[4 * k + 2] = q.z * scale; v[4 * k + 3] = q.w * scale;
+    }
+}
+
+__device__ __forceinline__ void store16(float* dst, const float (&v)[16]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        reinterpret_cast<float4*>(dst)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
 // Eight tokens of one lane's u / raw delta / z.
 struct Block8 {
     float u[8], x[8], z[8];
@@ -582,17 +598,19 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
         // Per-lane constants: A * log2(e), D, dt bias; the state from h0 (or
         // zero) for a unit's first part, else from the previous part's hand-off.
         float a[kN], h[kN];
-        const float* arow = p.a + (p.a_shared ? 0 : d * kN);
-#pragma unroll
-        for (int n = 0; n < kN; ++n) a[n] = arow[n] * kLog2e;
+        load16(p.a + (p.a_shared ? 0 : d * kN), a, kLog2e);
         const float dskip = p.has_d ? p.d[d] : 0.0f;
         const float bias = p.bias ? p.bias[d] : 0.0f;
         const T* wrow = kR > 0 ? static_cast<const T*>(p.wdt) + d * (kR > 0 ? kR : 1) : nullptr;
         float dtsum = 0.0f; // sum of Delta over the part (chunk-parallel local pass)
         if (kMode == 2 && w.c1 == w.c0) continue; // a pass the fused mode skips
         if (w.part == 0) {
+            if (p.h0) {
+                load16(p.h0 + lane * kN, h);
+            } else {
 #pragma unroll
-            for (int n = 0; n < kN; ++n) h[n] = p.h0 ? p.h0[lane * kN + n] : 0.0f;
+                for (int n = 0; n < kN; ++n) h[n] = 0.0f;
+            }
         } else if (kMode == 2) {
             if (w.pass == 0) {
 #pragma unroll
@@ -721,8 +739,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
                 __syncthreads();
                 if (tid == 0) flag_release(fused_flag(p, w, w.part), p.epoch);
             } else if (p.h_final && w.part + 1 == p.parts) {
-#pragma unroll
-                for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
+                store16(p.h_final + lane * kN, h);
             }
         } else if (p.phase == 1) {
             // Local pass: the part's end state and its sum of Delta go to the
@@ -736,8 +753,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             __syncthreads();
             if (tid == 0) flag_release(flag_at<T, kBDL>(p, w, static_cast<unsigned long long>(w.c1) * kT), p.epoch);
         } else if (p.h_final && w.part + 1 == p.parts) {
-#pragma unroll
-            for (int n = 0; n < kN; ++n) p.h_final[lane * kN + n] = h[n];
+            store16(p.h_final + lane * kN, h);
         }
     }
     if (fault) {
@@ -764,6 +780,7 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
 // chunk-parallel, with scratch).
 constexpr int kQ = 4;         // threads per lane
 constexpr int kQS = kN / kQ;  // states per thread
+static_assert(kQS == 4, "the quad kernel moves a thread's states as one float4");
 
 // quad form of fused_prefix: this thread's kQS states of the lane.
 __device__ __forceinline__ bool quad_prefix(const BulkParams& p, const Item& w, int tid, int li, int n0, const float (&a)[kQS],
@@ -858,16 +875,17 @@ __global__ void __launch_bounds__(kLanes * kQ, 2) quad_kernel(const __grid_const
         if (kMode == 2 && w.c1 == w.c0) continue; // a pass the fused mode skips
         const unsigned long long d = w.d0 + li, lane = w.b * D + d;
         float a[kQS], h[kQS];
-        const float* arow = p.a + (p.a_shared ? 0 : d * kN) + n0;
-#pragma unroll
-        for (int n = 0; n < kQS; ++n) a[n] = arow[n] * kLog2e;
+        {
+            const float4 av = __ldg(reinterpret_cast<const float4*>(p.a + (p.a_shared ? 0 : d * kN) + n0));
+            a[0] = av.x * kLog2e; a[1] = av.y * kLog2e; a[2] = av.z * kLog2e; a[3] = av.w * kLog2e;
+        }
         const float dskip = p.has_d ? p.d[d] : 0.0f;
         const float bias = p.bias ? p.bias[d] : 0.0f;
         const T* wrow = kR > 0 ? static_cast<const T*>(p.wdt) + d * (kR > 0 ? kR : 1) : nullptr;
         float dtsum = 0.0f;
         if (w.part == 0) {
-#pragma unroll
-            for (int n = 0; n < kQS; ++n) h[n] = p.h0 ? p.h0[lane * kN + n0 + n] : 0.0f;
+            const float4 hv = p.h0 ? __ldg(reinterpret_cast<const float4*>(p.h0 + lane * kN + n0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            h[0] = hv.x; h[1] = hv.y; h[2] = hv.z; h[3] = hv.w;
         } else if (w.pass == 0) {
 #pragma unroll
             for (int n = 0; n < kQS; ++n) h[n] = 0.0f; // fused local pass from zero
@@ -995,8 +1013,7 @@ __global__ void __launch_bounds__(kLanes * kQ, 2) quad_kernel(const __grid_const
             __syncthreads();
             if (tid == 0) flag_release(fused_flag(p, w, w.part), p.epoch);
         } else if (p.h_final && w.part + 1 == p.parts) {
-#pragma unroll
-            for (int n = 0; n < kQS; ++n) p.h_final[lane * kN + n0 + n] = h[n];
+            *reinterpret_cast<float4*>(p.h_final + lane * kN + n0) = make_float4(h[0], h[1], h[2], h[3]);
         }
     }
     if (fault) {
@@ -1349,7 +1366,8 @@ bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs) {
     } else {
         return false;
     }
-    for (const void* ptr : {a.u, a.delta, a.b, a.c, a.z, static_cast<const void*>(a.y)})
+    for (const void* ptr : {a.u, a.delta, a.b, a.c, a.z, static_cast<const void*>(a.y), static_cast<const void*>(a.a),
+                            static_cast<const void*>(a.h0), static_cast<const void*>(a.h_final)})
         if (ptr && !aligned16(ptr)) return false;
     const unsigned long long rows = a.batch * a.channels, tokens = a.batch * a.length;
     return rows <= 0x7fffffffull && tokens <= 0x7fffffffull && a.batch * a.groups * kN <= 0x7fffffffull;

@@ -9,6 +9,19 @@
  * lets TensorRT cast around them, include/saccade/head_trt_network.hpp:25-28):
  *   saccade::SelectiveScan   v3  fields: has_d (INT32); u, delta, B, C and y
  *                                kHALF, A and D kFLOAT (sacc_selective_scan_f16)
+ * and the whole head Mamba block as one plugin (the reference builds it from
+ * TensorRT layers around its scan plugin, src/head_trt_network.cpp:181-233):
+ *   saccade::MambaBlock      v1  fields: dt_rank, residual (INT32); inputs x
+ *                                (B, L, d_model), w_in (2 d_inner, d_model),
+ *                                conv_w (d_inner, d_conv), conv_b (d_inner),
+ *                                w_x (dt_rank + d_state + 1 or 2 d_state, d_inner),
+ *                                w_dt (d_inner, dt_rank), dt_bias (d_inner),
+ *                                A (d_inner, d_state), D (d_inner),
+ *                                w_out (d_model, d_inner); output (B, L, d_model).
+ *                                x, the weights and the output kHALF or kBF16
+ *                                (all alike), conv_w / conv_b / dt_bias / A / D
+ *                                kFLOAT; a workspace (sacc_plugin_workspace_bytes)
+ *                                runs sacc_mamba_block_forward; no status output.
  *   saccade::CrossScanExpand v1  fields: none
  *   saccade::CrossScanMerge  v1  fields: height, width (INT32)
  * Each entry point below implements one IPluginV3 / IPluginCreatorV3One method
@@ -38,6 +51,8 @@ extern "C" {
 #define SACC_PLUGIN_EXPAND_VERSION "1"
 #define SACC_PLUGIN_MERGE_NAME "CrossScanMerge"
 #define SACC_PLUGIN_MERGE_VERSION "1"
+#define SACC_PLUGIN_BLOCK_NAME "MambaBlock"
+#define SACC_PLUGIN_BLOCK_VERSION "1"
 
 /* Field and tensor type tags (the adapter maps TensorRT's PluginFieldType,
  * DataType and TensorFormat values onto these). */
@@ -45,6 +60,7 @@ extern "C" {
 #define SACC_FIELD_OTHER 0
 #define SACC_TENSOR_FLOAT 0
 #define SACC_TENSOR_HALF 1
+#define SACC_TENSOR_BF16 7
 #define SACC_TENSOR_INT32 3
 #define SACC_TENSOR_OTHER 99
 #define SACC_FORMAT_LINEAR 0
@@ -85,8 +101,13 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* plugin, const SaccTensorDesc
 /* supportsFormatCombination (:163-167): 1 when supported. */
 int sacc_plugin_supports_format(const SaccScanPlugin* plugin, int32_t pos, const SaccTensorDesc* io, int32_t nb_in,
                                 int32_t nb_out);
-/* getWorkspaceSize (:184-186): always 0. */
+/* getWorkspaceSize (:184-186): always 0 for the scan plugins. */
 size_t sacc_plugin_workspace_size(const SaccScanPlugin* plugin);
+/* getWorkspaceSize with the (maximum) input shapes: the MambaBlock plugin's
+ * workspace in bytes, 0 for the others. */
+int sacc_plugin_workspace_bytes(const SaccScanPlugin* plugin, const SaccTensorDesc* in, int32_t nb_in, size_t* bytes);
+/* getFieldsToSerialize of the MambaBlock plugin. */
+int sacc_plugin_block_fields(const SaccScanPlugin* plugin, int32_t* dt_rank, int32_t* residual);
 /* configurePlugin / attachToContext (:171-180, 233-242): load every kernel in
  * the current CUDA context and bind the plugin to that context. */
 int sacc_plugin_bind(SaccScanPlugin* plugin);
@@ -94,6 +115,11 @@ int sacc_plugin_bind(SaccScanPlugin* plugin);
  * descriptor checks (:299-341), then the operator on `stream`. */
 int sacc_plugin_enqueue(const SaccScanPlugin* plugin, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
                         const void* const* inputs, void* const* outputs, cudaStream_t stream);
+/* enqueue with TensorRT's workspace (required by MambaBlock, ignored by the
+ * scan plugins). */
+int sacc_plugin_enqueue_ws(const SaccScanPlugin* plugin, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
+                           const void* const* inputs, void* const* outputs, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream);
 const char* sacc_plugin_last_error(void);
 
 #ifdef __cplusplus

@@ -3,7 +3,9 @@
 // The reference registers three IPluginV3 plugins, saccade::SelectiveScan v2,
 // saccade::CrossScanExpand v1 and saccade::CrossScanMerge v1
 // (src/scan_trt_plugin.cpp:69-455); saccade::SelectiveScan v3 is the same
-// scan with FP16 activations (u, delta, B, C, y) for FP16 engines.  TensorRT itself is not available on this
+// scan with FP16 activations (u, delta, B, C, y) for FP16 engines, and
+// saccade::MambaBlock v1 the whole head block (sacc_mamba_block_forward) with
+// TensorRT's workspace.  TensorRT itself is not available on this
 // platform, so the plugin's logic lives here behind a C ABI whose calls map
 // one to one onto the IPluginV3 methods; a thin TensorRT adapter (see
 // INTEGRATION.md) translates TensorRT's descriptor and field types into these
@@ -17,6 +19,8 @@
 //   sacc_plugin_bind             configurePlugin / attachToContext   :171-180, 233-242, 267-279
 //   sacc_plugin_enqueue          enqueue (+ require_bound, check)    :201-229, 283-341
 //   sacc_plugin_workspace_size   getWorkspaceSize                    :184-186
+//   sacc_plugin_workspace_bytes  getWorkspaceSize with shapes (MambaBlock)
+//   sacc_plugin_enqueue_ws       enqueue with TensorRT's workspace (MambaBlock)
 //
 // Messages keep the reference's text ("saccade::SelectiveScan: ..." and
 // "... creator: ..."); rejections return SACC_EINVAL before any GPU work.
@@ -35,7 +39,7 @@
 namespace sacc {
 namespace {
 
-enum class Op { scan, expand, merge };
+enum class Op { scan, expand, merge, block };
 
 struct Identity {
     const char* name;
@@ -43,10 +47,16 @@ struct Identity {
 };
 
 Identity identity_of(Op op) {
-    return op == Op::scan ? Identity{SACC_PLUGIN_SCAN_NAME, SACC_PLUGIN_SCAN_VERSION}
-         : op == Op::expand ? Identity{SACC_PLUGIN_EXPAND_NAME, SACC_PLUGIN_EXPAND_VERSION}
-                            : Identity{SACC_PLUGIN_MERGE_NAME, SACC_PLUGIN_MERGE_VERSION};
+    return op == Op::scan    ? Identity{SACC_PLUGIN_SCAN_NAME, SACC_PLUGIN_SCAN_VERSION}
+         : op == Op::expand  ? Identity{SACC_PLUGIN_EXPAND_NAME, SACC_PLUGIN_EXPAND_VERSION}
+         : op == Op::merge   ? Identity{SACC_PLUGIN_MERGE_NAME, SACC_PLUGIN_MERGE_VERSION}
+                             : Identity{SACC_PLUGIN_BLOCK_NAME, SACC_PLUGIN_BLOCK_VERSION};
 }
+
+// MambaBlock inputs: x, w_in, conv_w, conv_b, w_x, w_dt, dt_bias, A, D, w_out.
+constexpr int kBlockInputs = 10;
+bool block_fp32_input(int pos) { return pos == 2 || pos == 3 || pos == 6 || pos == 7 || pos == 8; }
+bool activation_type(int32_t t) { return t == SACC_TENSOR_HALF || t == SACC_TENSOR_BF16; }
 
 struct PluginError {
     int code;
@@ -99,7 +109,9 @@ struct SaccScanPlugin {
     std::int32_t has_d, height, width;
     unsigned long long bound_context = 0; // 0: kernels not loaded for any context
     bool half = false;                    // SelectiveScan v3: FP16 activations
-    int inputs() const { return op == sacc::Op::scan ? 5 + has_d : 1; }
+    std::int32_t dt_rank = 0, residual = 0; // MambaBlock fields
+    int inputs() const { return op == sacc::Op::scan ? 5 + has_d : op == sacc::Op::block ? sacc::kBlockInputs : 1; }
+    int outputs() const { return op == sacc::Op::block ? 1 : 2; }
     std::string prefix() const { return std::string(SACC_PLUGIN_NAMESPACE) + "::" + sacc::identity_of(op).name + ": "; }
     // Data type of tensor `pos` (inputs, then y, then status).
     int32_t type_at(int pos) const {
@@ -188,6 +200,47 @@ std::string check(const SaccScanPlugin& p, const SaccTensorDesc* in, const SaccT
     return "unknown plugin";
 }
 
+// MambaBlock descriptors -> block arguments (shapes and dtype), or why not.
+std::string check_block(const SaccScanPlugin& p, const SaccTensorDesc* in, const SaccTensorDesc* out, SaccMambaBlockArgs& a) {
+    const int32_t act = in[0].type;
+    if (!activation_type(act)) return "input 0 is not FP16 or BF16";
+    for (int i = 0; i < kBlockInputs; ++i) {
+        if (in[i].format != SACC_FORMAT_LINEAR) return "input " + std::to_string(i) + " is not linear";
+        if (in[i].type != (block_fp32_input(i) ? SACC_TENSOR_FLOAT : act))
+            return "input " + std::to_string(i) + (block_fp32_input(i) ? " is not FP32" : " differs in type from x");
+        for (int k = 0; k < in[i].nb_dims; ++k)
+            if (in[i].dims[k] < 1) return "input " + std::to_string(i) + " has an empty or unresolved dimension";
+    }
+    if (out[0].type != act || out[0].format != SACC_FORMAT_LINEAR) return "output 0 differs in type from x";
+    const SaccTensorDesc &x = in[0], &w_in = in[1], &conv_w = in[2], &w_x = in[4], &A = in[7];
+    if (x.nb_dims != 3 || w_in.nb_dims != 2 || conv_w.nb_dims != 2 || A.nb_dims != 2 || w_x.nb_dims != 2)
+        return "x must be (batch, length, d_model) and the weights matrices";
+    const std::int64_t dm = x.dims[2], D = conv_w.dims[0], K = conv_w.dims[1], N = A.dims[1], R = p.dt_rank;
+    if (!equal(w_in, {2 * D, dm})) return "w_in " + text(w_in) + " is not (2 d_inner, d_model)";
+    if (!equal(in[3], {D})) return "conv_b " + text(in[3]) + " is not (d_inner)";
+    const std::int64_t cw = w_x.dims[0] - R - N;
+    if (w_x.dims[1] != D || (cw != 1 && cw != N)) return "w_x " + text(w_x) + " is not (dt_rank + d_state + 1 or 2 d_state, d_inner)";
+    if (!equal(in[5], {D, R})) return "w_dt " + text(in[5]) + " is not (d_inner, dt_rank)";
+    if (!equal(in[6], {D})) return "dt_bias " + text(in[6]) + " is not (d_inner)";
+    if (A.dims[0] != D) return "A " + text(A) + " is not (d_inner, d_state)";
+    if (!equal(in[8], {D})) return "D " + text(in[8]) + " is not (d_inner)";
+    if (!equal(in[9], {dm, D})) return "w_out " + text(in[9]) + " is not (d_model, d_inner)";
+    if (!equal(out[0], {x.dims[0], x.dims[1], dm})) return "out " + text(out[0]) + " differs from x";
+    a = SaccMambaBlockArgs{};
+    a.batch = static_cast<std::uint64_t>(x.dims[0]);
+    a.length = static_cast<std::uint64_t>(x.dims[1]);
+    a.d_model = static_cast<std::uint64_t>(dm);
+    a.d_inner = static_cast<std::uint64_t>(D);
+    a.d_state = static_cast<std::uint64_t>(N);
+    a.d_conv = static_cast<std::uint64_t>(K);
+    a.dt_rank = static_cast<std::uint64_t>(R);
+    a.dtype = act == SACC_TENSOR_BF16 ? SACC_DTYPE_BF16 : SACC_DTYPE_F16;
+    a.residual = p.residual;
+    a.eps = 0.0f;
+    a.c_width = static_cast<std::int32_t>(cw);
+    return "";
+}
+
 } // namespace
 } // namespace sacc
 
@@ -215,6 +268,8 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
             op = Op::expand;
         else if (name && !std::strcmp(name, SACC_PLUGIN_MERGE_NAME) && version && !std::strcmp(version, SACC_PLUGIN_MERGE_VERSION))
             op = Op::merge;
+        else if (name && !std::strcmp(name, SACC_PLUGIN_BLOCK_NAME) && version && !std::strcmp(version, SACC_PLUGIN_BLOCK_VERSION))
+            op = Op::block;
         else
             throw PluginError{SACC_EINVAL, std::string("plugin creator not registered: ") + SACC_PLUGIN_NAMESPACE + "::" +
                                                (name ? name : "(null)") + " v" + (version ? version : "(null)")};
@@ -224,6 +279,10 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
         if (op == Op::merge) {
             names[n_names++] = "height";
             names[n_names++] = "width";
+        }
+        if (op == Op::block) {
+            names[n_names++] = "dt_rank";
+            names[n_names++] = "residual";
         }
         const std::string who = std::string(SACC_PLUGIN_NAMESPACE) + "::" + identity_of(op).name + " creator: ";
         std::int32_t value[2] = {0, 0};
@@ -246,8 +305,11 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
         if (op == Op::scan && value[0] != 0 && value[0] != 1) throw PluginError{SACC_EINVAL, who + "has_d must be 0 or 1"};
         if (op == Op::merge && (value[0] < 1 || value[1] < 1))
             throw PluginError{SACC_EINVAL, who + "height and width must be positive"};
+        if (op == Op::block && value[0] < 1) throw PluginError{SACC_EINVAL, who + "dt_rank must be positive"};
+        if (op == Op::block && value[1] != 0 && value[1] != 1) throw PluginError{SACC_EINVAL, who + "residual must be 0 or 1"};
         *out = new SaccScanPlugin{op, op == Op::scan ? value[0] : 1, op == Op::merge ? value[0] : 0,
-                                  op == Op::merge ? value[1] : 0, 0, half};
+                                  op == Op::merge ? value[1] : 0, 0, half,
+                                  op == Op::block ? value[0] : 0, op == Op::block ? value[1] : 0};
     });
 }
 
@@ -270,10 +332,26 @@ int sacc_plugin_fields(const SaccScanPlugin* p, int32_t* has_d, int32_t* height,
     });
 }
 
+int sacc_plugin_block_fields(const SaccScanPlugin* p, int32_t* dt_rank, int32_t* residual) {
+    return plugin_guard([&] {
+        if (!p || p->op != Op::block) throw PluginError{SACC_EINVAL, "sacc_plugin_block_fields: a MambaBlock plugin is required"};
+        if (dt_rank) *dt_rank = p->dt_rank;
+        if (residual) *residual = p->residual;
+    });
+}
+
 int sacc_plugin_output_types(const SaccScanPlugin* p, const int32_t* in_types, int32_t nb_in, int32_t* out_types, int32_t nb_out) {
     return plugin_guard([&] {
         if (!p) throw PluginError{SACC_EINVAL, "sacc_plugin_output_types: plugin is required"};
-        if (nb_in != p->inputs() || nb_out != 2 || !in_types || !out_types) fail(p, "input or output count");
+        if (nb_in != p->inputs() || nb_out != p->outputs() || !in_types || !out_types) fail(p, "input or output count");
+        if (p->op == Op::block) {
+            if (!activation_type(in_types[0])) fail(p, "input 0 is not FP16 or BF16");
+            for (std::int32_t i = 1; i < nb_in; ++i)
+                if (in_types[i] != (block_fp32_input(i) ? SACC_TENSOR_FLOAT : in_types[0]))
+                    fail(p, "input " + std::to_string(i) + (block_fp32_input(i) ? " is not FP32" : " differs in type from x"));
+            out_types[0] = in_types[0];
+            return;
+        }
         for (std::int32_t i = 0; i < nb_in; ++i)
             if (in_types[i] != p->type_at(i)) fail(p, "input " + std::to_string(i) + " is not " + type_name(p->type_at(i)));
         out_types[0] = p->type_at(nb_in);
@@ -287,7 +365,15 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
                               int32_t nb_out) {
     return plugin_guard([&] {
         if (!p) throw PluginError{SACC_EINVAL, "sacc_plugin_output_shapes: plugin is required"};
-        if (nb_in != p->inputs() || nb_out != 2 || !in || !out) fail(p, "input or output count");
+        if (nb_in != p->inputs() || nb_out != p->outputs() || !in || !out) fail(p, "input or output count");
+        if (p->op == Op::block) {
+            SaccTensorDesc o{3, {in[0].dims[0], in[0].dims[1], in[0].dims[2]}, in[0].type, SACC_FORMAT_LINEAR};
+            SaccMambaBlockArgs a{};
+            const std::string why = check_block(*p, in, &o, a);
+            if (!why.empty()) fail(p, why);
+            out[0] = o;
+            return;
+        }
         out[1] = SaccTensorDesc{1, {2}, SACC_TENSOR_INT32, SACC_FORMAT_LINEAR};
         switch (p->op) {
         case Op::scan: {
@@ -327,8 +413,15 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
 // Dense row-major FP32 everywhere except the INT32 status output (:163-167);
 // v3: FP16 u, delta, B, C and y.
 int sacc_plugin_supports_format(const SaccScanPlugin* p, int32_t pos, const SaccTensorDesc* io, int32_t nb_in, int32_t nb_out) {
-    if (!p || !io || nb_in != p->inputs() || nb_out != 2 || pos < 0 || pos >= nb_in + nb_out) return 0;
-    return io[pos].format == SACC_FORMAT_LINEAR && io[pos].type == p->type_at(pos);
+    if (!p || !io || nb_in != p->inputs() || nb_out != p->outputs() || pos < 0 || pos >= nb_in + nb_out) return 0;
+    if (io[pos].format != SACC_FORMAT_LINEAR) return 0;
+    if (p->op == Op::block) {
+        // x decides the activation type (FP16 or BF16); weights in that type, the
+        // conv, bias, A and D rows in FP32, the output like x.
+        if (pos == 0) return activation_type(io[0].type);
+        return io[pos].type == (pos < nb_in && block_fp32_input(pos) ? SACC_TENSOR_FLOAT : io[0].type);
+    }
+    return io[pos].type == p->type_at(pos);
 }
 
 size_t sacc_plugin_workspace_size(const SaccScanPlugin*) { return 0; }
@@ -354,6 +447,25 @@ int sacc_plugin_bind(SaccScanPlugin* p) {
 // are checked before anything is enqueued.
 int sacc_plugin_enqueue(const SaccScanPlugin* p, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
                         const void* const* in, void* const* out, cudaStream_t stream) {
+    return sacc_plugin_enqueue_ws(p, in_desc, out_desc, in, out, nullptr, 0, stream);
+}
+
+int sacc_plugin_workspace_bytes(const SaccScanPlugin* p, const SaccTensorDesc* in_desc, int32_t nb_in, size_t* bytes) {
+    return plugin_guard([&] {
+        if (!p || !bytes) throw PluginError{SACC_EINVAL, "sacc_plugin_workspace_bytes: plugin and bytes are required"};
+        *bytes = 0;
+        if (p->op != Op::block) return;
+        if (!in_desc || nb_in != p->inputs()) fail(p, "input count");
+        SaccTensorDesc o{3, {in_desc[0].dims[0], in_desc[0].dims[1], in_desc[0].dims[2]}, in_desc[0].type, SACC_FORMAT_LINEAR};
+        SaccMambaBlockArgs a{};
+        const std::string why = check_block(*p, in_desc, &o, a);
+        if (!why.empty()) fail(p, why);
+        if (sacc_mamba_block_workspace(&a, bytes) != SACC_OK) fail(p, sacc_last_error());
+    });
+}
+
+int sacc_plugin_enqueue_ws(const SaccScanPlugin* p, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
+                           const void* const* in, void* const* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     return plugin_guard([&] {
         if (!p || !in_desc || !out_desc || !in || !out) throw PluginError{SACC_EINVAL, "sacc_plugin_enqueue: arguments are required"};
         if (stream == nullptr || stream == cudaStreamLegacy || stream == cudaStreamPerThread)
@@ -368,6 +480,25 @@ int sacc_plugin_enqueue(const SaccScanPlugin* p, const SaccTensorDesc* in_desc, 
             d.ctx_id(of_stream, &id) != CUDA_SUCCESS)
             fail(p, "the stream does not belong to the current CUDA context");
         if (id != p->bound_context) fail(p, "the kernels were loaded in another CUDA context");
+        if (p->op == Op::block) {
+            SaccMambaBlockArgs a{};
+            const std::string why = check_block(*p, in_desc, out_desc, a);
+            if (!why.empty()) fail(p, why);
+            a.x = in[0];
+            a.w_in = in[1];
+            a.conv_w = static_cast<const float*>(in[2]);
+            a.conv_b = static_cast<const float*>(in[3]);
+            a.w_x = in[4];
+            a.w_dt = in[5];
+            a.dt_bias = static_cast<const float*>(in[6]);
+            a.a = static_cast<const float*>(in[7]);
+            a.d = static_cast<const float*>(in[8]);
+            a.w_out = in[9];
+            a.out = out[0];
+            const int rc = sacc_mamba_block_forward(&a, workspace, workspace_bytes, stream);
+            if (rc != SACC_OK) fail(p, sacc_last_error(), rc);
+            return;
+        }
         SaccScanShape scan{};
         SaccCrossScanShape cross{};
         const std::string why = check(*p, in_desc, out_desc, scan, cross);

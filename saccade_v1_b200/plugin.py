@@ -13,10 +13,11 @@ import ctypes
 from . import _lib
 
 FIELD_INT32, FIELD_OTHER = 1, 0
-TENSOR_FLOAT, TENSOR_HALF, TENSOR_INT32, TENSOR_OTHER = 0, 1, 3, 99
+TENSOR_FLOAT, TENSOR_HALF, TENSOR_INT32, TENSOR_BF16, TENSOR_OTHER = 0, 1, 3, 7, 99
 FORMAT_LINEAR, FORMAT_OTHER = 0, 99
 SCAN, EXPAND, MERGE = ("SelectiveScan", "2"), ("CrossScanExpand", "1"), ("CrossScanMerge", "1")
 SCAN_F16 = ("SelectiveScan", "3")  # FP16 u, delta, B, C, y; FP32 A, D
+BLOCK = ("MambaBlock", "1")         # the head Mamba block; fields dt_rank, residual
 
 
 class PluginError(ValueError):
@@ -74,6 +75,13 @@ def _lib_plugin():
         L.sacc_plugin_enqueue.argtypes = [P, ctypes.POINTER(TensorDesc), ctypes.POINTER(TensorDesc), ctypes.POINTER(vp),
                                           ctypes.POINTER(vp), vp]
         L.sacc_plugin_enqueue.restype = i
+        L.sacc_plugin_workspace_bytes.argtypes = [P, ctypes.POINTER(TensorDesc), i32, ctypes.POINTER(ctypes.c_size_t)]
+        L.sacc_plugin_workspace_bytes.restype = i
+        L.sacc_plugin_block_fields.argtypes = [P, ctypes.POINTER(i32), ctypes.POINTER(i32)]
+        L.sacc_plugin_block_fields.restype = i
+        L.sacc_plugin_enqueue_ws.argtypes = [P, ctypes.POINTER(TensorDesc), ctypes.POINTER(TensorDesc), ctypes.POINTER(vp),
+                                             ctypes.POINTER(vp), vp, ctypes.c_size_t, vp]
+        L.sacc_plugin_enqueue_ws.restype = i
         L.sacc_plugin_last_error.argtypes = []
         L.sacc_plugin_last_error.restype = ctypes.c_char_p
         _bound = True
@@ -132,17 +140,29 @@ class ScanPlugin:
         _check(_lib_plugin().sacc_plugin_fields(self._h, *[ctypes.byref(x) for x in v]))
         return {k: x.value for k, x in zip(("has_d", "height", "width"), v) if x.value >= 0}
 
-    def output_types(self, in_types):
+    def output_types(self, in_types, nb_out=2):
         arr = (ctypes.c_int32 * len(in_types))(*in_types)
-        out = (ctypes.c_int32 * 2)()
-        _check(_lib_plugin().sacc_plugin_output_types(self._h, arr, len(in_types), out, 2))
+        out = (ctypes.c_int32 * nb_out)()
+        _check(_lib_plugin().sacc_plugin_output_types(self._h, arr, len(in_types), out, nb_out))
         return list(out)
 
-    def output_shapes(self, in_dims):
-        ins = (TensorDesc * len(in_dims))(*[TensorDesc.of(d) for d in in_dims])
-        outs = (TensorDesc * 2)()
-        _check(_lib_plugin().sacc_plugin_output_shapes(self._h, ins, len(in_dims), outs, 2))
-        return [outs[0].shape(), outs[1].shape()]
+    def output_shapes(self, in_dims, nb_out=2, in_types=None):
+        types = in_types or [TENSOR_FLOAT] * len(in_dims)
+        ins = (TensorDesc * len(in_dims))(*[TensorDesc.of(d, t) for d, t in zip(in_dims, types)])
+        outs = (TensorDesc * nb_out)()
+        _check(_lib_plugin().sacc_plugin_output_shapes(self._h, ins, len(in_dims), outs, nb_out))
+        return [outs[k].shape() for k in range(nb_out)]
+
+    def block_fields(self):
+        v = [ctypes.c_int32() for _ in range(2)]
+        _check(_lib_plugin().sacc_plugin_block_fields(self._h, *[ctypes.byref(x) for x in v]))
+        return {"dt_rank": v[0].value, "residual": v[1].value}
+
+    def workspace_bytes(self, in_descs) -> int:
+        arr = (TensorDesc * len(in_descs))(*in_descs)
+        n = ctypes.c_size_t()
+        _check(_lib_plugin().sacc_plugin_workspace_bytes(self._h, arr, len(in_descs), ctypes.byref(n)))
+        return n.value
 
     def supports_format(self, pos, descs, nb_in):
         arr = (TensorDesc * len(descs))(*descs)
@@ -154,10 +174,13 @@ class ScanPlugin:
     def bind(self):
         _check(_lib_plugin().sacc_plugin_bind(self._h))
 
-    def enqueue(self, in_descs, out_descs, inputs, outputs, stream):
+    def enqueue(self, in_descs, out_descs, inputs, outputs, stream, workspace=None, workspace_bytes=0):
         ind = (TensorDesc * len(in_descs))(*in_descs)
         outd = (TensorDesc * len(out_descs))(*out_descs)
         inp = (ctypes.c_void_p * len(inputs))(*inputs)
         outp = (ctypes.c_void_p * len(outputs))(*outputs)
         h = stream if isinstance(stream, int) else stream.cuda_stream
-        _check(_lib_plugin().sacc_plugin_enqueue(self._h, ind, outd, inp, outp, h))
+        if workspace is None:
+            _check(_lib_plugin().sacc_plugin_enqueue(self._h, ind, outd, inp, outp, h))
+        else:
+            _check(_lib_plugin().sacc_plugin_enqueue_ws(self._h, ind, outd, inp, outp, workspace, workspace_bytes, h))

@@ -122,3 +122,59 @@ def test_fp16_version_enqueue_rejects_fp32_descriptors():
     outs = [TensorDesc.of((4, 9, 8), H), TensorDesc.of((2,), I)]
     with pytest.raises(PluginError, match="kernels are not loaded|input 0 is not linear FP16|explicit non-default stream"):
         p.enqueue(descs, outs, [0x1000] * 6, [0x2000, 0x3000], 0x5EED)
+
+
+# ---------------------------------------------------------------- MambaBlock plugin
+
+from saccade_v1_b200.plugin import BLOCK, TENSOR_BF16  # noqa: E402
+
+HEAD = [(4, 240, 128), (512, 128), (256, 4), (256,), (33, 256), (256, 16), (256,), (256, 16), (256,), (128, 256)]
+FP32_IN = {2, 3, 6, 7, 8}
+
+
+def head_types(act=TENSOR_HALF):
+    return [TENSOR_FLOAT if i in FP32_IN else act for i in range(10)]
+
+
+def test_block_creator_fields_and_rejections():
+    p = ScanPlugin.create(*BLOCK, [("dt_rank", 16), ("residual", 1)])
+    assert p.block_fields() == {"dt_rank": 16, "residual": 1}
+    for fields, msg in (([("dt_rank", 16)], "missing field residual"), ([("dt_rank", 0), ("residual", 1)], "dt_rank must be positive"),
+                        ([("dt_rank", 8), ("residual", 2)], "residual must be 0 or 1"),
+                        ([("dt_rank", 8), ("residual", 1), ("has_d", 1)], "unknown field has_d")):
+        with pytest.raises(PluginError, match=msg) as e:
+            ScanPlugin.create(*BLOCK, fields)
+        assert str(e.value).startswith("saccade::MambaBlock creator: ")
+
+
+@pytest.mark.parametrize("act", [TENSOR_HALF, TENSOR_BF16])
+def test_block_types_shapes_formats(act):
+    p = ScanPlugin.create(*BLOCK, [("dt_rank", 16), ("residual", 1)])
+    types = head_types(act)
+    assert p.output_types(types, nb_out=1) == [act]
+    with pytest.raises(PluginError, match="input 2 is not FP32"):
+        p.output_types(types[:2] + [act] + types[3:], nb_out=1)
+    with pytest.raises(PluginError, match="input 4 differs in type from x"):
+        p.output_types(types[:4] + [TENSOR_FLOAT] + types[5:], nb_out=1)
+    assert p.output_shapes(HEAD, nb_out=1, in_types=types) == [(4, 240, 128)]
+    bad = list(HEAD)
+    bad[4] = (40, 256)  # neither rank-1 (16 + 16 + 1) nor full (16 + 32) C
+    with pytest.raises(PluginError, match="w_x"):
+        p.output_shapes(bad, nb_out=1, in_types=types)
+    io = [TensorDesc.of((1,), t) for t in types] + [TensorDesc.of((1,), act)]
+    assert all(p.supports_format(i, io, 10) for i in range(11))
+    wrong = list(io)
+    wrong[10] = TensorDesc.of((1,), TENSOR_FLOAT)
+    assert not p.supports_format(10, wrong, 10)
+    wrong = list(io)
+    wrong[7] = TensorDesc.of((1,), act)
+    assert not p.supports_format(7, wrong, 10)
+
+
+def test_block_workspace_needs_shapes():
+    p = ScanPlugin.create(*BLOCK, [("dt_rank", 16), ("residual", 1)])
+    assert p.workspace_size() == 0  # the shape-free query stays the scan plugins' 0
+    descs = [TensorDesc.of(d, t) for d, t in zip(HEAD, head_types())]
+    assert p.workspace_bytes(descs) > 4 * 240 * 256 * 2 * 4  # xz, u, y, ... of 960 tokens
+    scan = ScanPlugin.create(*SCAN, [("has_d", 1)])
+    assert scan.workspace_bytes([TensorDesc.of(d) for d in [(4, 9, 8), (4, 9, 8), (1, 4), (4, 9, 4), (4, 9, 1), (8,)]]) == 0

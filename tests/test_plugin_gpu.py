@@ -131,3 +131,34 @@ def test_fp16_plugin_enqueue_is_bitwise_the_direct_api(bad):
     ind[0].type = TENSOR_FLOAT
     with pytest.raises(PluginError, match="input 0 is not linear FP16"):
         p.enqueue(ind, outd, [t.data_ptr() for t in ins], [y.data_ptr(), st.data_ptr()], s)
+
+
+@pytest.mark.parametrize("dt,L", [("f16", 240), ("bf16", 60)])
+def test_block_plugin_is_bitwise_the_block_api(dt, L):
+    """saccade::MambaBlock v1 at the reference head's shapes (rank-1 C, no
+    RMSNorm, residual), given TensorRT's workspace, enqueues the same bits as
+    sacc_mamba_block_forward."""
+    from oracle import mamba_oracle as mo
+    from saccade_v1_b200.plugin import BLOCK, TENSOR_BF16
+    tt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    act = TENSOR_HALF if dt == "f16" else TENSOR_BF16
+    p = mo.random_block(31, 128, 256, 16, 16, 4, dt, norm=False, c_width=1)
+    s = gu.stream()
+    with torch.cuda.stream(s):
+        w = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).cuda().to(
+             tt if k in ("w_in", "w_x", "w_dt", "w_out") else torch.float32) for k, v in p.items()}
+        x = (torch.randn(4, L, 128, device="cuda") * 0.5).to(tt)
+        want = sb.mamba_block_forward(x, w, residual=True, stream=s)
+        ins = [x, w["w_in"], w["conv_w"], w["conv_b"], w["w_x"], w["w_dt"], w["dt_bias"], w["A"], w["D"], w["w_out"]]
+        descs = [TensorDesc.of(tuple(t.shape), TENSOR_FLOAT if t.dtype == torch.float32 else act) for t in ins]
+        plug = ScanPlugin.create(*BLOCK, [("dt_rank", 16), ("residual", 1)])
+        plug.bind()
+        nbytes = plug.workspace_bytes(descs)
+        ws = torch.empty(nbytes + 256, dtype=torch.uint8, device="cuda")
+        out = torch.empty_like(x)
+        plug.enqueue(descs, [TensorDesc.of(tuple(out.shape), act)], [t.data_ptr() for t in ins], [out.data_ptr()], s,
+                     workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+        with pytest.raises(PluginError, match="workspace"):
+            plug.enqueue(descs, [TensorDesc.of(tuple(out.shape), act)], [t.data_ptr() for t in ins], [out.data_ptr()], s)
+    s.synchronize()
+    assert torch.equal(out.view(torch.int16), want.view(torch.int16))

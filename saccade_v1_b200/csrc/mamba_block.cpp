@@ -31,12 +31,14 @@ struct Layout {
     bool fuse_dt; // dt_proj inside the scan
 };
 
-// Batch rows per scan call, so that each call stays within the int32
-// element capacity.
+// Batch rows per scan call: the bulk scan indexes rows (batch x channels) and
+// tokens (batch x length) with 32-bit integers and everything else with
+// 64-bit ones, so a call may hold any batch whose rows and tokens stay below
+// 2^31 (config 4's 512 x 4096 x 2048 layer is one call: 8192 units, 13.8 waves,
+// instead of eight 1024-unit calls of two waves, the second 73 % full).
 std::uint64_t scan_rows(const SaccMambaBlockArgs& a) {
-    const std::uint64_t per_seq = a.length * a.d_inner;
     std::uint64_t chunk = a.batch;
-    while (chunk > 1 && chunk * per_seq * 2 > kMaxElements) chunk = (chunk + 1) / 2;
+    while (chunk > 1 && (chunk * a.d_inner > kMaxElements || chunk * a.length > kMaxElements)) chunk = (chunk + 1) / 2;
     return chunk;
 }
 
@@ -147,8 +149,8 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
         return err;
 
     // Selective scan with D skip and SiLU(z) gate, (B, L, D) layout, z / B / C
-    // read in place through their row pitches; chunked by batch so that each
-    // call stays within the int32 element capacity.
+    // read in place through their row pitches; chunked by batch only where
+    // the scan's 32-bit row / token indices require it.
     const RowStrides pitch{2 * D, W, W};
     const std::uint64_t chunk = scan_rows(a);
     for (std::uint64_t b0 = 0; b0 < a.batch; b0 += chunk) {

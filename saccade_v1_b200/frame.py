@@ -61,12 +61,34 @@ def _addr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _need(name, t, dtype=None, numel=None, optional=False):
+    """Host check of a device buffer's type, layout and size (the C ABI sees only pointers)."""
+    if t is None:
+        if optional:
+            return
+        raise ScanInvalidArgument(f"{name} is required")
+    if not t.is_cuda or not t.is_contiguous():
+        raise ScanInvalidArgument(f"{name} must be a contiguous CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise ScanInvalidArgument(f"{name} must be {dtype}")
+    if numel is not None and t.numel() * t.element_size() < numel:
+        raise ScanInvalidArgument(f"{name} holds {t.numel() * t.element_size()} bytes, needs {numel}")
+
+
 def new_control(device="cuda") -> torch.Tensor:
     return torch.zeros(CONTROL_BYTES, dtype=torch.uint8, device=device)
 
 
 def new_records(capacity: int, device="cuda") -> torch.Tensor:
     return torch.zeros(max(capacity, 1) * RECORD_BYTES, dtype=torch.uint8, device=device)
+
+
+def _need_payload(control, payload, results, result_frames, records, capacity):
+    _need("control", control, numel=CONTROL_BYTES)
+    _need("payload", payload, torch.float32)
+    _need("results", results, torch.float32, 2 * payload.numel() * 4)
+    _need("result_frames", result_frames, torch.int64, 16)
+    _need("records", records, numel=max(capacity, 0) * RECORD_BYTES, optional=True)
 
 
 def scan_frame_load_kernels() -> str:
@@ -76,34 +98,45 @@ def scan_frame_load_kernels() -> str:
 
 
 def scan_frame_initialize(control, epoch: int, result_frames, stream=None) -> None:
+    _need("control", control, numel=CONTROL_BYTES)
+    _need("result_frames", result_frames, torch.int64, 16)
     _check(_lib.load().sacc_scan_frame_initialize(_addr(control), epoch, _addr(result_frames), _stream_handle(stream)))
 
 
 def scan_frame_begin(control, epoch: int, frame: int, stream=None) -> None:
+    _need("control", control, numel=CONTROL_BYTES)
     _check(_lib.load().sacc_scan_frame_begin(_addr(control), epoch, frame, _stream_handle(stream)))
 
 
 def scan_frame_gate(control, statuses, records=None, capacity: int = 0, stream=None) -> None:
+    _need("control", control, numel=CONTROL_BYTES)
+    _need("records", records, numel=max(capacity, 0) * RECORD_BYTES, optional=True)
     lst = _status_list(statuses)
     _check(_lib.load().sacc_scan_frame_gate(_addr(control), ctypes.byref(lst), _addr(records), capacity, _stream_handle(stream)))
 
 
 def scan_frame_publish(control, payload, results, result_frames, records=None, capacity: int = 0, stream=None) -> None:
+    _need_payload(control, payload, results, result_frames, records, capacity)
     _check(_lib.load().sacc_scan_frame_publish(_addr(control), _addr(payload), payload.numel(), _addr(results),
                                                _addr(result_frames), _addr(records), capacity, _stream_handle(stream)))
 
 
 def scan_frame_commit(control, stream=None) -> None:
+    _need("control", control, numel=CONTROL_BYTES)
     _check(_lib.load().sacc_scan_frame_commit(_addr(control), _stream_handle(stream)))
 
 
 def scan_frame_packet(control, packet, stream=None) -> None:
+    _need("control", control, numel=CONTROL_BYTES)
+    _need("packet", packet, numel=PACKET_BYTES)
     _check(_lib.load().sacc_scan_frame_packet(_addr(control), _addr(packet), _stream_handle(stream)))
 
 
 def scan_frame_step(control, epoch: int, frame: int, statuses, payload, results, result_frames, records=None,
                     capacity: int = 0, packet=None, stream=None) -> None:
     """begin + gate + publish + commit (+ packet) of one frame as one launch."""
+    _need_payload(control, payload, results, result_frames, records, capacity)
+    _need("packet", packet, numel=PACKET_BYTES, optional=True)
     lst = _status_list(statuses)
     _check(_lib.load().sacc_scan_frame_step(_addr(control), epoch, frame, ctypes.byref(lst), _addr(payload), payload.numel(),
                                             _addr(results), _addr(result_frames), _addr(records), capacity, _addr(packet),
@@ -111,6 +144,8 @@ def scan_frame_step(control, epoch: int, frame: int, statuses, payload, results,
 
 
 def scan_frame_check_finite(data, status, flag: int, stream=None) -> None:
+    _need("data", data, torch.float32)
+    _need("status", status, numel=8)
     _check(_lib.load().sacc_scan_frame_check_finite(_addr(data), data.numel(), _addr(status), flag, _stream_handle(stream)))
 
 
@@ -139,6 +174,10 @@ def model_producer_cuda(images, cls, reg, plugins, producer, workspace, stream=N
     nine status words ((9, 2) int32 tensor or nine rows); producer: int32 of 2."""
     if profile not in PROFILES:
         raise ScanInvalidArgument("unknown model profile (expected t01-640x640 or hr-1280x768)")
+    for name, t in [("images", images)] + [(f"cls[{i}]", c) for i, c in enumerate(cls)] + \
+            [(f"reg[{i}]", r) for i, r in enumerate(reg)]:
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ScanInvalidArgument(f"{name} must be a contiguous float32 tensor")
     raw = _lib.RawView()
     for level in range(3):
         raw.cls[level] = _addr(cls[level])

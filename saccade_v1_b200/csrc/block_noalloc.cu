@@ -21,7 +21,9 @@
 //
 // Sharing: every call on a device uses the same array, and the array keeps
 // the last call's contents.  Nothing in it needs to start at zero: each
-// intermediate is written in full before it is read.  Two calls whose work
+// intermediate is written in full before it is read, and the chunk-parallel
+// scan's hand-off flags in it are compared against a value that is new to
+// each launch, so flags left by an earlier call never match.  Two calls whose work
 // overlaps on the GPU (different streams without an event between them, or
 // different host threads) race on the array; order them on one stream.
 #include <cuda_runtime.h>

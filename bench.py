@@ -561,6 +561,7 @@ def secondary(torch, device, stream, peak, only=None, gemm_m=64 * 4096):
     """Other rows of the hot path, device-timed on this GPU (not part of `value`); `only` runs one of them."""
     runs = {"c3_step": c3_step, "c3_rescan": c3_rescan, "hr_deploy_f32_us": hr_deploy,
             "c1_block": lambda *a: c1_block(*a[:3]), "hr_head_block": lambda *a: hr_head_block(*a[:3]),
+            "hr_head_level": lambda *a: hr_head_level(*a[:3]),
             "gemm": lambda *a: gemm_probe(*a[:3], m=gemm_m),
             "frame_protocol": lambda *a: frame_protocol(*a[:3]),
             "c4_stack": lambda *a: c4_stack(*a[:3])}
@@ -735,6 +736,75 @@ def hr_head_block(torch, device, stream):
     return out
 
 
+def hr_head_level(torch, device, stream):
+    """The reference head's steps 3-5 at its three HR deploy levels (maps 24 x 40, 12 x 20, 6 x 10, d_model 128):
+    Cross-Scan expand, the Mamba block on the four directions (d_inner 256, N 16, dt_rank 16, rank-1 C, shared A,
+    residual on the tokens), merge.  Fused: sacc_cross_scan_block_forward per level.  Unfused, for comparison:
+    this library's expand kernel, an fp16 cast, the block, an FP32 cast and the merge kernel.  fp16 activations,
+    FP32 maps in and out; each variant's three levels replayed from one CUDA graph."""
+    import saccade_v1_b200 as sb
+    dm, D1, N1, R1 = 128, 256, 16, 16
+    p = synthetic_block(21, dm, D1, N1, R1)
+    r = np.random.default_rng(22)
+    p["w_x"] = p["w_x"][:R1 + N1 + 1]  # x_proj 256 -> 16 + 16 + 1
+    p["A"] = np.tile(-np.exp(r.uniform(-1, 1.5, (1, N1))).astype(np.float32), (D1, 1))
+    del p["norm_w"]
+    f16 = torch.float16
+    with torch.cuda.stream(stream):
+        dev = {k: (torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device=device, dtype=f16)
+                   if k in ("w_in", "w_x", "w_dt", "w_out") else torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(device))
+               for k, v in p.items()}
+        levels = []
+        for h, w in ((24, 40), (12, 20), (6, 10)):
+            x = torch.randn(1, dm, h, w, device=device) * 0.5
+            shape = sb.CrossScanShape(1, dm, h, w)
+            tok = torch.empty(4, h * w, dm, device=device)
+            lv = {"x": x, "out": torch.empty_like(x), "out2": torch.empty_like(x), "shape": shape, "tok": tok,
+                  "tok16": torch.empty(4, h * w, dm, device=device, dtype=f16), "r16": torch.empty(4, h * w, dm, device=device, dtype=f16),
+                  "r": torch.empty_like(tok), "st": torch.zeros(2, dtype=torch.int32, device=device),
+                  "ws": torch.empty(sb.cross_scan_block_workspace(x, dev, dtype=f16) + 256, dtype=torch.uint8, device=device)}
+            lv["ws_b"] = torch.empty(sb.mamba_block_workspace(lv["tok16"], dev) + 256, dtype=torch.uint8, device=device)
+            levels.append(lv)
+
+        def fused(lv):
+            sb.cross_scan_block_forward(lv["x"], dev, dtype=f16, out=lv["out"], workspace=lv["ws"], stream=stream)
+
+        def unfused(lv):
+            sb.cross_scan_expand_cuda(lv["shape"], lv["x"], lv["tok"], lv["st"], stream=stream)
+            lv["tok16"].copy_(lv["tok"])
+            sb.mamba_block_forward(lv["tok16"], dev, out=lv["r16"], workspace=lv["ws_b"], stream=stream)
+            lv["r"].copy_(lv["r16"])
+            sb.cross_scan_merge_cuda(lv["shape"], lv["r"], lv["out2"], lv["st"], stream=stream)
+
+        for lv in levels:
+            fused(lv)
+            unfused(lv)
+    stream.synchronize()
+    out = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for lv in levels:
+                fn(lv)
+
+        def replay():
+            with torch.cuda.stream(stream):
+                g.replay()
+
+        out[f"{name}_three_levels_us_graph"] = round(time_device(torch, stream, replay, 200), 2)
+        del g
+    stream.synchronize()
+    diff = max(float((lv["out"] - lv["out2"]).abs().max()) for lv in levels)
+    out["max_abs_diff_fused_vs_unfused"] = round(diff, 5)
+    flop_fused = sum(2 * lv["x"].shape[2] * lv["x"].shape[3] * (dm * 2 * D1 + 4 * D1 * (R1 + 2 * N1) + D1 * dm) for lv in levels)
+    flop_unfused = sum(2 * 4 * lv["x"].shape[2] * lv["x"].shape[3] * (dm * 2 * D1 + D1 * (R1 + 2 * N1) + D1 * dm) for lv in levels)
+    out["gemm_mflop_fused"] = round(flop_fused / 1e6, 1)
+    out["gemm_mflop_unfused"] = round(flop_unfused / 1e6, 1)
+    out["workload"] = ("reference head steps 3-5 x 3 HR levels (maps 24x40, 12x20, 6x10, d_model 128 FP32): expand, block "
+                       "(d_inner 256, N 16, dt_rank 16, rank-1 C, shared A, residual on the tokens, fp16), merge")
+    return out
+
+
 def gemm_probe(torch, device, stream, m=64 * 4096):
     """The tcgen05 projection GEMM at the config-4 in_proj shape of one 8-GPU shard (bf16 in, bf16 out;
     m = 64 tracks x 4096 tokens, n = 2 x d_inner, k = d_model)."""
@@ -840,7 +910,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-3 and deploy-shape timings")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (config 2: 64; smaller only for profiling)")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 stack (52 GB on one GPU)")
-    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "hr_head_block", "frame_protocol", "gemm",
+    ap.add_argument("--only", choices=["c3_step", "c3_rescan", "hr_deploy_f32_us", "c1_block", "hr_head_block", "hr_head_level",
+                                       "frame_protocol", "gemm",
                                        "c4_stack"],
                     help="run one secondary measurement alone on cuda:0 and print it (for profiling)")
     ap.add_argument("--gemm-m", type=int, default=64 * 4096, help="rows of the GEMM probe (smaller only for profiling)")

@@ -290,6 +290,39 @@ int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, si
 #define SACC_NOALLOC_SCRATCH_BYTES ((size_t)24 << 20)
 int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * sacc_cross_scan_block_forward -- one Cross-Scan head level with the expand
+ * and merge fused into the Mamba block.  Replaces the reference's steps 3-5 of
+ * a head level (src/head_trt_network.cpp:200-232): the CrossScanExpand plugin
+ * (cuda/selective_scan.cu:157-175, host :402-416), the block layers with the
+ * residual on the expanded tokens, and the CrossScanMerge plugin (:177-192,
+ * host :418-434):
+ *   tokens_k = expand_k(x)            direction k: 0 identity, 1 flip H and W, 2 flip W, 3 flip H
+ *   r_k = block(tokens_k) (+ tokens_k when block.residual)
+ *   out = (((r_0 + r_1) + r_2) + r_3) / 4 at each map position
+ * without materialising the (4 batch, H W, d_model) tokens: in_proj and
+ * out_proj act on each token alone, so in_proj runs once per map position and
+ * each direction reads its rows through the flip; the four directions' gated
+ * scan outputs are averaged per position (the merge's order and overflow
+ * rule) before one out_proj per position, whose epilogue adds x (a flip is an
+ * involution, so every direction's token at a position is x there).  The
+ * result equals the reference composition up to rounding (out_proj is linear).
+ * block: as for sacc_mamba_block_forward with batch = images and length =
+ * height * width; its x and out are not used.  x, out: (batch, d_model,
+ * height, width) FP32 maps, 16-byte aligned, not overlapping.  At most 65535
+ * images.  Workspace from sacc_cross_scan_block_workspace (256-byte aligned).
+ * ------------------------------------------------------------------------ */
+typedef struct SaccCrossScanBlockArgs {
+    SaccMambaBlockArgs block;
+    uint64_t height, width;
+    const float* x;
+    float* out;
+} SaccCrossScanBlockArgs;
+
+int sacc_cross_scan_block_workspace(const SaccCrossScanBlockArgs* args, size_t* bytes);
+int sacc_cross_scan_block_forward(const SaccCrossScanBlockArgs* args, void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

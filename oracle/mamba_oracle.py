@@ -83,3 +83,22 @@ def random_block(seed: int, d_model: int, d_inner: int, d_state: int, dt_rank: i
     if norm:
         p["norm_w"] = (1.0 + 0.1 * r.standard_normal(d_model)).astype(np.float32)
     return p
+
+
+def cross_block_forward(x, p, dt: str, eps: float = 1e-5, residual: bool = True) -> np.ndarray:
+    """One Cross-Scan head level in binary64, in the reference's order
+    (src/head_trt_network.cpp:200-232, steps 3-5): tokens = expand(x)
+    (cuda/selective_scan.cu:157-175; exact in FP32), r_k = block(tokens_k)
+    (+ tokens_k), out = merge(r) (:177-192).  x (B, C, H, W) float32; returns
+    (B, C, H, W) float64.  The block sees the tokens rounded to the activation
+    dtype (what the device's in_proj reads); the residual adds the FP32 tokens.
+    The device reorders this by linearity (in_proj once per position, the
+    merge before out_proj), so it agrees to rounding, not bit for bit."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, C, H, W = x.shape
+    L = H * W
+    tokens = oracle.cross_scan_expand(x, B, C, H, W).reshape(4 * B, L, C).astype(np.float64)
+    out = block_forward(rnd(tokens, dt), p, dt, eps, residual=False)
+    if residual:
+        out = out + tokens
+    return oracle.cross_scan_merge(out, B, C, H, W).reshape(B, C, H, W)

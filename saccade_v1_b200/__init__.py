@@ -15,6 +15,8 @@ from .scan import (  # noqa: F401
     gemm,
     identity,
     load_kernels,
+    cross_scan_block_forward,
+    cross_scan_block_workspace,
     mamba_block_forward,
     mamba_block_forward_noalloc,
     mamba_block_workspace,

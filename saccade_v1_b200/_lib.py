@@ -34,6 +34,8 @@ EXPORTS = (
     "sacc_mamba_block_workspace",
     "sacc_mamba_block_forward",
     "sacc_mamba_block_forward_noalloc",
+    "sacc_cross_scan_block_workspace",
+    "sacc_cross_scan_block_forward",
     "sacc_selective_scan_f16",
     # include/sacc_frame.h
     "sacc_scan_frame_load_kernels",
@@ -109,6 +111,11 @@ class MambaBlockArgs(ctypes.Structure):
                                        "w_out", "out")] + [("c_width", ctypes.c_int32)]
 
 
+class CrossScanBlockArgs(ctypes.Structure):
+    _fields_ = [("block", MambaBlockArgs), ("height", ctypes.c_uint64), ("width", ctypes.c_uint64),
+                ("x", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
 class FrameControl(ctypes.Structure):
     _fields_ = [("epoch", ctypes.c_uint64), ("current", ctypes.c_int64), ("committed", ctypes.c_int64),
                 ("fail_frame", ctypes.c_int64)] + [
@@ -173,6 +180,10 @@ def load() -> ctypes.CDLL:
     L.sacc_mamba_block_forward.restype = i
     L.sacc_mamba_block_forward_noalloc.argtypes = [ctypes.POINTER(MambaBlockArgs), vp]
     L.sacc_mamba_block_forward_noalloc.restype = i
+    L.sacc_cross_scan_block_workspace.argtypes = [ctypes.POINTER(CrossScanBlockArgs), ctypes.POINTER(ctypes.c_size_t)]
+    L.sacc_cross_scan_block_workspace.restype = i
+    L.sacc_cross_scan_block_forward.argtypes = [ctypes.POINTER(CrossScanBlockArgs), vp, sz, vp]
+    L.sacc_cross_scan_block_forward.restype = i
     i64, u64 = ctypes.c_int64, ctypes.c_uint64
     for name, args in (
             ("sacc_scan_frame_load_kernels", [ctypes.c_char_p, sz]),

@@ -29,7 +29,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FP_FLAGS = ["--ftz=false", "--prec-div=true", "--prec-sqrt=true", "--fmad=true"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-I" + os.path.join(ROOT, "include")]
-SOURCES = ["scan_f32.cu", "scan_ex.cu", "scan_bulk.cu", "scan_step.cu", "cross_scan.cu", "gemm_tcgen05.cu", "block_kernels.cu", "mamba_block.cpp", "block_noalloc.cu", "scan_frame.cu", "model_producer.cu", "scan_plugin.cpp", "capi.cpp"]
+SOURCES = ["scan_f32.cu", "scan_ex.cu", "scan_bulk.cu", "scan_step.cu", "cross_scan.cu", "gemm_tcgen05.cu", "block_kernels.cu", "cross_block.cu", "mamba_block.cpp", "block_noalloc.cu", "scan_frame.cu", "model_producer.cu", "scan_plugin.cpp", "capi.cpp"]
 
 
 def _flags_string() -> str:

@@ -266,6 +266,7 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
         CK(load_scan_step_kernels(text));
         CK(load_gemm_kernels(text));
         CK(load_block_kernels(text));
+        CK(load_cross_block_kernels(text));
         CK(load_frame_kernels(text));
         CK(load_producer_kernels(text));
         (void)sm_count();
@@ -553,6 +554,64 @@ int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_
             reject(api, "needs " + std::to_string(need) + " bytes of scratch, more than the static maximum of " +
                             std::to_string(kNoAllocScratchBytes) + "; use sacc_mamba_block_forward with a workspace");
         CK(launch_mamba_block_noalloc(*args, stream));
+    });
+}
+
+// One Cross-Scan head level (reference src/head_trt_network.cpp:200-232):
+// the block's shape rules with 4 x images sequences of height x width tokens,
+// FP32 maps for x and out.
+static void check_cross_block(const char* api, const SaccCrossScanBlockArgs& c) {
+    const SaccMambaBlockArgs& a = c.block;
+    if (c.height == 0 || c.width == 0) reject(api, "height and width must be positive");
+    if (c.height > 0xffffffffull || c.width > 0xffffffffull || a.length != c.height * c.width)
+        reject(api, "block.length must be height * width");
+    if (a.batch == 0 || a.batch > 65535) reject(api, "batch (images) must be in [1, 65535]");
+    SaccMambaBlockArgs v = a;
+    v.batch = 4 * a.batch; // the four directions' sequences
+    check_block_shape(api, v);
+    const std::uint64_t P = a.batch * a.length, D = a.d_inner, dm = a.d_model, R = a.dt_rank, N = a.d_state;
+    const Region x{c.x, P * dm * 4, "x"}, out{c.out, P * dm * 4, "out"};
+    require_pointer(api, x, 16);
+    require_pointer(api, out, 16);
+    for (const Region& r : {Region{a.w_in, 2 * D * dm * 2, "w_in"}, Region{a.w_x, (R + N + (a.c_width == 1 ? 1 : N)) * D * 2, "w_x"},
+                            Region{a.w_dt, D * R * 2, "w_dt"}, Region{a.w_out, dm * D * 2, "w_out"}})
+        require_pointer(api, r, 16);
+    for (const Region& r : {Region{a.conv_w, D * 4 * 4, "conv_w"}, Region{a.a, D * N * 4, "A"}})
+        require_pointer(api, r);
+    for (const Region& r : {Region{a.norm_w, a.norm_w ? dm * 4 : 0, "norm_w"}, Region{a.conv_b, a.conv_b ? D * 4 : 0, "conv_b"},
+                            Region{a.dt_bias, a.dt_bias ? D * 4 : 0, "dt_bias"}, Region{a.d, a.d ? D * 4 : 0, "D"}})
+        require_pointer(api, r);
+    if (overlaps(out, x)) reject(api, "out overlaps x");
+}
+
+int sacc_cross_scan_block_workspace(const SaccCrossScanBlockArgs* args, size_t* bytes) {
+    return guarded([&] {
+        constexpr const char* api = "cross_scan_block";
+        if (args == nullptr || bytes == nullptr) reject(api, "args and bytes are required");
+        const SaccCrossScanBlockArgs& c = *args;
+        if (c.height == 0 || c.width == 0 || c.height > 0xffffffffull || c.width > 0xffffffffull ||
+            c.block.length != c.height * c.width)
+            reject(api, "block.length must be height * width, both positive");
+        if (c.block.batch == 0 || c.block.batch > 65535) reject(api, "batch (images) must be in [1, 65535]");
+        SaccMambaBlockArgs v = c.block;
+        v.batch = 4 * c.block.batch;
+        check_block_shape(api, v);
+        *bytes = cross_block_workspace(c);
+    });
+}
+
+int sacc_cross_scan_block_forward(const SaccCrossScanBlockArgs* args, void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream) {
+    return guarded([&] {
+        constexpr const char* api = "cross_scan_block";
+        if (args == nullptr) reject(api, "args are required");
+        require_stream(api, stream);
+        check_cross_block(api, *args);
+        const std::size_t need = cross_block_workspace(*args);
+        if (workspace_bytes < need) reject(api, "workspace holds " + std::to_string(workspace_bytes) + " bytes, needs " +
+                                                    std::to_string(need));
+        require_pointer(api, Region{workspace, need, "workspace"}, 256);
+        CK(launch_cross_block(*args, workspace, stream));
     });
 }
 

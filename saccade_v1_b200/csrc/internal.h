@@ -107,6 +107,23 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
 // block needs more.
 constexpr std::size_t kNoAllocScratchBytes = SACC_NOALLOC_SCRATCH_BYTES;
 cudaError_t launch_mamba_block_noalloc(const SaccMambaBlockArgs& a, cudaStream_t stream);
+
+// One Cross-Scan head level, expand and merge fused into the block
+// (mamba_block.cpp; elementwise stages in cross_block.cu).
+std::size_t cross_block_workspace(const SaccCrossScanBlockArgs& c);
+cudaError_t launch_cross_block(const SaccCrossScanBlockArgs& c, void* workspace, cudaStream_t stream);
+// rows (batch, L, C) in dtype = x (batch, C, L) FP32, transposed.
+cudaError_t launch_rows_from_maps(int dtype, const float* x, unsigned long long batch, unsigned long long L,
+                                  unsigned long long C, void* rows, cudaStream_t stream);
+// u, z (4 batch, H W, D): conv + SiLU and gate of every direction, read from
+// the position-major in_proj rows xz (batch, H W, 2 D) through the flips.
+cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const float* bias, unsigned long long batch,
+                              unsigned long long H, unsigned long long W, unsigned long long D, void* u, void* z,
+                              cudaStream_t stream);
+// mean (batch, H W, D) = the merge of y (4 batch, H W, D) at each position.
+cudaError_t launch_cross_mean(int dtype, const void* y, unsigned long long batch, unsigned long long H, unsigned long long W,
+                              unsigned long long D, void* mean, cudaStream_t stream);
+cudaError_t load_cross_block_kernels(std::string& report);
 cudaError_t load_gemm_kernels(std::string& report);
 cudaError_t read_gemm_fault(unsigned* out, bool clear);
 cudaError_t load_scan_step_kernels(std::string& report);

@@ -280,6 +280,48 @@ def mamba_block_forward(x, params, *, eps=1e-5, residual=True, out=None, workspa
     return out
 
 
+def _cross_args(x, params, eps, residual, out, dtype):
+    if x.dim() != 4 or x.dtype != torch.float32 or not x.is_contiguous():
+        raise ScanInvalidArgument("cross_scan_block: x must be a contiguous (batch, d_model, height, width) float32 tensor")
+    batch, d_model, height, width = x.shape
+    # The block's shape fields from a stand-in of its (batch, length, d_model)
+    # input; the level reads x and writes out as maps, so block.x stays null.
+    blk = _block_args(torch.empty((), dtype=dtype).expand(batch, height * width, d_model), params, eps, residual, None)
+    blk.x = None
+    return _lib.CrossScanBlockArgs(blk, height, width, _ptr(x), _ptr(out))
+
+
+def cross_scan_block_workspace(x, params, eps=1e-5, residual=True, dtype=torch.bfloat16) -> int:
+    n = ctypes.c_size_t(0)
+    args = _cross_args(x, params, eps, residual, None, dtype)
+    _check(_lib.load().sacc_cross_scan_block_workspace(ctypes.byref(args), ctypes.byref(n)))
+    return n.value
+
+
+def cross_scan_block_forward(x, params, *, eps=1e-5, residual=True, dtype=torch.bfloat16, out=None, workspace=None,
+                             stream=None):
+    """One Cross-Scan head level: expand x into four scan directions, the Mamba
+    block on each (with the residual on the tokens when `residual`), and the
+    merge back to the map, in one call without the expanded tokens
+    (reference src/head_trt_network.cpp:200-232).
+
+    x (batch, d_model, height, width) float32; params as for
+    mamba_block_forward, weights in `dtype` (bf16 / fp16, the block's
+    activation type); returns out like x (float32).
+    """
+    if out is None:
+        out = torch.empty_like(x)
+    args = _cross_args(x, params, eps, residual, out, dtype)
+    need = cross_scan_block_workspace(x, params, eps, residual, dtype)
+    if workspace is None:
+        workspace = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+    base = workspace.data_ptr()
+    off = (-base) % 256
+    _check(_lib.load().sacc_cross_scan_block_forward(ctypes.byref(args), base + off, workspace.numel() - off,
+                                                     _stream_handle(stream)))
+    return out
+
+
 def mamba_block_forward_noalloc(x, params, *, eps=1e-5, residual=True, out=None, stream=None):
     """mamba_block_forward with the intermediates in the library's static
     device scratch (SACC_NOALLOC_SCRATCH_BYTES per device) instead of a

@@ -304,8 +304,9 @@ int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_
  * out_proj act on each token alone, so in_proj runs once per map position and
  * each direction reads its rows through the flip; the four directions' gated
  * scan outputs are averaged per position (the merge's order and overflow
- * rule) before one out_proj per position, whose epilogue adds x (a flip is an
- * involution, so every direction's token at a position is x there).  The
+ * rule) before one out_proj per position, and x is added as the maps are
+ * written (a flip is an involution, so every direction's token at a position
+ * is x there).  The
  * result equals the reference composition up to rounding (out_proj is linear).
  * block: as for sacc_mamba_block_forward with batch = images and length =
  * height * width; its x and out are not used.  x, out: (batch, d_model,

@@ -12,8 +12,9 @@
 //   * cross_conv reads the conv window of every direction through src and
 //     writes u and the gate z of the 4 batch sequences the scan walks;
 //   * cross_mean averages the four directions' gated scan outputs at each
-//     position (the merge's order and overflow rule), and one out_proj per
-//     position follows, with x as the residual: every direction's token at a
+//     position (the merge's order and overflow rule), one out_proj per
+//     position follows (FP32 rows), and maps_from_rows writes them back to
+//     the maps adding x as the residual: every direction's token at a
 //     position is x there (each flip is an involution).
 // src(k, t): direction 0 identity, 1 flip H and W, 2 flip W, 3 flip H.
 #include <cuda_bf16.h>
@@ -91,6 +92,27 @@ __global__ void __launch_bounds__(kTile* kRows) rows_from_maps_kernel(const floa
     for (int r = threadIdx.y; r < kTile; r += kRows) {
         const unsigned p = p0 + r, c = c0 + threadIdx.x;
         if (c < C && p < L) rows[(static_cast<unsigned long long>(b) * L + p) * C + c] = from_f32<T>(tile[threadIdx.x][r]);
+    }
+}
+
+// out[b, c, p] = rows[b, p, c] (+ x[b, c, p]), FP32.  grid (ceil(L/32),
+// ceil(C/32), batch); reads coalesced along channels, writes along positions.
+__global__ void __launch_bounds__(kTile* kRows) maps_from_rows_kernel(const float* __restrict__ rows, const float* __restrict__ x,
+                                                                      unsigned L, unsigned C, float* __restrict__ out) {
+    pdl_wait();
+    __shared__ float tile[kTile][kTile + 1];
+    const unsigned b = blockIdx.z, p0 = blockIdx.x * kTile, c0 = blockIdx.y * kTile;
+    for (int r = threadIdx.y; r < kTile; r += kRows) {
+        const unsigned p = p0 + r, c = c0 + threadIdx.x;
+        if (c < C && p < L) tile[r][threadIdx.x] = rows[(static_cast<unsigned long long>(b) * L + p) * C + c];
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < kTile; r += kRows) {
+        const unsigned c = c0 + r, p = p0 + threadIdx.x;
+        if (c < C && p < L) {
+            const unsigned long long i = (static_cast<unsigned long long>(b) * C + c) * L + p;
+            out[i] = x ? tile[threadIdx.x][r] + x[i] : tile[threadIdx.x][r];
+        }
     }
 }
 
@@ -187,6 +209,16 @@ cudaError_t launch_rows_from_maps(int dtype, const float* x, unsigned long long 
         return launch_pdl_k(rows_from_maps_kernel<__nv_bfloat16>, grid, dim3(kTile, kRows), 0, stream, x, l, c,
                             static_cast<__nv_bfloat16*>(rows));
     return launch_pdl_k(rows_from_maps_kernel<__half>, grid, dim3(kTile, kRows), 0, stream, x, l, c, static_cast<__half*>(rows));
+}
+
+cudaError_t launch_maps_from_rows(const float* rows, const float* x, unsigned long long batch, unsigned long long L,
+                                  unsigned long long C, float* out, cudaStream_t stream) {
+    if (batch > 65535 || (L + kTile - 1) / kTile > 0x7fffffffull || (C + kTile - 1) / kTile > 65535 || L * C > 0xffffffffull)
+        return cudaErrorInvalidConfiguration;
+    const dim3 grid(static_cast<unsigned>((L + kTile - 1) / kTile), static_cast<unsigned>((C + kTile - 1) / kTile),
+                    static_cast<unsigned>(batch));
+    return launch_pdl_k(maps_from_rows_kernel, grid, dim3(kTile, kRows), 0, stream, rows, x, static_cast<unsigned>(L),
+                        static_cast<unsigned>(C), out);
 }
 
 cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const float* bias, unsigned long long batch,

@@ -178,7 +178,14 @@ __device__ __forceinline__ void apply_chunk(const GemmParams& p, unsigned long l
         }
     }
     if (p.residual) {
-        if (full && p.res_vec) {
+        if (full && p.res_vec && p.out_dtype == SACC_DTYPE_F32) {
+            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.residual) + row * p.ldr + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 t = src[q];
+                v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+            }
+        } else if (full && p.res_vec) {
             const uint4* src = reinterpret_cast<const uint4*>(static_cast<const std::uint16_t*>(p.residual) + row * p.ldr + col0);
             const bool bf = p.out_dtype == SACC_DTYPE_BF16;
 #pragma unroll
@@ -501,8 +508,7 @@ cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     p.kblocks = static_cast<int>((a.k + kBK - 1) / kBK);
     const std::size_t eo = a.out_dtype == SACC_DTYPE_F32 ? 4 : 2;
     p.vec_store = (reinterpret_cast<std::uintptr_t>(a.c) % 16 == 0) && ((a.ldc * eo) % 16 == 0);
-    p.res_vec = a.residual && a.out_dtype != SACC_DTYPE_F32 && (reinterpret_cast<std::uintptr_t>(a.residual) % 16 == 0) &&
-                ((a.ldr * 2) % 16 == 0);
+    p.res_vec = a.residual && (reinterpret_cast<std::uintptr_t>(a.residual) % 16 == 0) && ((a.ldr * eo) % 16 == 0);
     CUtensorMap tc{};
     p.tma_store = a.out_dtype != SACC_DTYPE_F32 && p.vec_store && c_map(&tc, a.out_dtype, a.c, a.n, a.m, a.ldc);
     if (bn == 64) return launch_bn<64>(ta, tb, tc, p, sms, stream);

@@ -115,6 +115,9 @@ cudaError_t launch_cross_block(const SaccCrossScanBlockArgs& c, void* workspace,
 // rows (batch, L, C) in dtype = x (batch, C, L) FP32, transposed.
 cudaError_t launch_rows_from_maps(int dtype, const float* x, unsigned long long batch, unsigned long long L,
                                   unsigned long long C, void* rows, cudaStream_t stream);
+// out (batch, C, L) FP32 = rows (batch, L, C) FP32 transposed (+ x).
+cudaError_t launch_maps_from_rows(const float* rows, const float* x, unsigned long long batch, unsigned long long L,
+                                  unsigned long long C, float* out, cudaStream_t stream);
 // u, z (4 batch, H W, D): conv + SiLU and gate of every direction, read from
 // the position-major in_proj rows xz (batch, H W, 2 D) through the flips.
 cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const float* bias, unsigned long long batch,

@@ -154,7 +154,7 @@ cudaError_t xproj_scan(const SaccMambaBlockArgs& a, const void* u, const void* z
 // Workspace of one Cross-Scan head level: P = images x positions map rows,
 // M = 4 P direction tokens.
 struct CrossLayout {
-    std::size_t r, wn, wx, rows, xz, u, z, dbc, delta, y, mean, scan, scan_bytes, total;
+    std::size_t r, wn, wx, rows, xz, u, z, dbc, delta, y, mean, out_rows, scan, scan_bytes, total;
     bool fuse_dt;
 };
 
@@ -192,6 +192,7 @@ CrossLayout plan_cross(const SaccCrossScanBlockArgs& c) {
     l.delta = l.fuse_dt ? 0 : take(M * D * e);
     l.y = take(M * D * e);
     l.mean = take(P * D * e);
+    l.out_rows = take(P * dm * sizeof(float));
     l.scan = l.scan_bytes ? take(l.scan_bytes) : 0;
     l.total = off;
     return l;
@@ -279,17 +280,14 @@ cudaError_t launch_cross_block(const SaccCrossScanBlockArgs& c, void* workspace,
                           stream)) != cudaSuccess)
         return err;
 
-    // The merge of the gated outputs per position, then out_proj per image
-    // as out^T = W_out mean^T, which lands in the maps' (d_model, positions)
-    // layout, FP32, with x as the residual.
+    // The merge of the gated outputs per position, out_proj per position
+    // (FP32 rows), and the rows back to the maps with x as the residual.
     if ((err = launch_cross_mean(dt_, ws + l.y, B, c.height, c.width, D, mean, stream)) != cudaSuccess) return err;
-    for (std::uint64_t b = 0; b < B; ++b) {
-        g = gemm_args(dt_, dm, L, D, a.w_out, D, static_cast<unsigned char*>(mean) + b * L * D * 2, D, c.out + b * dm * L, L);
-        g.out_dtype = SACC_DTYPE_F32;
-        g.residual = a.residual ? c.x + b * dm * L : nullptr;
-        g.ldr = L;
-        if ((err = launch_gemm(g, stream)) != cudaSuccess) return err;
-    }
+    float* orows = reinterpret_cast<float*>(ws + l.out_rows);
+    g = gemm_args(dt_, P, dm, D, mean, D, a.w_out, D, orows, dm);
+    g.out_dtype = SACC_DTYPE_F32;
+    if ((err = launch_gemm(g, stream)) != cudaSuccess) return err;
+    if ((err = launch_maps_from_rows(orows, a.residual ? c.x : nullptr, B, L, dm, c.out, stream)) != cudaSuccess) return err;
     return cudaSuccess;
 }
 

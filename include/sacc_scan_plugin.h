@@ -22,6 +22,14 @@
  *                                (all alike), conv_w / conv_b / dt_bias / A / D
  *                                kFLOAT; a workspace (sacc_plugin_workspace_bytes)
  *                                runs sacc_mamba_block_forward; no status output.
+ *   saccade::CrossScanMambaBlock v1  fields: dt_rank, residual (INT32); the
+ *                                head level's CrossScanExpand -> block -> merge
+ *                                (src/head_trt_network.cpp:200-232) as one plugin
+ *                                (sacc_cross_scan_block_forward): inputs as
+ *                                MambaBlock except x, the kFLOAT map (B, d_model,
+ *                                H, W); the weights' type (w_in) sets the
+ *                                activation type; output the kFLOAT map
+ *                                (B, d_model, H, W); workspace required.
  *   saccade::CrossScanExpand v1  fields: none
  *   saccade::CrossScanMerge  v1  fields: height, width (INT32)
  * Each entry point below implements one IPluginV3 / IPluginCreatorV3One method
@@ -53,6 +61,8 @@ extern "C" {
 #define SACC_PLUGIN_MERGE_VERSION "1"
 #define SACC_PLUGIN_BLOCK_NAME "MambaBlock"
 #define SACC_PLUGIN_BLOCK_VERSION "1"
+#define SACC_PLUGIN_LEVEL_NAME "CrossScanMambaBlock"
+#define SACC_PLUGIN_LEVEL_VERSION "1"
 
 /* Field and tensor type tags (the adapter maps TensorRT's PluginFieldType,
  * DataType and TensorFormat values onto these). */
@@ -103,10 +113,10 @@ int sacc_plugin_supports_format(const SaccScanPlugin* plugin, int32_t pos, const
                                 int32_t nb_out);
 /* getWorkspaceSize (:184-186): always 0 for the scan plugins. */
 size_t sacc_plugin_workspace_size(const SaccScanPlugin* plugin);
-/* getWorkspaceSize with the (maximum) input shapes: the MambaBlock plugin's
- * workspace in bytes, 0 for the others. */
+/* getWorkspaceSize with the (maximum) input shapes: the MambaBlock and
+ * CrossScanMambaBlock plugins' workspace in bytes, 0 for the others. */
 int sacc_plugin_workspace_bytes(const SaccScanPlugin* plugin, const SaccTensorDesc* in, int32_t nb_in, size_t* bytes);
-/* getFieldsToSerialize of the MambaBlock plugin. */
+/* getFieldsToSerialize of the MambaBlock and CrossScanMambaBlock plugins. */
 int sacc_plugin_block_fields(const SaccScanPlugin* plugin, int32_t* dt_rank, int32_t* residual);
 /* configurePlugin / attachToContext (:171-180, 233-242): load every kernel in
  * the current CUDA context and bind the plugin to that context. */
@@ -115,8 +125,8 @@ int sacc_plugin_bind(SaccScanPlugin* plugin);
  * descriptor checks (:299-341), then the operator on `stream`. */
 int sacc_plugin_enqueue(const SaccScanPlugin* plugin, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
                         const void* const* inputs, void* const* outputs, cudaStream_t stream);
-/* enqueue with TensorRT's workspace (required by MambaBlock, ignored by the
- * scan plugins). */
+/* enqueue with TensorRT's workspace (required by MambaBlock and
+ * CrossScanMambaBlock, ignored by the scan plugins). */
 int sacc_plugin_enqueue_ws(const SaccScanPlugin* plugin, const SaccTensorDesc* in_desc, const SaccTensorDesc* out_desc,
                            const void* const* inputs, void* const* outputs, void* workspace, size_t workspace_bytes,
                            cudaStream_t stream);

@@ -5,7 +5,8 @@
 // (src/scan_trt_plugin.cpp:69-455); saccade::SelectiveScan v3 is the same
 // scan with FP16 activations (u, delta, B, C, y) for FP16 engines, and
 // saccade::MambaBlock v1 the whole head block (sacc_mamba_block_forward) with
-// TensorRT's workspace.  TensorRT itself is not available on this
+// TensorRT's workspace, and saccade::CrossScanMambaBlock v1 a head level's
+// expand -> block -> merge on the FP32 maps (sacc_cross_scan_block_forward).  TensorRT itself is not available on this
 // platform, so the plugin's logic lives here behind a C ABI whose calls map
 // one to one onto the IPluginV3 methods; a thin TensorRT adapter (see
 // INTEGRATION.md) translates TensorRT's descriptor and field types into these
@@ -39,7 +40,7 @@
 namespace sacc {
 namespace {
 
-enum class Op { scan, expand, merge, block };
+enum class Op { scan, expand, merge, block, level };
 
 struct Identity {
     const char* name;
@@ -50,7 +51,8 @@ Identity identity_of(Op op) {
     return op == Op::scan    ? Identity{SACC_PLUGIN_SCAN_NAME, SACC_PLUGIN_SCAN_VERSION}
          : op == Op::expand  ? Identity{SACC_PLUGIN_EXPAND_NAME, SACC_PLUGIN_EXPAND_VERSION}
          : op == Op::merge   ? Identity{SACC_PLUGIN_MERGE_NAME, SACC_PLUGIN_MERGE_VERSION}
-                             : Identity{SACC_PLUGIN_BLOCK_NAME, SACC_PLUGIN_BLOCK_VERSION};
+         : op == Op::block   ? Identity{SACC_PLUGIN_BLOCK_NAME, SACC_PLUGIN_BLOCK_VERSION}
+                             : Identity{SACC_PLUGIN_LEVEL_NAME, SACC_PLUGIN_LEVEL_VERSION};
 }
 
 // MambaBlock inputs: x, w_in, conv_w, conv_b, w_x, w_dt, dt_bias, A, D, w_out.
@@ -109,9 +111,10 @@ struct SaccScanPlugin {
     std::int32_t has_d, height, width;
     unsigned long long bound_context = 0; // 0: kernels not loaded for any context
     bool half = false;                    // SelectiveScan v3: FP16 activations
-    std::int32_t dt_rank = 0, residual = 0; // MambaBlock fields
-    int inputs() const { return op == sacc::Op::scan ? 5 + has_d : op == sacc::Op::block ? sacc::kBlockInputs : 1; }
-    int outputs() const { return op == sacc::Op::block ? 1 : 2; }
+    std::int32_t dt_rank = 0, residual = 0; // MambaBlock / CrossScanMambaBlock fields
+    bool blockish() const { return op == sacc::Op::block || op == sacc::Op::level; }
+    int inputs() const { return op == sacc::Op::scan ? 5 + has_d : blockish() ? sacc::kBlockInputs : 1; }
+    int outputs() const { return blockish() ? 1 : 2; }
     std::string prefix() const { return std::string(SACC_PLUGIN_NAMESPACE) + "::" + sacc::identity_of(op).name + ": "; }
     // Data type of tensor `pos` (inputs, then y, then status).
     int32_t type_at(int pos) const {
@@ -241,6 +244,34 @@ std::string check_block(const SaccScanPlugin& p, const SaccTensorDesc* in, const
     return "";
 }
 
+// CrossScanMambaBlock descriptors -> level arguments, or why not: x and the
+// output are the FP32 maps (batch, d_model, height, width), w_in sets the
+// activation type, and the weights follow MambaBlock's rules.
+std::string check_level(const SaccScanPlugin& p, const SaccTensorDesc* in, const SaccTensorDesc* out, SaccCrossScanBlockArgs& c) {
+    const SaccTensorDesc& x = in[0];
+    if (x.type != SACC_TENSOR_FLOAT || x.format != SACC_FORMAT_LINEAR) return "input 0 is not linear FP32";
+    if (x.nb_dims != 4) return "x must be (batch, d_model, height, width)";
+    for (int k = 0; k < 4; ++k)
+        if (x.dims[k] < 1) return "input 0 has an empty or unresolved dimension";
+    if (!activation_type(in[1].type)) return "input 1 is not FP16 or BF16";
+    if (out[0].type != SACC_TENSOR_FLOAT || out[0].format != SACC_FORMAT_LINEAR ||
+        !equal(out[0], {x.dims[0], x.dims[1], x.dims[2], x.dims[3]}))
+        return "out " + text(out[0]) + " differs from x";
+    // The block's view: (batch, height * width, d_model) tokens of w_in's type.
+    SaccTensorDesc tok[kBlockInputs];
+    for (int i = 0; i < kBlockInputs; ++i) tok[i] = in[i];
+    tok[0] = SaccTensorDesc{3, {x.dims[0], x.dims[2] * x.dims[3], x.dims[1]}, in[1].type, SACC_FORMAT_LINEAR};
+    const SaccTensorDesc o = tok[0];
+    SaccMambaBlockArgs a{};
+    const std::string why = check_block(p, tok, &o, a);
+    if (!why.empty()) return why;
+    c = SaccCrossScanBlockArgs{};
+    c.block = a;
+    c.height = static_cast<std::uint64_t>(x.dims[2]);
+    c.width = static_cast<std::uint64_t>(x.dims[3]);
+    return "";
+}
+
 } // namespace
 } // namespace sacc
 
@@ -270,6 +301,8 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
             op = Op::merge;
         else if (name && !std::strcmp(name, SACC_PLUGIN_BLOCK_NAME) && version && !std::strcmp(version, SACC_PLUGIN_BLOCK_VERSION))
             op = Op::block;
+        else if (name && !std::strcmp(name, SACC_PLUGIN_LEVEL_NAME) && version && !std::strcmp(version, SACC_PLUGIN_LEVEL_VERSION))
+            op = Op::level;
         else
             throw PluginError{SACC_EINVAL, std::string("plugin creator not registered: ") + SACC_PLUGIN_NAMESPACE + "::" +
                                                (name ? name : "(null)") + " v" + (version ? version : "(null)")};
@@ -280,7 +313,8 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
             names[n_names++] = "height";
             names[n_names++] = "width";
         }
-        if (op == Op::block) {
+        const bool blockish = op == Op::block || op == Op::level;
+        if (blockish) {
             names[n_names++] = "dt_rank";
             names[n_names++] = "residual";
         }
@@ -305,11 +339,11 @@ int sacc_plugin_create(const char* name, const char* version, const SaccPluginFi
         if (op == Op::scan && value[0] != 0 && value[0] != 1) throw PluginError{SACC_EINVAL, who + "has_d must be 0 or 1"};
         if (op == Op::merge && (value[0] < 1 || value[1] < 1))
             throw PluginError{SACC_EINVAL, who + "height and width must be positive"};
-        if (op == Op::block && value[0] < 1) throw PluginError{SACC_EINVAL, who + "dt_rank must be positive"};
-        if (op == Op::block && value[1] != 0 && value[1] != 1) throw PluginError{SACC_EINVAL, who + "residual must be 0 or 1"};
+        if (blockish && value[0] < 1) throw PluginError{SACC_EINVAL, who + "dt_rank must be positive"};
+        if (blockish && value[1] != 0 && value[1] != 1) throw PluginError{SACC_EINVAL, who + "residual must be 0 or 1"};
         *out = new SaccScanPlugin{op, op == Op::scan ? value[0] : 1, op == Op::merge ? value[0] : 0,
                                   op == Op::merge ? value[1] : 0, 0, half,
-                                  op == Op::block ? value[0] : 0, op == Op::block ? value[1] : 0};
+                                  blockish ? value[0] : 0, blockish ? value[1] : 0};
     });
 }
 
@@ -334,7 +368,8 @@ int sacc_plugin_fields(const SaccScanPlugin* p, int32_t* has_d, int32_t* height,
 
 int sacc_plugin_block_fields(const SaccScanPlugin* p, int32_t* dt_rank, int32_t* residual) {
     return plugin_guard([&] {
-        if (!p || p->op != Op::block) throw PluginError{SACC_EINVAL, "sacc_plugin_block_fields: a MambaBlock plugin is required"};
+        if (!p || !p->blockish())
+            throw PluginError{SACC_EINVAL, "sacc_plugin_block_fields: a MambaBlock or CrossScanMambaBlock plugin is required"};
         if (dt_rank) *dt_rank = p->dt_rank;
         if (residual) *residual = p->residual;
     });
@@ -344,6 +379,15 @@ int sacc_plugin_output_types(const SaccScanPlugin* p, const int32_t* in_types, i
     return plugin_guard([&] {
         if (!p) throw PluginError{SACC_EINVAL, "sacc_plugin_output_types: plugin is required"};
         if (nb_in != p->inputs() || nb_out != p->outputs() || !in_types || !out_types) fail(p, "input or output count");
+        if (p->op == Op::level) {
+            if (in_types[0] != SACC_TENSOR_FLOAT) fail(p, "input 0 is not FP32");
+            if (!activation_type(in_types[1])) fail(p, "input 1 is not FP16 or BF16");
+            for (std::int32_t i = 2; i < nb_in; ++i)
+                if (in_types[i] != (block_fp32_input(i) ? SACC_TENSOR_FLOAT : in_types[1]))
+                    fail(p, "input " + std::to_string(i) + (block_fp32_input(i) ? " is not FP32" : " differs in type from w_in"));
+            out_types[0] = SACC_TENSOR_FLOAT;
+            return;
+        }
         if (p->op == Op::block) {
             if (!activation_type(in_types[0])) fail(p, "input 0 is not FP16 or BF16");
             for (std::int32_t i = 1; i < nb_in; ++i)
@@ -366,6 +410,14 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
     return plugin_guard([&] {
         if (!p) throw PluginError{SACC_EINVAL, "sacc_plugin_output_shapes: plugin is required"};
         if (nb_in != p->inputs() || nb_out != p->outputs() || !in || !out) fail(p, "input or output count");
+        if (p->op == Op::level) {
+            SaccTensorDesc o{4, {in[0].dims[0], in[0].dims[1], in[0].dims[2], in[0].dims[3]}, SACC_TENSOR_FLOAT, SACC_FORMAT_LINEAR};
+            SaccCrossScanBlockArgs c{};
+            const std::string why = check_level(*p, in, &o, c);
+            if (!why.empty()) fail(p, why);
+            out[0] = o;
+            return;
+        }
         if (p->op == Op::block) {
             SaccTensorDesc o{3, {in[0].dims[0], in[0].dims[1], in[0].dims[2]}, in[0].type, SACC_FORMAT_LINEAR};
             SaccMambaBlockArgs a{};
@@ -415,6 +467,13 @@ int sacc_plugin_output_shapes(const SaccScanPlugin* p, const SaccTensorDesc* in,
 int sacc_plugin_supports_format(const SaccScanPlugin* p, int32_t pos, const SaccTensorDesc* io, int32_t nb_in, int32_t nb_out) {
     if (!p || !io || nb_in != p->inputs() || nb_out != p->outputs() || pos < 0 || pos >= nb_in + nb_out) return 0;
     if (io[pos].format != SACC_FORMAT_LINEAR) return 0;
+    if (p->op == Op::level) {
+        // The maps (x, output) FP32; w_in decides the activation type (FP16 or
+        // BF16) of the other weights; conv, bias, A and D rows FP32.
+        if (pos == 0 || pos == nb_in) return io[pos].type == SACC_TENSOR_FLOAT;
+        if (pos == 1) return activation_type(io[1].type);
+        return io[pos].type == (block_fp32_input(pos) ? SACC_TENSOR_FLOAT : io[1].type);
+    }
     if (p->op == Op::block) {
         // x decides the activation type (FP16 or BF16); weights in that type, the
         // conv, bias, A and D rows in FP32, the output like x.
@@ -454,8 +513,17 @@ int sacc_plugin_workspace_bytes(const SaccScanPlugin* p, const SaccTensorDesc* i
     return plugin_guard([&] {
         if (!p || !bytes) throw PluginError{SACC_EINVAL, "sacc_plugin_workspace_bytes: plugin and bytes are required"};
         *bytes = 0;
-        if (p->op != Op::block) return;
+        if (!p->blockish()) return;
         if (!in_desc || nb_in != p->inputs()) fail(p, "input count");
+        if (p->op == Op::level) {
+            SaccTensorDesc o{4, {in_desc[0].dims[0], in_desc[0].dims[1], in_desc[0].dims[2], in_desc[0].dims[3]}, SACC_TENSOR_FLOAT,
+                             SACC_FORMAT_LINEAR};
+            SaccCrossScanBlockArgs c{};
+            const std::string why = check_level(*p, in_desc, &o, c);
+            if (!why.empty()) fail(p, why);
+            if (sacc_cross_scan_block_workspace(&c, bytes) != SACC_OK) fail(p, sacc_last_error());
+            return;
+        }
         SaccTensorDesc o{3, {in_desc[0].dims[0], in_desc[0].dims[1], in_desc[0].dims[2]}, in_desc[0].type, SACC_FORMAT_LINEAR};
         SaccMambaBlockArgs a{};
         const std::string why = check_block(*p, in_desc, &o, a);
@@ -480,9 +548,10 @@ int sacc_plugin_enqueue_ws(const SaccScanPlugin* p, const SaccTensorDesc* in_des
             d.ctx_id(of_stream, &id) != CUDA_SUCCESS)
             fail(p, "the stream does not belong to the current CUDA context");
         if (id != p->bound_context) fail(p, "the kernels were loaded in another CUDA context");
-        if (p->op == Op::block) {
-            SaccMambaBlockArgs a{};
-            const std::string why = check_block(*p, in_desc, out_desc, a);
+        if (p->blockish()) {
+            SaccCrossScanBlockArgs c{};
+            SaccMambaBlockArgs& a = c.block;
+            const std::string why = p->op == Op::level ? check_level(*p, in_desc, out_desc, c) : check_block(*p, in_desc, out_desc, a);
             if (!why.empty()) fail(p, why);
             a.x = in[0];
             a.w_in = in[1];
@@ -495,7 +564,16 @@ int sacc_plugin_enqueue_ws(const SaccScanPlugin* p, const SaccTensorDesc* in_des
             a.d = static_cast<const float*>(in[8]);
             a.w_out = in[9];
             a.out = out[0];
-            const int rc = sacc_mamba_block_forward(&a, workspace, workspace_bytes, stream);
+            int rc;
+            if (p->op == Op::level) {
+                c.x = static_cast<const float*>(in[0]);
+                c.out = static_cast<float*>(out[0]);
+                a.x = nullptr;
+                a.out = nullptr;
+                rc = sacc_cross_scan_block_forward(&c, workspace, workspace_bytes, stream);
+            } else {
+                rc = sacc_mamba_block_forward(&a, workspace, workspace_bytes, stream);
+            }
             if (rc != SACC_OK) fail(p, sacc_last_error(), rc);
             return;
         }

@@ -18,6 +18,7 @@ FORMAT_LINEAR, FORMAT_OTHER = 0, 99
 SCAN, EXPAND, MERGE = ("SelectiveScan", "2"), ("CrossScanExpand", "1"), ("CrossScanMerge", "1")
 SCAN_F16 = ("SelectiveScan", "3")  # FP16 u, delta, B, C, y; FP32 A, D
 BLOCK = ("MambaBlock", "1")         # the head Mamba block; fields dt_rank, residual
+LEVEL = ("CrossScanMambaBlock", "1")  # a head level: expand -> block -> merge on FP32 maps; fields dt_rank, residual
 
 
 class PluginError(ValueError):

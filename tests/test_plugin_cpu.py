@@ -178,3 +178,54 @@ def test_block_workspace_needs_shapes():
     assert p.workspace_bytes(descs) > 4 * 240 * 256 * 2 * 4  # xz, u, y, ... of 960 tokens
     scan = ScanPlugin.create(*SCAN, [("has_d", 1)])
     assert scan.workspace_bytes([TensorDesc.of(d) for d in [(4, 9, 8), (4, 9, 8), (1, 4), (4, 9, 4), (4, 9, 1), (8,)]]) == 0
+
+
+# ---------------------------------------------------------------- CrossScanMambaBlock plugin
+
+from saccade_v1_b200.plugin import LEVEL  # noqa: E402
+
+LEVEL_HEAD = [(1, 128, 12, 20)] + HEAD[1:]
+
+
+def level_types(act=TENSOR_HALF):
+    return [TENSOR_FLOAT] + head_types(act)[1:]
+
+
+def test_level_creator_fields_and_rejections():
+    p = ScanPlugin.create(*LEVEL, [("dt_rank", 16), ("residual", 1)])
+    assert p.block_fields() == {"dt_rank": 16, "residual": 1}
+    with pytest.raises(PluginError, match="missing field residual") as e:
+        ScanPlugin.create(*LEVEL, [("dt_rank", 16)])
+    assert str(e.value).startswith("saccade::CrossScanMambaBlock creator: ")
+
+
+@pytest.mark.parametrize("act", [TENSOR_HALF, TENSOR_BF16])
+def test_level_types_shapes_formats(act):
+    """x and the output are the FP32 maps; w_in sets the activation type."""
+    p = ScanPlugin.create(*LEVEL, [("dt_rank", 16), ("residual", 1)])
+    types = level_types(act)
+    assert p.output_types(types, nb_out=1) == [TENSOR_FLOAT]
+    with pytest.raises(PluginError, match="input 0 is not FP32"):
+        p.output_types([act] + types[1:], nb_out=1)
+    with pytest.raises(PluginError, match="input 9 differs in type from w_in"):
+        p.output_types(types[:9] + [TENSOR_FLOAT], nb_out=1)
+    assert p.output_shapes(LEVEL_HEAD, nb_out=1, in_types=types) == [(1, 128, 12, 20)]
+    with pytest.raises(PluginError, match=r"x must be \(batch, d_model, height, width\)"):
+        p.output_shapes([(1, 240, 128)] + HEAD[1:], nb_out=1, in_types=types)
+    bad = list(LEVEL_HEAD)
+    bad[9] = (128, 128)  # w_out not (d_model, d_inner)
+    with pytest.raises(PluginError, match="w_out"):
+        p.output_shapes(bad, nb_out=1, in_types=types)
+    io = [TensorDesc.of((1,), t) for t in types] + [TensorDesc.of((1,), TENSOR_FLOAT)]
+    assert all(p.supports_format(i, io, 10) for i in range(11))
+    for pos, t in ((0, act), (10, act), (4, TENSOR_FLOAT)):
+        wrong = list(io)
+        wrong[pos] = TensorDesc.of((1,), t)
+        assert not p.supports_format(pos, wrong, 10)
+
+
+def test_level_workspace_needs_shapes():
+    p = ScanPlugin.create(*LEVEL, [("dt_rank", 16), ("residual", 1)])
+    assert p.workspace_size() == 0
+    descs = [TensorDesc.of(d, t) for d, t in zip(LEVEL_HEAD, level_types())]
+    assert p.workspace_bytes(descs) > 4 * 240 * 256 * 2 * 3  # u, z, y of the four directions' 960 tokens

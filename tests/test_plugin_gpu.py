@@ -162,3 +162,33 @@ def test_block_plugin_is_bitwise_the_block_api(dt, L):
             plug.enqueue(descs, [TensorDesc.of(tuple(out.shape), act)], [t.data_ptr() for t in ins], [out.data_ptr()], s)
     s.synchronize()
     assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("dt,hw", [("f16", (12, 20)), ("bf16", (6, 10))])
+def test_level_plugin_is_bitwise_the_level_api(dt, hw):
+    """saccade::CrossScanMambaBlock v1 (a head level's expand -> block ->
+    merge on the FP32 maps), given TensorRT's workspace, enqueues the same
+    bits as sacc_cross_scan_block_forward."""
+    from oracle import mamba_oracle as mo
+    from saccade_v1_b200.plugin import LEVEL, TENSOR_BF16
+    tt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    act = TENSOR_HALF if dt == "f16" else TENSOR_BF16
+    p = mo.random_block(32, 128, 256, 16, 16, 4, dt, norm=False, c_width=1)
+    s = gu.stream()
+    with torch.cuda.stream(s):
+        w = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).cuda().to(
+             tt if k in ("w_in", "w_x", "w_dt", "w_out") else torch.float32) for k, v in p.items()}
+        x = torch.randn(1, 128, *hw, device="cuda") * 0.5
+        want = sb.cross_scan_block_forward(x, w, dtype=tt, stream=s)
+        ins = [x, w["w_in"], w["conv_w"], w["conv_b"], w["w_x"], w["w_dt"], w["dt_bias"], w["A"], w["D"], w["w_out"]]
+        descs = [TensorDesc.of(tuple(t.shape), TENSOR_FLOAT if t.dtype == torch.float32 else act) for t in ins]
+        plug = ScanPlugin.create(*LEVEL, [("dt_rank", 16), ("residual", 1)])
+        plug.bind()
+        ws = torch.empty(plug.workspace_bytes(descs) + 256, dtype=torch.uint8, device="cuda")
+        out = torch.empty_like(x)
+        plug.enqueue(descs, [TensorDesc.of(tuple(out.shape), TENSOR_FLOAT)], [t.data_ptr() for t in ins], [out.data_ptr()], s,
+                     workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+        with pytest.raises(PluginError, match="workspace"):
+            plug.enqueue(descs, [TensorDesc.of(tuple(out.shape), TENSOR_FLOAT)], [t.data_ptr() for t in ins], [out.data_ptr()], s)
+    s.synchronize()
+    assert torch.equal(out.view(torch.int32), want.view(torch.int32))

@@ -81,6 +81,32 @@ def test_pointer_rules_without_gpu():
         assert rc == _lib.SACC_EINVAL and diag in _lib.last_error(), _lib.last_error()
 
 
+def _level_args(batch=1, height=6, width=10, length=None, d_model=128, x=0x100000, out=0x200000):
+    """A Cross-Scan head level's arguments with fake (never dereferenced) device addresses."""
+    blk = _lib.MambaBlockArgs(batch, height * width if length is None else length, d_model, 256, 16, 4, 16,
+                              _lib.DTYPE_BF16, 1, 1e-5, None, None, 0x300000, 0x400000, 0x410000, 0x420000, 0x430000,
+                              0x440000, 0x450000, 0x460000, 0x470000, None, 1)
+    return _lib.CrossScanBlockArgs(blk, height, width, x, out)
+
+
+@pytest.mark.parametrize("kw,diag", [
+    ({"length": 59}, "block.length must be height * width"),
+    ({"batch": 0}, "batch (images) must be in [1, 65535]"),
+    ({"d_model": 64}, "d_inner and d_model must be positive multiples of 128"),
+    ({"out": 0x100000 + 4096}, "out overlaps x"),
+    ({"x": 0x100004}, "x is not 16-byte aligned"),
+])
+def test_cross_scan_level_rejections_without_gpu(kw, diag):
+    """sacc_cross_scan_block_forward rejects bad shapes and buffers on the host, before any CUDA call."""
+    L = _lib.load()
+    args = _level_args(**kw)
+    rc = L.sacc_cross_scan_block_forward(ctypes.byref(args), 0x900000, 1 << 30, FAKE_STREAM)
+    assert rc == _lib.SACC_EINVAL and diag in _lib.last_error(), _lib.last_error()
+    assert _lib.last_error().startswith("cross_scan_block: ")
+    rc = L.sacc_cross_scan_block_forward(ctypes.byref(_level_args()), 0x900000, 1 << 30, 0)
+    assert rc == _lib.SACC_EINVAL and "explicit non-default stream" in _lib.last_error()
+
+
 def test_cpp_adapter_compiles_and_links(tmp_path):
     """include/sacc_scan.hpp gives reference-signature C++ (selective_scan_cuda etc.) over the C ABI."""
     import shutil

@@ -33,6 +33,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cfloat>
 #include <climits>
 #include <cstdint>
@@ -420,6 +421,28 @@ const void* pick_kernel_t(unsigned state) {
 
 const void* pick_kernel(unsigned state, bool half) { return half ? pick_kernel_t<__half>(state) : pick_kernel_t<float>(state); }
 
+// CTAs of the FP32 scan kernel for `state` that one SM holds at once, queried
+// once per state count.  The FP16-activation launch uses the FP32 kernel's
+// figure too, so both split a lane into the same chunks and the FP16 outputs
+// stay the FP32 outputs rounded.
+int resident_per_sm(unsigned state) {
+    static std::atomic<int> cache[6] = {};
+    int idx = 0;
+    while ((1u << idx) < state && idx < 5) ++idx;
+    int v = cache[idx].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+    const void* fn = pick_kernel(state, false);
+    const size_t smem = static_cast<size_t>(kThreads) * state * sizeof(float2);
+    int n = 0;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+        n = 1;
+    else if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1)
+        n = 1;
+    cache[idx].store(n, std::memory_order_relaxed);
+    return n;
+}
+
 unsigned long long total_checked(const CheckList& l) {
     unsigned long long n = 0;
     for (unsigned i = 0; i < l.size; ++i) n += l.tensor[i].count;
@@ -443,11 +466,16 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     p.vec_b = (reinterpret_cast<std::uintptr_t>(s.b) & vec_align) == 0;
     p.vec_c = (reinterpret_cast<std::uintptr_t>(s.c) & vec_align) == 0;
     p.check = s.check;
-    // Chunks: enough (lane, chunk) threads for ~4 warps per SM scheduler, at
-    // least 4 tokens per chunk, at most 64 chunks; one chunk when lanes suffice.
-    const unsigned long long target = static_cast<unsigned long long>(sm_count) * 512ull;
+    // Chunks: as many (lane, chunk) threads as the SMs hold at once (one wave:
+    // a chunk's work grows with L / K and its fold with K, and a second wave
+    // doubles the time), at least 4 tokens per chunk, at most 64 chunks; one
+    // chunk when the lanes alone fill the SMs.  At 165 registers an SM holds
+    // one 256-thread CTA of the N = 16 kernel, so the HR deploy level of 1,024
+    // lanes x 960 tokens runs 32 chunks in 128 CTAs.
+    const unsigned long long target =
+        static_cast<unsigned long long>(sm_count) * static_cast<unsigned long long>(resident_per_sm(s.state)) * kThreads;
     int K = 1;
-    while (K < 64 && s.lanes * static_cast<unsigned long long>(K) < target &&
+    while (K < 64 && s.lanes * static_cast<unsigned long long>(K) * 2ull <= target &&
            s.length >= static_cast<unsigned long long>(K) * 2ull * 4ull)
         K *= 2;
     p.chunks = K;

@@ -468,7 +468,7 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     p.check = s.check;
     // Chunks: as many (lane, chunk) threads as the SMs hold at once (one wave:
     // a chunk's work grows with L / K and its fold with K, and a second wave
-    // doubles the time), at least 4 tokens per chunk, at most 64 chunks; one
+    // doubles the time), at least 2 tokens per chunk, at most 64 chunks; one
     // chunk when the lanes alone fill the SMs.  At 165 registers an SM holds
     // one 256-thread CTA of the N = 16 kernel, so the HR deploy level of 1,024
     // lanes x 960 tokens runs 32 chunks in 128 CTAs.
@@ -476,7 +476,7 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
         static_cast<unsigned long long>(sm_count) * static_cast<unsigned long long>(resident_per_sm(s.state)) * kThreads;
     int K = 1;
     while (K < 64 && s.lanes * static_cast<unsigned long long>(K) * 2ull <= target &&
-           s.length >= static_cast<unsigned long long>(K) * 2ull * 4ull)
+           s.length >= static_cast<unsigned long long>(K) * 2ull * 2ull)
         K *= 2;
     p.chunks = K;
     p.lanes_per_cta = kThreads / K;

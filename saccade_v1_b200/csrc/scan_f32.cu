@@ -422,7 +422,8 @@ const void* pick_kernel_t(unsigned state) {
 const void* pick_kernel(unsigned state, bool half) { return half ? pick_kernel_t<__half>(state) : pick_kernel_t<float>(state); }
 
 // CTAs of the FP32 scan kernel for `state` that one SM holds at once, queried
-// once per state count.  The FP16-activation launch uses the FP32 kernel's
+// once per state count and process (every GPU of a process is taken to be
+// alike; the kernel loader fills the figures).  The FP16-activation launch uses the FP32 kernel's
 // figure too, so both split a lane into the same chunks and the FP16 outputs
 // stay the FP32 outputs rounded.
 int resident_per_sm(unsigned state) {
@@ -544,6 +545,9 @@ cudaError_t load_scan_f32_kernels(std::string& report) {
                   " local_bytes=" + std::to_string(attr.localSizeBytes) + " shared_bytes=" +
                   std::to_string(attr.sharedSizeBytes) + " max_threads=" + std::to_string(attr.maxThreadsPerBlock) + "\n";
     }
+    // The chunk split's residency figures, so that no call queries them later.
+    for (unsigned state = 1; state <= 32; state *= 2) report += "scan_f32_resident_ctas_per_sm_n" + std::to_string(state) + "=" +
+                                                               std::to_string(resident_per_sm(state)) + "\n";
     return cudaSuccess;
 }
 

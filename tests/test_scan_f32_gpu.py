@@ -30,6 +30,9 @@ import saccade_v1_b200 as sb  # noqa: E402
 def loaded():
     report = sb.load_kernels()
     assert "scan_f32_n16" in report
+    # The loader also fills the residency figures the chunk split uses (>= 1 CTA per SM).
+    resident = dict(line.split("=") for line in report.splitlines() if line.startswith("scan_f32_resident_ctas_per_sm_n"))
+    assert len(resident) == 6 and all(int(v) >= 1 for v in resident.values()), resident
     return report
 
 

@@ -144,32 +144,29 @@ __device__ __forceinline__ void load_row(const T* p, float (&out)[N], bool vec) 
 }
 
 // Operands of one token of one lane.
-template <int N>
+// One token of a lane: u, raw delta, the B row and the C row (CW = N values,
+// or one value broadcast over the states when C has width 1).
+template <int N, int CW>
 struct Token {
     float u, x;
     float b[N];
-    float c[N];
+    float c[CW];
 };
 
-template <typename T, int N>
-__device__ __forceinline__ void load_token(const Params& p, unsigned long long token, unsigned long long d, Token<N>& k) {
+template <typename T, int N, int CW>
+__device__ __forceinline__ void load_token(const Params& p, unsigned long long token, unsigned long long d, Token<N, CW>& k) {
     const unsigned long long at = token * p.channels + d;
     k.u = load_act(static_cast<const T*>(p.u) + at);
     k.x = load_act(static_cast<const T*>(p.delta) + at);
     load_row<T, N>(static_cast<const T*>(p.b) + token * N, k.b, p.vec_b);
-    if (p.c_full) {
-        load_row<T, N>(static_cast<const T*>(p.c) + token * N, k.c, p.vec_c);
-    } else {
-        const float cv = load_act(static_cast<const T*>(p.c) + token);
-#pragma unroll
-        for (int n = 0; n < N; ++n) k.c[n] = cv;
-    }
+    if constexpr (CW > 1) load_row<T, N>(static_cast<const T*>(p.c) + token * N, k.c, p.vec_c);
+    else k.c[0] = load_act(static_cast<const T*>(p.c) + token);
 }
 
 // New states of one token; returns false when the plain FP32 products may
 // differ from the reference's scaled ones (then the caller uses the scaled form).
-template <int N>
-__device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a)[N], const Token<N>& k, float (&hn)[N],
+template <int N, int CW>
+__device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a)[N], const Token<N, CW>& k, float (&hn)[N],
                                             float (&decay)[N], float (&drive)[N]) {
     if (!(k.x >= -80.0f)) return false;
     const float dv = k.x > 20.0f ? k.x : log1pf(expf(k.x));
@@ -186,8 +183,8 @@ __device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a
 }
 
 // The reference's scaled per-token state update (cuda/selective_scan.cu:189-192).
-template <int N>
-__device__ __forceinline__ void states_scaled(const float (&h)[N], const float (&a)[N], const Token<N>& k, float (&hn)[N],
+template <int N, int CW>
+__device__ __forceinline__ void states_scaled(const float (&h)[N], const float (&a)[N], const Token<N, CW>& k, float (&hn)[N],
                                            float (&decay)[N], float (&drive)[N]) {
     const Scaled dl = softplus_scaled(k.x), su = split(k.u);
 #pragma unroll
@@ -200,10 +197,10 @@ __device__ __forceinline__ void states_scaled(const float (&h)[N], const float (
 }
 
 // Pass 1: state update without outputs, accumulating the decay product.
-template <int N>
-__device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], const float (&a)[N], const Token<N>& k) {
+template <int N, int CW>
+__device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], const float (&a)[N], const Token<N, CW>& k) {
     float hn[N], decay[N], drive[N];
-    if (!states_fast<N>(h, a, k, hn, decay, drive)) states_scaled<N>(h, a, k, hn, decay, drive);
+    if (!states_fast<N, CW>(h, a, k, hn, decay, drive)) states_scaled<N, CW>(h, a, k, hn, decay, drive);
 #pragma unroll
     for (int n = 0; n < N; ++n) {
         h[n] = hn[n];
@@ -214,16 +211,16 @@ __device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], cons
 // Pass 2: one token with output and the reference's failure order
 // (cuda/selective_scan.cu:193-212).  Returns the failure bits (0 = ok).  With
 // kHalfOut an output that FP16 cannot hold is an output range failure.
-template <int N, bool kHalfOut>
-__device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N], const Token<N>& k, bool has_d, float skip_d,
+template <int N, int CW, bool kHalfOut>
+__device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N], const Token<N, CW>& k, bool has_d, float skip_d,
                                              float& y) {
     float hn[N], decay[N], drive[N];
-    if (!states_fast<N>(h, a, k, hn, decay, drive)) states_scaled<N>(h, a, k, hn, decay, drive);
+    if (!states_fast<N, CW>(h, a, k, hn, decay, drive)) states_scaled<N, CW>(h, a, k, hn, decay, drive);
     unsigned fail = 0;
     float term[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) {
-        term[n] = __fmul_rn(k.c[n], hn[n]);
+        term[n] = __fmul_rn(k.c[CW > 1 ? n : 0], hn[n]);
         fail |= !finite32(decay[n]) ? kDecay : !finite32(drive[n]) ? kDrive : !finite32(hn[n]) ? kState
               : !finite32(term[n]) ? kTerm : 0u;
         h[n] = hn[n];
@@ -299,7 +296,7 @@ __device__ void check_tensors(const CheckList& list, unsigned long long first, u
     if (found) atomicOr(&status->flags, found);
 }
 
-template <typename T, int N>
+template <typename T, int N, int CW>
 __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanStatus* status) {
     if (blockIdx.x >= p.scan_blocks) {
         const unsigned long long first = static_cast<unsigned long long>(blockIdx.x - p.scan_blocks) * kThreads + threadIdx.x;
@@ -330,12 +327,12 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
 #pragma unroll
         for (int n = 0; n < N; ++n) prod[n] = 1.0f;
         if (active && k < K - 1) {
-            Token<N> cur;
-            if (t0 < t1) load_token<T, N>(p, bb * L + t0, d, cur);
+            Token<N, CW> cur;
+            if (t0 < t1) load_token<T, N, CW>(p, bb * L + t0, d, cur);
             for (unsigned long long t = t0; t < t1; ++t) {
-                Token<N> nxt;
-                if (t + 1 < t1) load_token<T, N>(p, bb * L + t + 1, d, nxt);
-                step_carry<N>(h, prod, a, cur);
+                Token<N, CW> nxt;
+                if (t + 1 < t1) load_token<T, N, CW>(p, bb * L + t + 1, d, nxt);
+                step_carry<N, CW>(h, prod, a, cur);
                 cur = nxt;
             }
         }
@@ -358,13 +355,13 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
 
     unsigned fail = 0;
     if (active && t0 < t1) {
-        Token<N> cur;
-        load_token<T, N>(p, bb * L + t0, d, cur);
+        Token<N, CW> cur;
+        load_token<T, N, CW>(p, bb * L + t0, d, cur);
         for (unsigned long long t = t0; t < t1; ++t) {
-            Token<N> nxt;
-            if (t + 1 < t1) load_token<T, N>(p, bb * L + t + 1, d, nxt);
+            Token<N, CW> nxt;
+            if (t + 1 < t1) load_token<T, N, CW>(p, bb * L + t + 1, d, nxt);
             float y = 0.0f;
-            fail = step_out<N, std::is_same_v<T, __half>>(h, a, cur, p.has_d != 0, skip_d, y);
+            fail = step_out<N, CW, std::is_same_v<T, __half>>(h, a, cur, p.has_d != 0, skip_d, y);
             if (fail) break;
             store_act(static_cast<T*>(p.y) + (bb * L + t) * Dc + d, y);
             cur = nxt;
@@ -402,37 +399,41 @@ __global__ void __launch_bounds__(kThreads) finalize_kernel(W* out, unsigned lon
     if (first == 0) status->done = SACC_SCAN_DONE;
 }
 
-template <typename T, int N>
+// CW: the C row's width, N (full) or 1 (one C per token).
+template <typename T, int N, int CW = N>
 const void* scan_kernel_ptr() {
-    return reinterpret_cast<const void*>(scan_f32_kernel<T, N>);
+    return reinterpret_cast<const void*>(scan_f32_kernel<T, N, CW>);
 }
 
 template <typename T>
-const void* pick_kernel_t(unsigned state) {
+const void* pick_kernel_t(unsigned state, bool c_full) {
     switch (state) {
     case 1: return scan_kernel_ptr<T, 1>();
-    case 2: return scan_kernel_ptr<T, 2>();
-    case 4: return scan_kernel_ptr<T, 4>();
-    case 8: return scan_kernel_ptr<T, 8>();
-    case 16: return scan_kernel_ptr<T, 16>();
-    default: return scan_kernel_ptr<T, 32>();
+    case 2: return c_full ? scan_kernel_ptr<T, 2>() : scan_kernel_ptr<T, 2, 1>();
+    case 4: return c_full ? scan_kernel_ptr<T, 4>() : scan_kernel_ptr<T, 4, 1>();
+    case 8: return c_full ? scan_kernel_ptr<T, 8>() : scan_kernel_ptr<T, 8, 1>();
+    case 16: return c_full ? scan_kernel_ptr<T, 16>() : scan_kernel_ptr<T, 16, 1>();
+    default: return c_full ? scan_kernel_ptr<T, 32>() : scan_kernel_ptr<T, 32, 1>();
     }
 }
 
-const void* pick_kernel(unsigned state, bool half) { return half ? pick_kernel_t<__half>(state) : pick_kernel_t<float>(state); }
+const void* pick_kernel(unsigned state, bool half, bool c_full) {
+    return half ? pick_kernel_t<__half>(state, c_full) : pick_kernel_t<float>(state, c_full);
+}
 
-// CTAs of the FP32 scan kernel for `state` that one SM holds at once, queried
-// once per state count and process (every GPU of a process is taken to be
-// alike; the kernel loader fills the figures).  The FP16-activation launch uses the FP32 kernel's
-// figure too, so both split a lane into the same chunks and the FP16 outputs
-// stay the FP32 outputs rounded.
-int resident_per_sm(unsigned state) {
-    static std::atomic<int> cache[6] = {};
+// CTAs of the FP32 scan kernel for (`state`, C width) that one SM holds at
+// once, queried once per kernel and process (every GPU of a process is taken
+// to be alike; the kernel loader fills the figures).  The FP16-activation
+// launch uses the FP32 kernel's figure too, so both split a lane into the same
+// chunks and the FP16 outputs stay the FP32 outputs rounded.
+int resident_per_sm(unsigned state, bool c_full) {
+    static std::atomic<int> cache[12] = {};
     int idx = 0;
     while ((1u << idx) < state && idx < 5) ++idx;
+    idx = 2 * idx + (c_full ? 1 : 0);
     int v = cache[idx].load(std::memory_order_relaxed);
     if (v > 0) return v;
-    const void* fn = pick_kernel(state, false);
+    const void* fn = pick_kernel(state, false, c_full);
     const size_t smem = static_cast<size_t>(kThreads) * state * sizeof(float2);
     int n = 0;
     if (smem > 48 * 1024 &&
@@ -474,7 +475,7 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     // one 256-thread CTA of the N = 16 kernel, so the HR deploy level of 1,024
     // lanes x 960 tokens runs 32 chunks in 128 CTAs.
     const unsigned long long target =
-        static_cast<unsigned long long>(sm_count) * static_cast<unsigned long long>(resident_per_sm(s.state)) * kThreads;
+        static_cast<unsigned long long>(sm_count) * static_cast<unsigned long long>(resident_per_sm(s.state, s.c_full)) * kThreads;
     int K = 1;
     while (K < 64 && s.lanes * static_cast<unsigned long long>(K) * 2ull <= target &&
            s.length >= static_cast<unsigned long long>(K) * 2ull * 2ull)
@@ -487,7 +488,7 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     const unsigned extra = check_blocks(total_checked(s.check), sm_count);
     const size_t smem = K > 1 ? static_cast<size_t>(kThreads) * s.state * sizeof(float2) : 0;
     void* args[] = {&p, &status};
-    const void* fn = pick_kernel(s.state, s.half);
+    const void* fn = pick_kernel(s.state, s.half, s.c_full);
     if (smem > 48 * 1024) {
         // Also set by the kernel loader; repeated here so that a call before
         // sacc_scan_load_kernels still launches.
@@ -529,6 +530,16 @@ cudaError_t load_scan_f32_kernels(std::string& report) {
         {"scan_f16io_n8", scan_kernel_ptr<__half, 8>(), kThreads * 8 * sizeof(float2)},
         {"scan_f16io_n16", scan_kernel_ptr<__half, 16>(), kThreads * 16 * sizeof(float2)},
         {"scan_f16io_n32", scan_kernel_ptr<__half, 32>(), kThreads * 32 * sizeof(float2)},
+        {"scan_f32_c1_n2", scan_kernel_ptr<float, 2, 1>(), kThreads * 2 * sizeof(float2)},
+        {"scan_f32_c1_n4", scan_kernel_ptr<float, 4, 1>(), kThreads * 4 * sizeof(float2)},
+        {"scan_f32_c1_n8", scan_kernel_ptr<float, 8, 1>(), kThreads * 8 * sizeof(float2)},
+        {"scan_f32_c1_n16", scan_kernel_ptr<float, 16, 1>(), kThreads * 16 * sizeof(float2)},
+        {"scan_f32_c1_n32", scan_kernel_ptr<float, 32, 1>(), kThreads * 32 * sizeof(float2)},
+        {"scan_f16io_c1_n2", scan_kernel_ptr<__half, 2, 1>(), kThreads * 2 * sizeof(float2)},
+        {"scan_f16io_c1_n4", scan_kernel_ptr<__half, 4, 1>(), kThreads * 4 * sizeof(float2)},
+        {"scan_f16io_c1_n8", scan_kernel_ptr<__half, 8, 1>(), kThreads * 8 * sizeof(float2)},
+        {"scan_f16io_c1_n16", scan_kernel_ptr<__half, 16, 1>(), kThreads * 16 * sizeof(float2)},
+        {"scan_f16io_c1_n32", scan_kernel_ptr<__half, 32, 1>(), kThreads * 32 * sizeof(float2)},
         {"check", reinterpret_cast<const void*>(check_kernel), 0},
         {"finalize", reinterpret_cast<const void*>(finalize_kernel<unsigned, 0x7fc00000u>), 0},
         {"finalize_f16", reinterpret_cast<const void*>(finalize_kernel<unsigned short, 0x7e00u>), 0},
@@ -547,7 +558,9 @@ cudaError_t load_scan_f32_kernels(std::string& report) {
     }
     // The chunk split's residency figures, so that no call queries them later.
     for (unsigned state = 1; state <= 32; state *= 2) report += "scan_f32_resident_ctas_per_sm_n" + std::to_string(state) + "=" +
-                                                               std::to_string(resident_per_sm(state)) + "\n";
+                                                               std::to_string(resident_per_sm(state, true)) + "\n";
+    for (unsigned state = 2; state <= 32; state *= 2) report += "scan_f32_c1_resident_ctas_per_sm_n" + std::to_string(state) + "=" +
+                                                               std::to_string(resident_per_sm(state, false)) + "\n";
     return cudaSuccess;
 }
 

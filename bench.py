@@ -18,6 +18,14 @@ same metric through the public API with the inputs copied from pinned host
 memory and y copied back inside the timed region.  `roofline` compares the
 scan kernel against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
 
+`secondary` (skipped with --no-secondary; `--only NAME` runs one alone) times
+the other rows of the path on the device: config 3's L = 1 step, packed
+re-scan and frame average, config 1's Mamba block, the reference ABI at the
+HR deploy shapes (FP32, FP16 plugin v3, FP32 with casts; eager and from a
+CUDA graph), the HR head block and the fused Cross-Scan head level (against
+its unfused composition), the frame-end protocol, the projection GEMM and
+config 4's four-layer stack.
+
 --impl reference times the reference's own CPU implementation
 (selective_scan_reference built from its sources into oracle/_ref) on all host
 cores over a bounded sample of the same workload (one batch row per thread),

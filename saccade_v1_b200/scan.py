@@ -57,6 +57,20 @@ def _stream_handle(stream) -> int:
     return stream.cuda_stream
 
 
+def _stream_scratch(nbytes: int, device, stream):
+    """A uint8 device buffer from torch's caching allocator for use on `stream`:
+    allocated while that stream is current (so the allocator does not hand it
+    to another stream's work while the call's kernels may still run), or, for
+    a raw stream handle, marked as used by it."""
+    if isinstance(stream, torch.cuda.Stream):
+        with torch.cuda.stream(stream):
+            return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    if isinstance(stream, int) and stream not in (0,):
+        buf.record_stream(torch.cuda.ExternalStream(stream, device=device))
+    return buf
+
+
 def load_kernels() -> str:
     """Loads every kernel in the current CUDA context; returns the resource report."""
     L = _lib.load()
@@ -272,7 +286,7 @@ def mamba_block_forward(x, params, *, eps=1e-5, residual=True, out=None, workspa
     args = _block_args(x, params, eps, residual, out)
     need = mamba_block_workspace(x, params, eps, residual)
     if workspace is None:
-        workspace = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+        workspace = _stream_scratch(need + 256, x.device, stream)
     base = workspace.data_ptr()
     off = (-base) % 256
     _check(_lib.load().sacc_mamba_block_forward(ctypes.byref(args), base + off, workspace.numel() - off,
@@ -314,7 +328,7 @@ def cross_scan_block_forward(x, params, *, eps=1e-5, residual=True, dtype=torch.
     args = _cross_args(x, params, eps, residual, out, dtype)
     need = cross_scan_block_workspace(x, params, eps, residual, dtype)
     if workspace is None:
-        workspace = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+        workspace = _stream_scratch(need + 256, x.device, stream)
     base = workspace.data_ptr()
     off = (-base) % 256
     _check(_lib.load().sacc_cross_scan_block_forward(ctypes.byref(args), base + off, workspace.numel() - off,

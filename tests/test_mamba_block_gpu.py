@@ -125,3 +125,20 @@ def test_block_lengths_not_multiple_of_8(L):
     x = mo.rnd(np.random.default_rng(18).standard_normal((B, L, dm)) * 0.1, "bf16")
     check(f"block_L{L}", run_block(x, p, "bf16"), mo.block_forward(x, p, "bf16"))
     assert sb.scan_fault() == 0
+
+
+def test_block_on_a_stream_that_is_not_current():
+    """The wrapper's own workspace is taken for the launch stream, so a call on
+    a stream other than the current one gives the same bits."""
+    B, L, dm, D, N, R = 4, 32, 128, 256, 16, 8
+    p = mo.random_block(13, dm, D, N, R, 4, "bf16", norm=False)
+    x_np = mo.rnd(np.random.default_rng(6).standard_normal((B, L, dm)) * 0.1, "bf16")
+    want = run_block(x_np, p, "bf16")
+    s = torch.cuda.Stream()
+    x = torch.from_numpy(np.ascontiguousarray(x_np, np.float32)).to(device="cuda", dtype=torch.bfloat16)
+    dev = to_dev(p, "bf16")
+    torch.cuda.synchronize()
+    out = torch.empty_like(x)
+    y = sb.mamba_block_forward(x, dev, out=out, stream=s)  # the current stream stays the default one
+    s.synchronize()
+    assert np.array_equal(y.float().cpu().numpy(), want)

@@ -75,12 +75,23 @@ def _need(name, t, dtype=None, numel=None, optional=False):
         raise ScanInvalidArgument(f"{name} holds {t.numel() * t.element_size()} bytes, needs {numel}")
 
 
-def new_control(device="cuda") -> torch.Tensor:
-    return torch.zeros(CONTROL_BYTES, dtype=torch.uint8, device=device)
+def _zeros(nbytes: int, device, stream) -> torch.Tensor:
+    if isinstance(stream, torch.cuda.Stream):
+        with torch.cuda.stream(stream):
+            return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
 
-def new_records(capacity: int, device="cuda") -> torch.Tensor:
-    return torch.zeros(max(capacity, 1) * RECORD_BYTES, dtype=torch.uint8, device=device)
+def new_control(device="cuda", stream=None) -> torch.Tensor:
+    """A zeroed frame control block.  The zero fill runs on `stream` (default:
+    the current stream): pass the stream the frame calls will use, or order
+    the two streams, so that the fill lands before scan_frame_initialize."""
+    return _zeros(CONTROL_BYTES, device, stream)
+
+
+def new_records(capacity: int, device="cuda", stream=None) -> torch.Tensor:
+    """`capacity` zeroed frame records; the zero fill runs on `stream` as in new_control."""
+    return _zeros(max(capacity, 1) * RECORD_BYTES, device, stream)
 
 
 def _need_payload(control, payload, results, result_frames, records, capacity):

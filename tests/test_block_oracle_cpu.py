@@ -56,3 +56,31 @@ def test_block_oracle_matches_loop_restatement():
                 y[bb, t, d] = acc * z[bb, t, d] / (1 + np.exp(-z[bb, t, d]))
     want = np.einsum("bld,nd->bln", mo.rnd(y, dt), f["w_out"]) + x
     np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-12)
+
+
+def test_cross_level_oracle_on_a_single_position():
+    """On a 1 x 1 map the four Cross-Scan directions are the same one token, so
+    the level oracle (expand -> block -> + tokens -> merge) must equal the block
+    on that token plus x there."""
+    p = mo.random_block(91, 128, 256, 16, 16, 4, "bf16", norm=False, c_width=1)
+    x = (np.random.default_rng(92).standard_normal((2, 128, 1, 1)) * 0.5).astype(np.float32)
+    got = mo.cross_block_forward(x, p, "bf16")
+    tok = x.reshape(2, 1, 128).astype(np.float64)
+    want = (mo.block_forward(mo.rnd(tok, "bf16"), p, "bf16", residual=False) + tok).reshape(2, 128, 1, 1)
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_cross_level_oracle_direction_symmetry():
+    """On a 1 x W map directions 0 and 3 (identity, flip H) see the row in map
+    order and directions 1 and 2 (flip H and W, flip W) the reversed row: the
+    level is the merge of the block over the row and over the reversed row,
+    read back in map order."""
+    p = mo.random_block(93, 128, 256, 16, 16, 4, "bf16", norm=False, c_width=1)
+    W = 6
+    x = (np.random.default_rng(94).standard_normal((1, 128, 1, W)) * 0.5).astype(np.float32)
+    got = mo.cross_block_forward(x, p, "bf16")
+    tok = np.transpose(x[0, :, 0, :]).astype(np.float64)[None]                # (1, W, 128) in map order
+    fwd = mo.block_forward(mo.rnd(tok, "bf16"), p, "bf16", residual=False) + tok
+    rev = mo.block_forward(mo.rnd(tok[:, ::-1].copy(), "bf16"), p, "bf16", residual=False) + tok[:, ::-1]
+    want = (((fwd[0] + rev[0, ::-1]) + rev[0, ::-1]) + fwd[0]) * 0.25       # merge order: k = 0, 1, 2, 3
+    np.testing.assert_allclose(got[0, :, 0, :], np.transpose(want), rtol=1e-12, atol=1e-12)

@@ -284,8 +284,10 @@ int sacc_mamba_block_forward(const SaccMambaBlockArgs* args, void* workspace, si
  * Blocks whose sacc_mamba_block_workspace exceeds that size are rejected with
  * SACC_EINVAL.  The first call on a device looks up the array's address:
  * make it before any stream capture.  All calls on a device share the array
- * (it keeps the last call's contents; nothing needs to start at zero), so
- * calls that overlap on the GPU race: order them on one stream.
+ * and it keeps the last call's contents: every intermediate is written before
+ * it is read, and the scan's hand-off flags in it are cleared on the stream
+ * before each use.  Calls that overlap on the GPU race on the array: order
+ * them on one stream.
  * ------------------------------------------------------------------------ */
 #define SACC_NOALLOC_SCRATCH_BYTES ((size_t)24 << 20)
 int sacc_mamba_block_forward_noalloc(const SaccMambaBlockArgs* args, cudaStream_t stream);

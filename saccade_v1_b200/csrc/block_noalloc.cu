@@ -20,10 +20,11 @@
 // stale, so do not use this entry point across a device reset.
 //
 // Sharing: every call on a device uses the same array, and the array keeps
-// the last call's contents.  Nothing in it needs to start at zero: each
-// intermediate is written in full before it is read, and the chunk-parallel
-// scan's hand-off flags in it are compared against a value that is new to
-// each launch, so flags left by an earlier call never match.  Two calls whose work
+// the last call's contents.  Each intermediate is written in full before it
+// is read; the one region that must start at zero, the chunk-parallel scan's
+// hand-off flags, is cleared on the stream (cudaMemsetAsync, which allocates
+// nothing) right before the scan launch that uses it, so flags left by an
+// earlier call or graph replay never match.  Two calls whose work
 // overlaps on the GPU (different streams without an event between them, or
 // different host threads) race on the array; order them on one stream.
 #include <cuda_runtime.h>

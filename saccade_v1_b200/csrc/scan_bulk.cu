@@ -34,6 +34,7 @@
 #include <random>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "internal.h"
 #include "scan_common.cuh"
@@ -325,6 +326,73 @@ __device__ __forceinline__ void scan_block8(const float (*bc)[2 * kN], int q, in
             }
         }
         float y = fmaf(dskip, blk.u[j], (acc[0] + acc[1]) + (acc[2] + acc[3]));
+        if constexpr (kHasZ) y *= silu(blk.z[j]);
+        out[j] = y;
+    }
+}
+
+// True when this lane's A row is S4D-real in exact FP32 arithmetic:
+// A[n] == (n + 1) * A[0] for every n (the S4D-real initialisation
+// A[d, n] = -(n + 1) and any per-lane scale of it).  Then
+// exp(Delta A[n]) = q^(n + 1) with q = exp(Delta A[0]) exactly in real
+// arithmetic, and the decays need one exponential per token instead of 16.
+__device__ __forceinline__ bool s4d_row(const float* arow) {
+    float v[kN];
+    load16(arow, v);
+    bool ok = true;
+#pragma unroll
+    for (int n = 1; n < kN; ++n) ok = ok && v[n] == static_cast<float>(n + 1) * v[0];
+    return ok;
+}
+
+// scan_block8 for S4D-real rows: q = 2^(Delta a0) from the special-function
+// unit once per token, the 16 decays q^1..q^16 by a product tree of packed
+// FP32 multiplies (q2 = q q; (q3, q4) = q2 (q1, q2); (q5..q8) = q4 (q1..q4);
+// (q9..q16) = q8 (q1..q8): depth 4, each power within a few ulp plus 16 times
+// q's own error), and the state and output updates as packed pairs
+// (fma.rn.f32x2 / mul.rn.f32x2: half the issue slots of scalar FP32).
+// Per token: 2 special-function ops (softplus and q) instead of 17.
+template <bool kFullC, bool kHasZ, bool kGuard, bool kSum>
+__device__ __forceinline__ void scan_block8_pow(const float (*bc)[2 * kN], int q, int count, const Block8& blk, float a0,
+                                                float (&h)[kN], float bias, float dskip, int softplus, float (&out)[8],
+                                                float& dtsum) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        out[j] = 0.0f;
+        if (kGuard && j >= count) continue;
+        const int t = q * 8 + j;
+        const float xv = blk.x[j] + bias;
+        const float dt = softplus ? softplus_poly(xv) : xv;
+        if constexpr (kSum) dtsum += dt;
+        const float du = dt * blk.u[j];
+        const float q1 = fast_exp2(dt * a0);
+        float2 pw[kN / 2];
+        pw[0] = make_float2(q1, q1 * q1);
+        pw[1] = __fmul2_rn(make_float2(pw[0].y, pw[0].y), pw[0]);
+        const float2 q4 = make_float2(pw[1].y, pw[1].y);
+        pw[2] = __fmul2_rn(q4, pw[0]);
+        pw[3] = __fmul2_rn(q4, pw[1]);
+        const float2 q8 = make_float2(pw[3].y, pw[3].y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pw[4 + k] = __fmul2_rn(q8, pw[k]);
+        const float2 du2 = make_float2(du, du);
+        const float4* bcv = reinterpret_cast<const float4*>(bc[t]);
+        const float cr = kFullC ? 0.0f : bc[t][kN];
+        float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 bq = bcv[k4];
+            float4 cq = make_float4(cr, cr, cr, cr);
+            if constexpr (kFullC) cq = bcv[4 + k4];
+            const int n = 4 * k4;
+            float2 h0 = make_float2(h[n], h[n + 1]), h1 = make_float2(h[n + 2], h[n + 3]);
+            h0 = __ffma2_rn(pw[2 * k4], h0, __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+            h1 = __ffma2_rn(pw[2 * k4 + 1], h1, __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+            acc0 = __ffma2_rn(make_float2(cq.x, cq.y), h0, acc0);
+            acc1 = __ffma2_rn(make_float2(cq.z, cq.w), h1, acc1);
+            h[n] = h0.x; h[n + 1] = h0.y; h[n + 2] = h1.x; h[n + 3] = h1.y;
+        }
+        float y = fmaf(dskip, blk.u[j], (acc0.x + acc1.x) + (acc0.y + acc1.y));
         if constexpr (kHasZ) y *= silu(blk.z[j]);
         out[j] = y;
     }
@@ -644,87 +712,101 @@ __global__ void __launch_bounds__(kLanes, kMinBlocks) bulk_kernel(const __grid_c
             stash_load<T, kBDL>(p, w, d, h);
         }
 
-        for (int chunk = w.c0; chunk < w.c1; ++chunk, ++gc) {
-            const int s = gc % kStages;
-            const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((gc / kStages) & 1));
-            if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
-            if (!__syncthreads_and(ok)) {
-                fault = true;
-                break;
-            }
-            // B / C tiles to an FP32 token-major table.
-            if (kBDL) {
-                // raw [state][token]: a thread takes 8 tokens of one state (16 bytes).
-                for (int i = tid; i < (kN + cw) * (kT / 8); i += kLanes) {
-                    const int rowi = i / (kT / 8), t0 = (i % (kT / 8)) * 8;
-                    const T* src = rowi < kN ? sm.braw[s] + rowi * kT + t0 : sm.craw[s] + (rowi - kN) * kT + t0;
-                    const uint4 v = *reinterpret_cast<const uint4*>(src);
-                    const std::uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 f = unpack2<T>(wv[j]);
-                        sm.bc[t0 + 2 * j][rowi] = f.x;
-                        sm.bc[t0 + 2 * j + 1][rowi] = f.y;
+        // S4D-real A rows take the power-form decays; the choice is uniform
+        // over the CTA, so the barriers inside the chunk loop stay uniform, and
+        // every other A runs the exp-per-state loop unchanged.
+        const bool pw = __syncthreads_and(s4d_row(p.a + (p.a_shared ? 0 : d * kN)));
+        const float a0 = a[0];
+        auto run_chunks = [&](auto pow_tag) {
+            constexpr bool kPow = decltype(pow_tag)::value;
+            for (int chunk = w.c0; chunk < w.c1; ++chunk, ++gc) {
+                const int s = gc % kStages;
+                const bool ok = mbar_wait_bounded(&sm.full[s], static_cast<std::uint32_t>((gc / kStages) & 1));
+                if (tid == 0) bulk_wait_read<0>(); // the y tile is no longer read by the previous chunk's store
+                if (!__syncthreads_and(ok)) {
+                    fault = true;
+                    break;
+                }
+                // B / C tiles to an FP32 token-major table.
+                if (kBDL) {
+                    // raw [state][token]: a thread takes 8 tokens of one state (16 bytes).
+                    for (int i = tid; i < (kN + cw) * (kT / 8); i += kLanes) {
+                        const int rowi = i / (kT / 8), t0 = (i % (kT / 8)) * 8;
+                        const T* src = rowi < kN ? sm.braw[s] + rowi * kT + t0 : sm.craw[s] + (rowi - kN) * kT + t0;
+                        const uint4 v = *reinterpret_cast<const uint4*>(src);
+                        const std::uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    #pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 f = unpack2<T>(wv[j]);
+                            sm.bc[t0 + 2 * j][rowi] = f.x;
+                            sm.bc[t0 + 2 * j + 1][rowi] = f.y;
+                        }
+                    }
+                } else {
+                    // raw [token][state]: already token-major.
+                    for (int i = tid; i < kN * kT; i += kLanes) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
+                    for (int i = tid; i < cw * kT; i += kLanes) sm.bc[i / cw][kN + i % cw] = to_f32(sm.craw[s][i]);
+                }
+                __syncthreads();
+
+                // Tokens past the end of the sequence (zero-filled by the TMA, or the
+                // next packed sequence) are not run through the recurrence.
+                const unsigned long long left = w.len - static_cast<unsigned long long>(chunk) * kT;
+                const int valid = static_cast<int>(left < kT ? left : kT);
+                const int blocks8 = (valid + 7) / 8;
+    #pragma unroll 1
+                for (int q = 0; q < blocks8; ++q) {
+                    Block8 blk;
+                    if constexpr (kBDL)
+                        load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                    else
+                    {
+                        load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], static_cast<const T*>(p.zg),
+                                                 static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
+                                                     static_cast<unsigned long long>(chunk) * kT,
+                                                 p.zld, d, tid, q, valid - q * 8, blk);
+                        if constexpr (kR > 0) delta_from_dt<T, kR>(sm.dl[s], wrow, q, blk);
+                    }
+                    float out[8];
+                    if constexpr (kPow)
+                        scan_block8_pow<kFullC, kHasZ, true, kMode != 1>(sm.bc, q, valid - q * 8, blk, a0, h, bias, dskip, p.softplus,
+                                                                        out, dtsum);
+                    else
+                        scan_block8<kFullC, kHasZ, true, kMode != 1>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out,
+                                                                    dtsum);
+                    if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
+                    else store_block_bld<T>(sm.y, tid, q, out);
+                }
+                fence_async_shared();
+                __syncthreads();
+                const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
+                // Local-pass outputs (parts after the first) are not final.
+                const bool write_y = !((p.phase == 1 || (kMode == 2 && w.pass == 0)) && w.part > 0);
+                const bool tail = !kBDL && p.cu && valid < kT;
+                if (tail && write_y) {
+                    // A packed sequence's partial last chunk: a tile store would also
+                    // write the next sequence's rows, so store the valid rows only.
+                    T* yg = static_cast<T*>(p.y);
+                    for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
+                }
+                if (tid == 0) {
+                    if (!tail && write_y) {
+                        if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, w.row0);
+                        else tma_store_3d(&tm_y, sm.y, w.row0, tc0, w.bb);
+                    }
+                    bulk_commit();
+                    Cursor& c = sm.next;
+                    if (c.more) {
+                        // Stage s is free again: the chunk kStages ahead in this CTA's list.
+                        issue_chunk<T, kBDL, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
+                                                        c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
+                        cursor_next<kBDL, kFullC>(c, p);
                     }
                 }
-            } else {
-                // raw [token][state]: already token-major.
-                for (int i = tid; i < kN * kT; i += kLanes) sm.bc[i / kN][i % kN] = to_f32(sm.braw[s][i]);
-                for (int i = tid; i < cw * kT; i += kLanes) sm.bc[i / cw][kN + i % cw] = to_f32(sm.craw[s][i]);
             }
-            __syncthreads();
-
-            // Tokens past the end of the sequence (zero-filled by the TMA, or the
-            // next packed sequence) are not run through the recurrence.
-            const unsigned long long left = w.len - static_cast<unsigned long long>(chunk) * kT;
-            const int valid = static_cast<int>(left < kT ? left : kT);
-            const int blocks8 = (valid + 7) / 8;
-#pragma unroll 1
-            for (int q = 0; q < blocks8; ++q) {
-                Block8 blk;
-                if constexpr (kBDL)
-                    load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
-                else
-                {
-                    load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], static_cast<const T*>(p.zg),
-                                             static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
-                                                 static_cast<unsigned long long>(chunk) * kT,
-                                             p.zld, d, tid, q, valid - q * 8, blk);
-                    if constexpr (kR > 0) delta_from_dt<T, kR>(sm.dl[s], wrow, q, blk);
-                }
-                float out[8];
-                scan_block8<kFullC, kHasZ, true, kMode != 1>(sm.bc, q, valid - q * 8, blk, a, h, bias, dskip, p.softplus, out,
-                                                            dtsum);
-                if (kBDL) store_block_bdl<T>(sm.y, tid, q, out);
-                else store_block_bld<T>(sm.y, tid, q, out);
-            }
-            fence_async_shared();
-            __syncthreads();
-            const int tc0 = static_cast<int>(w.tok0) + chunk * kT;
-            // Local-pass outputs (parts after the first) are not final.
-            const bool write_y = !((p.phase == 1 || (kMode == 2 && w.pass == 0)) && w.part > 0);
-            const bool tail = !kBDL && p.cu && valid < kT;
-            if (tail && write_y) {
-                // A packed sequence's partial last chunk: a tile store would also
-                // write the next sequence's rows, so store the valid rows only.
-                T* yg = static_cast<T*>(p.y);
-                for (int t = 0; t < valid; ++t) yg[(static_cast<unsigned long long>(tc0) + t) * D + d] = sm.y[t * kLanes + tid];
-            }
-            if (tid == 0) {
-                if (!tail && write_y) {
-                    if (kBDL) tma_store_2d(&tm_y, sm.y, tc0, w.row0);
-                    else tma_store_3d(&tm_y, sm.y, w.row0, tc0, w.bb);
-                }
-                bulk_commit();
-                Cursor& c = sm.next;
-                if (c.more) {
-                    // Stage s is free again: the chunk kStages ahead in this CTA's list.
-                    issue_chunk<T, kBDL, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
-                                                    c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
-                    cursor_next<kBDL, kFullC>(c, p);
-                }
-            }
-        }
+        };
+        if (pw) run_chunks(std::true_type{});
+        else run_chunks(std::false_type{});
         if (fault) break;
         if (kMode == 2) {
             if (w.pass == 0) {
@@ -1142,6 +1224,7 @@ struct Pick {
     const void* fn;
     size_t smem;
     cudaError_t (*prepare)();
+    int threads = kLanes; // threads per CTA the variant launches with
 };
 
 template <typename T, bool kBDL, bool kHasZ, bool kFullC>
@@ -1207,10 +1290,10 @@ template <typename T, bool kHasZ, int kR>
 Pick make_pick_quad(int mode) {
     if (mode == 2) {
         using V = QuadVariant<T, kHasZ, 2, kR>;
-        return {V::fn(), V::smem(), &V::prepare};
+        return {V::fn(), V::smem(), &V::prepare, kLanes * kQ};
     }
     using V = QuadVariant<T, kHasZ, 0, kR>;
-    return {V::fn(), V::smem(), &V::prepare};
+    return {V::fn(), V::smem(), &V::prepare, kLanes * kQ};
 }
 
 template <typename T>
@@ -1238,7 +1321,7 @@ Pick pick_for(const SaccScanExArgs& a, const DtFusion* dtf, int mode) {
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
 // CTAs of a variant resident at once on the current device (SMs x CTAs per
-// SM), queried once per (variant, device).
+// SM at the variant's own block size), queried once per (variant, device).
 unsigned long long resident_ctas(const Pick& k) {
     struct Entry {
         const void* fn;
@@ -1257,7 +1340,7 @@ unsigned long long resident_ctas(const Pick& k) {
     }
     int sms = 148, per_sm = 1;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kLanes, k.smem) != cudaSuccess || per_sm < 1) per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, k.threads, k.smem) != cudaSuccess || per_sm < 1) per_sm = 1;
     const unsigned long long ctas = static_cast<unsigned long long>(sms) * static_cast<unsigned long long>(per_sm);
     std::lock_guard<std::mutex> lock(mu);
     if (used < 64) cache[used++] = Entry{k.fn, dev, ctas};
@@ -1465,9 +1548,17 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
             p.passes = 2;
             p.scratch = static_cast<float*>(scratch);
             p.epoch = next_epoch();
+            // The flags stay in the scratch after the launch (nothing in it
+            // overwrites them), and a CUDA graph replays this launch with the
+            // same epoch: clear them on the stream first, so that a part never
+            // sees a flag that an earlier launch or replay left (the epoch is
+            // never zero).
+            const std::size_t records = static_cast<std::size_t>(p.units) * fused * (kN + 1) * kLanes;
+            cudaError_t me = cudaMemsetAsync(p.scratch + records, 0, static_cast<std::size_t>(p.units) * fused * 8, stream);
+            if (me != cudaSuccess) return me;
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(static_cast<unsigned>(p.units * fused));
-            cfg.blockDim = dim3(quad_eligible(a) ? kLanes * kQ : kLanes);
+            cfg.blockDim = dim3(static_cast<unsigned>(fk.threads));
             cfg.dynamicSmemBytes = fk.smem;
             cfg.stream = stream;
             cudaLaunchAttribute attrs[2]{};

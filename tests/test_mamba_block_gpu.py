@@ -142,3 +142,37 @@ def test_block_on_a_stream_that_is_not_current():
     y = sb.mamba_block_forward(x, dev, out=out, stream=s)  # the current stream stays the default one
     s.synchronize()
     assert np.array_equal(y.float().cpu().numpy(), want)
+
+
+def test_fused_scan_graph_replay_new_inputs():
+    """The reference head's block at the HR L = 960 level scans 8 units of 960 tokens, which takes the fused
+    chunk-parallel launch (one cooperative launch whose parts hand their records over through flags in the
+    workspace).  A CUDA graph captured once and replayed with new inputs in the same buffers must give the
+    same bits as eager calls on those inputs: every replay reuses the captured launch's flag value, so the
+    flags of the previous replay must not be taken for this one's."""
+    B, L, dm, D, N, R = 4, 960, 128, 256, 16, 16
+    p = mo.random_block(19, dm, D, N, R, 4, "f16", norm=False, c_width=1)
+    dev = to_dev(p, "f16")
+    rng = np.random.default_rng(20)
+    xs = [torch.from_numpy(mo.rnd(rng.standard_normal((B, L, dm)) * 0.5, "f16").astype(np.float32)).to("cuda", torch.float16)
+          for _ in range(3)]
+    s = torch.cuda.Stream()
+    x_static = xs[0].clone()
+    out_static = torch.empty_like(x_static)
+    ws = torch.empty(sb.mamba_block_workspace(x_static, dev) + 256, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        refs = [sb.mamba_block_forward(x, dev, stream=s) for x in xs]
+        sb.mamba_block_forward(x_static, dev, out=out_static, workspace=ws, stream=s)  # warm-up before capture
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        sb.mamba_block_forward(x_static, dev, out=out_static, workspace=ws, stream=s)
+    for i in (1, 2, 0, 2):
+        x_static.copy_(xs[i])
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_static, refs[i]), f"replay with input {i} differs from the eager call"
+    # The replayed output is also the block's result: direction 0 against the binary64 block oracle.
+    check("hr_l960_graph", out_static.float().cpu().numpy()[:1], mo.block_forward(xs[2].float().cpu().numpy()[:1], p, "f16"))
+    assert sb.scan_fault() == 0

@@ -82,3 +82,39 @@ def test_noalloc_rejects_blocks_beyond_the_static_scratch():
         sb.mamba_block_forward_noalloc(x, p, out=y, stream=s)
     s.synchronize()
     assert bool((y == 7.0).all())
+
+
+def test_noalloc_fused_scan_path_two_inputs_and_graph_replay():
+    """The reference head's block at its HR L = 960 level (4 directions x 960 tokens, d_inner 256, dt_rank 16,
+    one C per token, fp16): few units over long sequences, so the scan runs as the fused chunk-parallel
+    launch whose part records and hand-off flags live in the static scratch.  Two calls with different
+    inputs, then a CUDA graph of the no-alloc call replayed with a third input, each against
+    sacc_mamba_block_forward on the same input."""
+    B, L, dm, D, N, R = 4, 960, 128, 256, 16, 16
+    p = weights(23, dm, D, N, R, torch.float16)
+    p.pop("norm_w")
+    p["w_x"] = p["w_x"][: R + N + 1].contiguous()  # x_proj 256 -> 16 + 16 + 1: one C per token
+    s = torch.cuda.Stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(41)
+    with torch.cuda.stream(s):
+        xs = [(torch.randn(B, L, dm, device="cuda", generator=g) * 0.5).to(torch.float16) for _ in range(3)]
+        assert sb.mamba_block_workspace(xs[0], p) <= SCRATCH_MAX
+        ref = [sb.mamba_block_forward(x, p, stream=s) for x in xs]
+        got = [torch.empty_like(x) for x in xs[:2]]
+        for x, y in zip(xs[:2], got):
+            noalloc_call(x, p, y, s)
+    s.synchronize()
+    for a, b in zip(got, ref[:2]):
+        assert bool(torch.isfinite(a.float()).all())
+        close(a, b)
+    x_static, y_static = xs[0].clone(), torch.empty_like(xs[0])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        noalloc_call(x_static, p, y_static, s)
+    for i in (2, 1):
+        x_static.copy_(xs[i])
+        graph.replay()
+        torch.cuda.synchronize()
+        close(y_static, ref[i])
+    assert sb.scan_fault() == 0

@@ -66,6 +66,10 @@ def lib():
         L.sacc_oracle_scan_bound.argtypes = [ctypes.POINTER(_Shape)] + [_f32p] * 6 + [_f64p]
         L.sacc_oracle_scan_ex.restype = None
         L.sacc_oracle_scan_ex.argtypes = [ctypes.POINTER(_ExShape)] + [_f32p] * 9 + [_i32p, _f64p, _f64p, _f64p]
+        L.sacc_oracle_silu.argtypes = [_f64p, ctypes.c_size_t, _f64p]
+        L.sacc_oracle_neg_exp.argtypes = [_f32p, ctypes.c_size_t, _f64p]
+        L.sacc_oracle_scan_ex_f64.argtypes = [ctypes.POINTER(_ExShape)] + [_f64p] * 5 + [_f32p, _f64p] + [_f32p] * 2 + [
+            _i32p, _f64p, _f64p, _f64p]
         L.sacc_oracle_cross_scan_source.restype = ctypes.c_size_t
         L.sacc_oracle_cross_scan_source.argtypes = [ctypes.c_size_t] * 4
         L.sacc_oracle_cross_scan_expand.restype = None
@@ -288,7 +292,7 @@ def scan_bound(k: Case) -> np.ndarray:
 
 def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bias=None, softplus: bool = True,
             h0=None, want_final: bool = False, cu_seqlens=None, groups: int = 1, c_width: int | None = None,
-            want_scale: bool = False):
+            want_scale: bool = False, exact: bool = False):
     """Extended scan in binary64 (see scan_oracle.c sacc_oracle_scan_ex).
 
     Shapes, layout "BLD": u/delta/z (B, L, D); b (B, L, G, N); c (B, L, G, CW).
@@ -296,9 +300,11 @@ def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bia
     a (D or 1, N); d, delta_bias (D,); h0 (nseq, D, N).
     Returns (y float64 with u's shape, h_final float64 (nseq, D, N) or None),
     plus the per-element term magnitude sum_n |C h| + |D u| (times |silu(z)|)
-    when want_scale.
+    when want_scale.  exact: u, delta, a, b, c and z are taken as binary64
+    values (sacc_oracle_scan_ex_f64) instead of being rounded to FP32 first.
     """
-    u = np.ascontiguousarray(u, np.float32)
+    act = np.float64 if exact else np.float32
+    u = np.ascontiguousarray(u, act)
     if layout == "BLD":
         B, L, D = u.shape
         N = b.shape[-1]
@@ -307,7 +313,7 @@ def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bia
         B, D, L = u.shape
         N = b.shape[-2]
         CW = c.shape[-2] if c_width is None else c_width
-    a = np.ascontiguousarray(a, np.float32).reshape(-1, N)
+    a = np.ascontiguousarray(a, act).reshape(-1, N)
     nseq = (len(cu_seqlens) - 1) if cu_seqlens is not None else B
     sh = _ExShape(B, L, D, N, groups, CW, a.shape[0], 0 if layout == "BLD" else 1, int(d is not None),
                   int(z is not None), int(delta_bias is not None), int(softplus), int(h0 is not None),
@@ -317,12 +323,36 @@ def scan_ex(u, delta, a, b, c, *, layout: str = "BLD", d=None, z=None, delta_bia
     hf = np.zeros((nseq, D, N), np.float64) if want_final else None
     conv = lambda t: None if t is None else np.ascontiguousarray(t, np.float32)
     cu = None if cu_seqlens is None else np.ascontiguousarray(cu_seqlens, np.int32)
-    tensors = [u, conv(delta), a, conv(b), conv(c), conv(d), conv(z), conv(delta_bias), conv(h0)]
-    lib().sacc_oracle_scan_ex(ctypes.byref(sh), *[_fp(t) for t in tensors],
+    if exact:
+        convd = lambda t: None if t is None else np.ascontiguousarray(t, np.float64)
+        fn = lib().sacc_oracle_scan_ex_f64
+        ptrs = [_dp(u), _dp(convd(delta)), _dp(a), _dp(convd(b)), _dp(convd(c)), _fp(conv(d)), _dp(convd(z)),
+                _fp(conv(delta_bias)), _fp(conv(h0))]
+    else:
+        fn = lib().sacc_oracle_scan_ex
+        tensors = [u, conv(delta), a, conv(b), conv(c), conv(d), conv(z), conv(delta_bias), conv(h0)]
+        ptrs = [_fp(t) for t in tensors]
+    fn(ctypes.byref(sh), *ptrs,
                               ctypes.cast(None, _i32p) if cu is None else cu.ctypes.data_as(_i32p),
                               _dp(y), _dp(hf) if hf is not None else ctypes.cast(None, _f64p),
                               _dp(sc) if sc is not None else ctypes.cast(None, _f64p))
     return (y, hf, sc) if want_scale else (y, hf)
+
+
+def silu(x) -> np.ndarray:
+    """x sigmoid(x) in binary64, the reference head's form (src/head_reference.cpp:54-58, :221-232)."""
+    x = np.ascontiguousarray(x, np.float64)
+    y = np.empty_like(x)
+    lib().sacc_oracle_silu(_dp(x), x.size, _dp(y))
+    return y
+
+
+def neg_exp(a_log) -> np.ndarray:
+    """A = -exp(A_log) in binary64 from FP32 A_log (src/head_reference.cpp:347-354)."""
+    a_log = np.ascontiguousarray(a_log, np.float32)
+    a = np.empty(a_log.shape, np.float64)
+    lib().sacc_oracle_neg_exp(_fp(a_log), a_log.size, _dp(a))
+    return a
 
 
 def cross_scan_source(direction: int, token: int, height: int, width: int) -> int:

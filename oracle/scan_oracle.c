@@ -219,8 +219,22 @@ typedef struct {
     int32_t layout, has_d, has_z, has_bias, apply_softplus, has_h0, want_final, nseq;
 } OracleExShape;
 
-void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* delta, const float* a, const float* b,
-                         const float* c, const float* d, const float* z, const float* bias, const float* h0,
+/* Element i of an FP32 (f64 == 0) or binary64 (f64 == 1) array, as binary64
+ * (FP32 values widen exactly). */
+static double rd(const void* p, size_t i, int f64) {
+    return f64 ? ((const double*)p)[i] : (double)((const float*)p)[i];
+}
+
+/* sigmoid(x) in the reference head's form (src/head_reference.cpp:54-58):
+ * 1 / (1 + e^-x) for x >= 0, e^x / (1 + e^x) below. */
+static double sigmoid(double x) {
+    if (x >= 0) return 1.0 / (1.0 + exp(-x));
+    const double e = exp(x);
+    return e / (1.0 + e);
+}
+
+static void scan_ex_core(const OracleExShape* s, int f64, const void* u, const void* delta, const void* a, const void* b,
+                         const void* c, const float* d, const void* z, const float* bias, const float* h0,
                          const int32_t* cu_seqlens, double* y, double* h_final, double* scale) {
     const size_t Bt = s->batch, L = s->length, D = s->channels, N = s->state, G = s->groups, CW = s->c_width;
     const size_t per_group = D / G;
@@ -230,7 +244,7 @@ void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* de
         const size_t bb = cu_seqlens ? 0 : seq;
         const size_t t0 = cu_seqlens ? (size_t)cu_seqlens[seq] : 0, t1 = cu_seqlens ? (size_t)cu_seqlens[seq + 1] : L;
         for (size_t ch = 0; ch < D; ++ch) {
-            const float* a_row = a + (s->a_rows == 1 ? 0 : ch * N);
+            const size_t a_row = s->a_rows == 1 ? 0 : ch * N;
             const size_t g = ch / per_group;
             for (size_t n = 0; n < N; ++n) h[n] = s->has_h0 ? (double)h0[(seq * D + ch) * N + n] : 0.0;
             for (size_t t = t0; t < t1; ++t) {
@@ -244,16 +258,16 @@ void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* de
                     bat0 = ((bb * G + g) * N) * L + t; bstride = L;
                     cat0 = ((bb * G + g) * CW) * L + t; cstride = L;
                 }
-                const double uu = u[at];
-                double raw = delta[at];
+                const double uu = rd(u, at, f64);
+                double raw = rd(delta, at, f64);
                 if (s->has_bias) raw += (double)bias[ch];
                 const double dt = s->apply_softplus ? sacc_oracle_softplus(raw) : raw;
                 double acc = 0.0, mag = 0.0;
                 for (size_t n = 0; n < N; ++n) {
-                    const double decay = exp(dt * a_row[n]);
-                    const double drive = dt * b[bat0 + n * bstride] * uu;
+                    const double decay = exp(dt * rd(a, a_row + n, f64));
+                    const double drive = dt * rd(b, bat0 + n * bstride, f64) * uu;
                     h[n] = decay * h[n] + drive;
-                    const double term = c[cat0 + (CW == 1 ? 0 : n) * cstride] * h[n];
+                    const double term = rd(c, cat0 + (CW == 1 ? 0 : n) * cstride, f64) * h[n];
                     acc += term;
                     mag += fabs(term);
                 }
@@ -262,7 +276,9 @@ void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* de
                     mag += fabs((double)d[ch] * uu);
                 }
                 if (s->has_z) {
-                    const double zz = z[at], gate = zz / (1.0 + exp(-zz));
+                    /* y * silu(z), silu(z) = z sigmoid(z) as the reference head's
+                     * multiply(y, silu(z)) (src/head_reference.cpp:221 silu, :490 the gate). */
+                    const double zz = rd(z, at, f64), gate = zz * sigmoid(zz);
                     acc *= gate;
                     mag *= fabs(gate);
                 }
@@ -275,6 +291,32 @@ void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* de
                 for (size_t n = 0; n < N; ++n) h_final[(seq * D + ch) * N + n] = h[n];
         }
     }
+}
+
+void sacc_oracle_scan_ex(const OracleExShape* s, const float* u, const float* delta, const float* a, const float* b,
+                         const float* c, const float* d, const float* z, const float* bias, const float* h0,
+                         const int32_t* cu_seqlens, double* y, double* h_final, double* scale) {
+    scan_ex_core(s, 0, u, delta, a, b, c, d, z, bias, h0, cu_seqlens, y, h_final, scale);
+}
+
+/* The same scan on binary64 u, delta, A, B, C and z (the activations of the
+ * binary64 block oracle, which are not FP32 values); D, the bias and h0 stay
+ * FP32 parameters. */
+void sacc_oracle_scan_ex_f64(const OracleExShape* s, const double* u, const double* delta, const double* a, const double* b,
+                             const double* c, const float* d, const double* z, const float* bias, const float* h0,
+                             const int32_t* cu_seqlens, double* y, double* h_final, double* scale) {
+    scan_ex_core(s, 1, u, delta, a, b, c, d, z, bias, h0, cu_seqlens, y, h_final, scale);
+}
+
+/* silu(x) = x sigmoid(x) elementwise in binary64 with the C library's exp
+ * (the reference head's silu value, src/head_reference.cpp:221-232). */
+void sacc_oracle_silu(const double* x, size_t n, double* y) {
+    for (size_t i = 0; i < n; ++i) y[i] = x[i] * sigmoid(x[i]);
+}
+
+/* A = -exp(A_log) in binary64 from FP32 A_log (src/head_reference.cpp:347-354). */
+void sacc_oracle_neg_exp(const float* a_log, size_t n, double* a) {
+    for (size_t i = 0; i < n; ++i) a[i] = -exp((double)a_log[i]);
 }
 
 /* src/selective_scan.cpp:175-180 (cross_scan_source).  Returns (size_t)-1 on a bad argument. */

@@ -3,10 +3,17 @@
 // include/saccade/selective_scan_cuda.hpp (the TensorRT plugin, the reference's
 // tests and benchmark) compiles unchanged against libsacc_scan.so:
 //
-//   saccade::selective_scan_cuda(shape, inputs, y, status, stream)   cuda/selective_scan.cu:359-400
-//   saccade::selective_scan_cuda_load_kernels()                       cuda/selective_scan.cu:341-357
-//   saccade::cross_scan_expand_cuda / cross_scan_merge_cuda           cuda/selective_scan.cu:402-434
-//   saccade::selective_scan_cuda_identity()                           cuda/selective_scan.cu:436-446
+//   saccade::selective_scan_cuda(shape, inputs, y, status, stream)   cuda/selective_scan.cu:270-311
+//   saccade::selective_scan_cuda_load_kernels()                       cuda/selective_scan.cu:252-268
+//   saccade::cross_scan_expand_cuda / cross_scan_merge_cuda           cuda/selective_scan.cu:313-345
+//   saccade::selective_scan_cuda_identity()                           cuda/selective_scan.cu:347-357
+//
+// include/saccade/selective_scan_cuda.hpp of this repository includes this
+// file, so a tree that builds against the reference's headers replaces that
+// one file and links libsacc_scan.so.  saccade::SelectiveScanShape comes from
+// the reference's own include/saccade/selective_scan.hpp whenever that header
+// is on the include path (it is the host reference's type too); only without
+// it is the same shape defined here.
 //
 // Error behaviour is the reference's: SACC_EINVAL becomes std::invalid_argument
 // (nothing was enqueued), SACC_ECUDA becomes std::runtime_error, each with the
@@ -20,8 +27,10 @@
 
 #include "sacc_scan.h"
 
+#if __has_include("saccade/selective_scan.hpp")
+#include "saccade/selective_scan.hpp"
+#else
 namespace saccade {
-
 // include/saccade/selective_scan.hpp:19-27
 struct SelectiveScanShape {
     std::size_t batch = 0;
@@ -32,6 +41,10 @@ struct SelectiveScanShape {
     std::size_t c_width = 1;
     bool has_d = true;
 };
+} // namespace saccade
+#endif
+
+namespace saccade {
 
 // include/saccade/selective_scan_cuda.hpp:21-55
 using ScanStatus = SaccScanStatus;

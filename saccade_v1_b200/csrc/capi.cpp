@@ -157,13 +157,14 @@ void reference_scan(const char* api, const SaccScanShape& s, const void* u, cons
                     {c, cn, SACC_SCAN_NONFINITE_C, h},
                     {d, dn, SACC_SCAN_NONFINITE_D, 0}},
                    6};
+    // memset, check, scan, finalize: the reference's four operations per call
+    // (cuda/selective_scan.cu:298-310); the scan overlaps the check.
+    CK(launch_check(list, status, sms, stream));
     if (s.length > 0) {
         ScanF32Launch p{u, delta, a, b, c, d, y, s.batch, s.length, s.channels,
                         s.batch * s.channels, static_cast<unsigned>(s.state), s.a_rows == 1, s.c_width != 1,
-                        s.has_d != 0, list, half};
+                        s.has_d != 0, half};
         CK(launch_scan_f32(p, status, sms, stream));
-    } else {
-        CK(launch_check(list, status, sms, stream));
     }
     CK(launch_finalize(y, ud, status, sms, stream, half));
 }

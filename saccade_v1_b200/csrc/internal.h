@@ -56,18 +56,20 @@ struct ScanF32Launch {
     unsigned long long batch, length, channels, lanes;
     unsigned state;
     bool a_shared, c_full, has_d;
-    CheckList check;
     bool half = false;
 };
 
-// Enqueues the fused input-check + scan kernel on `stream` (status already
-// cleared by the caller).  Returns a CUDA error (launch only).
+// Enqueues the scan kernel on `stream` right after the input check
+// (launch_check), with programmatic stream serialization: the check releases
+// it at once and it waits for the check grid before it completes (status
+// already cleared by the caller).  Returns a CUDA error (launch only).
 cudaError_t launch_scan_f32(const ScanF32Launch& p, SaccScanStatus* status, int sm_count, cudaStream_t stream);
 // Poisons `count` outputs (FP32, or FP16 when `half`) with quiet NaN when
 // flags != 0, then writes done.
 cudaError_t launch_finalize(void* out, unsigned long long count, SaccScanStatus* status, int sm_count, cudaStream_t stream,
                             bool half = false);
-// Input check only (Cross-Scan and L = 0 paths).
+// Exact NaN / Inf bits of the listed tensors (every reference-ABI and
+// Cross-Scan call runs it first).
 cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream);
 
 struct CrossLaunch {

@@ -15,8 +15,11 @@
 //    then folds its predecessors' carries into its true starting state and
 //    reruns its tokens with outputs (pass 2).  All chunks of a lane live in one
 //    CTA: no workspace, one kernel;
-//  * the input finiteness check runs in the same launch (extra CTAs after the
-//    scan CTAs), so one call is memset + 1 kernel + finalize.
+//  * one call is the reference's memset + check + scan + finalize (the
+//    graph a captured call holds), with the scan overlapping the check: the
+//    check kernel releases the scan at once (programmatic dependent launch),
+//    the scan waits for the check grid only at its end, and finalize waits for
+//    the scan, so it sees both grids' status bits.
 //
 // The same kernels serve FP16 activations (plugin SelectiveScan v3): u,
 // delta, B and C are widened to FP32 as they are loaded and y is rounded to
@@ -41,6 +44,7 @@
 #include <type_traits>
 
 #include "internal.h"
+#include "scan_common.cuh"
 
 namespace sacc {
 namespace {
@@ -115,7 +119,6 @@ struct Params {
     int a_shared, c_full, has_d, vec_b, vec_c;
     int chunks, lanes_per_cta;
     unsigned scan_blocks;
-    CheckList check;
 };
 
 // N values of a row; `vec`: the row starts 16-byte (FP32) or 8-byte (FP16)
@@ -298,12 +301,6 @@ __device__ void check_tensors(const CheckList& list, unsigned long long first, u
 
 template <typename T, int N, int CW>
 __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanStatus* status) {
-    if (blockIdx.x >= p.scan_blocks) {
-        const unsigned long long first = static_cast<unsigned long long>(blockIdx.x - p.scan_blocks) * kThreads + threadIdx.x;
-        const unsigned long long stride = static_cast<unsigned long long>(gridDim.x - p.scan_blocks) * kThreads;
-        check_tensors(p.check, first, stride, status);
-        return;
-    }
     extern __shared__ float2 carry[]; // [chunk][lane in CTA][state]: (decay product, local state)
     __shared__ int chunk_failed[kThreads];
     const int K = p.chunks, LPC = p.lanes_per_cta;
@@ -380,9 +377,17 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
     } else if (fail) {
         atomicOr(&status->flags, fail);
     }
+    // The check grid released this grid before it finished: one thread waits
+    // for it here, so this grid completes only after the check has (finalize
+    // waits for this grid and then reads both grids' status bits).
+    if (blockIdx.x == 0 && threadIdx.x == 0) pdl_wait();
 }
 
+// Exact NaN / Inf bits of the inputs.  Releases the next kernel of the stream
+// at once when that one is launched with programmatic stream serialization
+// (the scan, which does not read what the check writes).
 __global__ void __launch_bounds__(kThreads) check_kernel(CheckList list, SaccScanStatus* status) {
+    pdl_launch_dependents();
     check_tensors(list, static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x,
                   static_cast<unsigned long long>(gridDim.x) * kThreads, status);
 }
@@ -392,6 +397,7 @@ __global__ void __launch_bounds__(kThreads) check_kernel(CheckList list, SaccSca
 // cuda/selective_scan.cu:238-244).
 template <typename W, unsigned kPoison>
 __global__ void __launch_bounds__(kThreads) finalize_kernel(W* out, unsigned long long count, SaccScanStatus* status) {
+    pdl_wait(); // launched with programmatic stream serialization: the previous grid's status bits first
     const unsigned long long first = static_cast<unsigned long long>(blockIdx.x) * kThreads + threadIdx.x;
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * kThreads;
     if (status->flags)
@@ -467,7 +473,6 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     const std::uintptr_t vec_align = s.half ? 7u : 15u; // four values per load
     p.vec_b = (reinterpret_cast<std::uintptr_t>(s.b) & vec_align) == 0;
     p.vec_c = (reinterpret_cast<std::uintptr_t>(s.c) & vec_align) == 0;
-    p.check = s.check;
     // Chunks: as many (lane, chunk) threads as the SMs hold at once (one wave:
     // a chunk's work grows with L / K and its fold with K, and a second wave
     // doubles the time), at least 2 tokens per chunk, at most 64 chunks; one
@@ -485,7 +490,6 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     const unsigned long long blocks = (s.lanes + p.lanes_per_cta - 1) / p.lanes_per_cta;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidValue;
     p.scan_blocks = static_cast<unsigned>(blocks);
-    const unsigned extra = check_blocks(total_checked(s.check), sm_count);
     const size_t smem = K > 1 ? static_cast<size_t>(kThreads) * s.state * sizeof(float2) : 0;
     void* args[] = {&p, &status};
     const void* fn = pick_kernel(s.state, s.half, s.c_full);
@@ -495,7 +499,8 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    return cudaLaunchKernel(fn, dim3(p.scan_blocks + extra), dim3(kThreads), args, smem, stream);
+    // After the check kernel, which releases this launch at its start.
+    return launch_pdl(fn, dim3(p.scan_blocks), dim3(kThreads), smem, stream, args);
 }
 
 cudaError_t launch_check(const CheckList& list, SaccScanStatus* status, int sm_count, cudaStream_t stream) {
@@ -509,10 +514,10 @@ cudaError_t launch_finalize(void* out, unsigned long long count, SaccScanStatus*
     const unsigned long long cap = 4ull * static_cast<unsigned long long>(sm_count);
     const unsigned blocks = static_cast<unsigned>(want < 1 ? 1 : want > cap ? cap : want);
     if (half)
-        finalize_kernel<unsigned short, 0x7e00u><<<blocks, kThreads, 0, stream>>>(static_cast<unsigned short*>(out), count, status);
-    else
-        finalize_kernel<unsigned, 0x7fc00000u><<<blocks, kThreads, 0, stream>>>(static_cast<unsigned*>(out), count, status);
-    return cudaGetLastError();
+        return launch_pdl_k(finalize_kernel<unsigned short, 0x7e00u>, dim3(blocks), dim3(kThreads), 0, stream,
+                            static_cast<unsigned short*>(out), count, status);
+    return launch_pdl_k(finalize_kernel<unsigned, 0x7fc00000u>, dim3(blocks), dim3(kThreads), 0, stream,
+                        static_cast<unsigned*>(out), count, status);
 }
 
 cudaError_t load_scan_f32_kernels(std::string& report) {

@@ -432,8 +432,30 @@ def c3_step(torch, device, stream, peak):
                                           delta_bias=t["bias"], out=t["y"], stream=stream)
     us = time_device(torch, stream, step, 50)
     nbytes = 2 * t["state"].numel() * 4 + 4 * t["u"].numel() * 2 + 2 * t["bm"].numel() * 2 + 4 * (t["A"].numel() + 2 * 256)
+    # L2-cold: in deployment one step runs per frame between other work that evicts the 126 MB L2, while back
+    # to back the 64 MiB state partly stays there.  Each step is timed alone after writing a 256 MB buffer
+    # (outside its event pair), so its state is read from HBM.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    cold = []
+    for i in range(23):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        e1.synchronize()
+        if i >= 3:
+            cold.append(e0.elapsed_time(e1) * 1e3)
+    del flush
+    cold_us = statistics.median(cold)
     return {"us": round(us, 2), "tracks_frames_per_s": round(4096 / (us * 1e-6), 1),
             "GB_per_s": round(nbytes / (us * 1e-6) / 1e9, 1), "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4),
+            "l2_cold_us": round(cold_us, 2), "l2_cold_GB_per_s": round(nbytes / (cold_us * 1e-6) / 1e9, 1),
+            "l2_cold_hbm_frac": round(nbytes / (cold_us * 1e-6) / 1e9 / peak, 4),
+            "l2_cold_tracks_frames_per_s": round(4096 / (cold_us * 1e-6), 1),
+            "note": "us / hbm_frac: 50 steps back to back (the state partly L2-resident); l2_cold_*: median of 20 "
+                    "steps each timed alone after a 256 MB L2-evicting write",
             "bytes": nbytes, "workload": "4096 tracks, D=256, N=16, fp16 acts, fp32 carried state, gate+bias+D"}
 
 
@@ -959,6 +981,10 @@ def main():
         return
     if world > 1:
         import datetime
+        # NCCL's initialisation log (communicator size and rank per process) stays on, so a run's output shows
+        # that every rank joined one communicator of `world` ranks.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))

@@ -1,5 +1,5 @@
-"""ctypes binding of libsacc_scan.so (the C ABI declared in include/sacc_scan.h
-and include/sacc_frame.h).
+"""ctypes binding of libsacc_scan.so (the C ABI declared in include/sacc_scan.h,
+include/sacc_frame.h and include/sacc_shard.h).
 
 The library is built in-tree (saccade_v1_b200/libsacc_scan.so).  There is no
 fallback: if the library is missing or does not load, every entry point
@@ -52,6 +52,11 @@ EXPORTS = (
     "sacc_model_producer_workspace_bytes",
     "sacc_model_producer_load_kernels",
     "sacc_model_producer_cuda",
+    # include/sacc_shard.h
+    "sacc_shard_rows",
+    "sacc_shard_group_create",
+    "sacc_shard_group_destroy",
+    "sacc_scan_sharded_forward",
 )
 
 FRAME_MAX_STATUSES = 16
@@ -184,6 +189,14 @@ def load() -> ctypes.CDLL:
     L.sacc_cross_scan_block_workspace.restype = i
     L.sacc_cross_scan_block_forward.argtypes = [ctypes.POINTER(CrossScanBlockArgs), vp, sz, vp]
     L.sacc_cross_scan_block_forward.restype = i
+    L.sacc_shard_rows.argtypes = [ctypes.c_uint64, i, i, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
+    L.sacc_shard_rows.restype = i
+    L.sacc_shard_group_create.argtypes = [i, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(vp)]
+    L.sacc_shard_group_create.restype = i
+    L.sacc_shard_group_destroy.argtypes = [vp]
+    L.sacc_shard_group_destroy.restype = i
+    L.sacc_scan_sharded_forward.argtypes = [vp, ctypes.POINTER(ScanExArgs), ctypes.POINTER(vp), ctypes.POINTER(vp), sz]
+    L.sacc_scan_sharded_forward.restype = i
     i64, u64 = ctypes.c_int64, ctypes.c_uint64
     for name, args in (
             ("sacc_scan_frame_load_kernels", [ctypes.c_char_p, sz]),

@@ -6,6 +6,8 @@
 // A rejected call enqueues nothing, so the caller's status words stay as they
 // were.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cstdarg>
 #include <cstdint>
@@ -14,7 +16,9 @@
 #include <initializer_list>
 #include <mutex>
 #include <string>
+#include <vector>
 
+#include "../../include/sacc_shard.h"
 #include "internal.h"
 
 #ifndef SACC_BUILD_FLAGS
@@ -363,55 +367,59 @@ int sacc_scan_wait_probe(uint32_t limit, cudaStream_t stream) {
     });
 }
 
+// Host checks of one extended scan (throws Reject; enqueues nothing).
+static void validate_scan_ex(const char* api, const SaccScanExArgs& a, cudaStream_t stream) {
+    require_stream(api, stream);
+    if (a.dtype != SACC_DTYPE_F32 && a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16)
+        reject(api, "dtype must be f32, bf16 or f16");
+    if (a.layout != SACC_LAYOUT_BLD && a.layout != SACC_LAYOUT_BDL) reject(api, "layout must be BLD or BDL");
+    if (a.batch == 0 || a.channels == 0) reject(api, "batch and channels must be positive");
+    if (a.state == 0 || a.state > 32 || (a.state & (a.state - 1)) != 0)
+        reject(api, "state " + std::to_string(a.state) + " must be a power of two in [1, 32]");
+    if (a.groups == 0 || a.channels % a.groups != 0) reject(api, "groups must divide channels");
+    if (a.a_rows != 1 && a.a_rows != a.channels) reject(api, "A rows must be 1 or channels");
+    if (a.c_width != 1 && a.c_width != a.state) reject(api, "C width must be 1 or state");
+    std::uint64_t nseq = a.batch;
+    if (a.cu_seqlens) {
+        if (a.batch != 1) reject(api, "cu_seqlens needs batch 1");
+        if (a.nseq <= 0) reject(api, "nseq must be positive with cu_seqlens");
+        nseq = static_cast<std::uint64_t>(a.nseq);
+    }
+    // Kernels index in 64 bits; the 32-bit limit here is per tensor, as in
+    // the reference ABI, so the int32 sequence offsets stay valid.
+    const auto ud = elements(api, {a.batch, a.length, a.channels}, "u/delta/y");
+    const auto bn = elements(api, {a.batch, a.length, a.groups, a.state}, "B");
+    const auto cn = elements(api, {a.batch, a.length, a.groups, a.c_width}, "C");
+    const auto an = elements(api, {a.a_rows, a.state}, "A");
+    const auto hn = elements(api, {nseq, a.channels, a.state}, "state");
+    const std::size_t e = dtype_bytes(a.dtype), f = sizeof(float);
+    const std::size_t dn = a.d ? a.channels : 0, bias_n = a.delta_bias ? a.channels : 0;
+    const std::size_t align = a.dtype == SACC_DTYPE_F32 ? 4 : 2;
+    for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                            Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}, Region{a.y, ud * e, "y"}})
+        require_pointer(api, r, align);
+    for (const Region& r : {Region{a.a, an * f, "A"}, Region{a.d, dn * f, "D"}, Region{a.delta_bias, bias_n * f, "delta_bias"},
+                            Region{a.h0, a.h0 ? hn * f : 0, "h0"}, Region{a.h_final, a.h_final ? hn * f : 0, "h_final"},
+                            Region{a.cu_seqlens, a.cu_seqlens ? (nseq + 1) * sizeof(std::int32_t) : 0, "cu_seqlens"}})
+        require_pointer(api, r);
+    if (a.u == nullptr || a.delta == nullptr || a.a == nullptr || a.y == nullptr) reject(api, "u, delta, A and y are required");
+    if (a.length > 0 && (a.b == nullptr || a.c == nullptr)) reject(api, "B and C are required");
+    const Region yr{a.y, ud * e, "y"};
+    for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
+                            Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}})
+        if (overlaps(yr, r)) reject(api, std::string("y overlaps ") + r.name);
+    if (a.h_final) {
+        const Region hr{a.h_final, hn * f, "h_final"};
+        if (overlaps(hr, yr)) reject(api, "h_final overlaps y");
+    }
+}
+
 int sacc_selective_scan_ex(const SaccScanExArgs* args, cudaStream_t stream) {
     return guarded([&] {
         constexpr const char* api = "selective_scan_ex";
         if (args == nullptr) reject(api, "args are required");
-        const SaccScanExArgs& a = *args;
-        require_stream(api, stream);
-        if (a.dtype != SACC_DTYPE_F32 && a.dtype != SACC_DTYPE_BF16 && a.dtype != SACC_DTYPE_F16)
-            reject(api, "dtype must be f32, bf16 or f16");
-        if (a.layout != SACC_LAYOUT_BLD && a.layout != SACC_LAYOUT_BDL) reject(api, "layout must be BLD or BDL");
-        if (a.batch == 0 || a.channels == 0) reject(api, "batch and channels must be positive");
-        if (a.state == 0 || a.state > 32 || (a.state & (a.state - 1)) != 0)
-            reject(api, "state " + std::to_string(a.state) + " must be a power of two in [1, 32]");
-        if (a.groups == 0 || a.channels % a.groups != 0) reject(api, "groups must divide channels");
-        if (a.a_rows != 1 && a.a_rows != a.channels) reject(api, "A rows must be 1 or channels");
-        if (a.c_width != 1 && a.c_width != a.state) reject(api, "C width must be 1 or state");
-        std::uint64_t nseq = a.batch;
-        if (a.cu_seqlens) {
-            if (a.batch != 1) reject(api, "cu_seqlens needs batch 1");
-            if (a.nseq <= 0) reject(api, "nseq must be positive with cu_seqlens");
-            nseq = static_cast<std::uint64_t>(a.nseq);
-        }
-        // Kernels index in 64 bits; the 32-bit limit here is per tensor, as in
-        // the reference ABI, so the int32 sequence offsets stay valid.
-        const auto ud = elements(api, {a.batch, a.length, a.channels}, "u/delta/y");
-        const auto bn = elements(api, {a.batch, a.length, a.groups, a.state}, "B");
-        const auto cn = elements(api, {a.batch, a.length, a.groups, a.c_width}, "C");
-        const auto an = elements(api, {a.a_rows, a.state}, "A");
-        const auto hn = elements(api, {nseq, a.channels, a.state}, "state");
-        const std::size_t e = dtype_bytes(a.dtype), f = sizeof(float);
-        const std::size_t dn = a.d ? a.channels : 0, bias_n = a.delta_bias ? a.channels : 0;
-        const std::size_t align = a.dtype == SACC_DTYPE_F32 ? 4 : 2;
-        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
-                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}, Region{a.y, ud * e, "y"}})
-            require_pointer(api, r, align);
-        for (const Region& r : {Region{a.a, an * f, "A"}, Region{a.d, dn * f, "D"}, Region{a.delta_bias, bias_n * f, "delta_bias"},
-                                Region{a.h0, a.h0 ? hn * f : 0, "h0"}, Region{a.h_final, a.h_final ? hn * f : 0, "h_final"},
-                                Region{a.cu_seqlens, a.cu_seqlens ? (nseq + 1) * sizeof(std::int32_t) : 0, "cu_seqlens"}})
-            require_pointer(api, r);
-        if (a.u == nullptr || a.delta == nullptr || a.a == nullptr || a.y == nullptr) reject(api, "u, delta, A and y are required");
-        if (a.length > 0 && (a.b == nullptr || a.c == nullptr)) reject(api, "B and C are required");
-        const Region yr{a.y, ud * e, "y"};
-        for (const Region& r : {Region{a.u, ud * e, "u"}, Region{a.delta, ud * e, "delta"}, Region{a.b, bn * e, "B"},
-                                Region{a.c, cn * e, "C"}, Region{a.z, a.z ? ud * e : 0, "z"}})
-            if (overlaps(yr, r)) reject(api, std::string("y overlaps ") + r.name);
-        if (a.h_final) {
-            const Region hr{a.h_final, hn * f, "h_final"};
-            if (overlaps(hr, yr)) reject(api, "h_final overlaps y");
-        }
-        CK(launch_scan_ex(a, sm_count(), stream));
+        validate_scan_ex(api, *args, stream);
+        CK(launch_scan_ex(*args, sm_count(), stream));
     });
 }
 
@@ -789,6 +797,160 @@ int sacc_model_producer_cuda(const float* images, size_t image_elements, const S
             for (int j = i + 1; j < 18; ++j)
                 if (overlaps(regions[i], regions[j])) reject(api, "overlapping model producer buffers");
         CK(launch_model_producer(p, producer, workspace, sm_count(), stream));
+    });
+}
+
+// ---- batch-sharded scan over the GPUs of one process (include/sacc_shard.h)
+
+int sacc_shard_rows(uint64_t total, int world, int rank, uint64_t* row0, uint64_t* rows) {
+    return guarded([&] {
+        constexpr const char* api = "shard_rows";
+        if (world <= 0 || rank < 0 || rank >= world) reject(api, "rank must be in [0, world)");
+        if (row0 == nullptr || rows == nullptr) reject(api, "row0 and rows are required");
+        const uint64_t base = total / static_cast<uint64_t>(world), extra = total % static_cast<uint64_t>(world);
+        const uint64_t r = static_cast<uint64_t>(rank);
+        *row0 = r * base + (r < extra ? r : extra);
+        *rows = base + (r < extra ? 1 : 0);
+    });
+}
+
+} // extern "C"
+
+namespace {
+// NCCL entry points, resolved from libnccl.so.2 on first use (a process that
+// already loaded NCCL, e.g. through its framework, gets that copy).
+struct Nccl {
+    ncclResult_t (*comm_init_all)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+    std::string why;
+};
+
+const Nccl& nccl() {
+    static const Nccl lib = [] {
+        Nccl n;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h == nullptr) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (h == nullptr) {
+            n.why = std::string("NCCL is not available: ") + dlerror();
+            return n;
+        }
+        n.comm_init_all = reinterpret_cast<decltype(n.comm_init_all)>(dlsym(h, "ncclCommInitAll"));
+        n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
+        n.group_start = reinterpret_cast<decltype(n.group_start)>(dlsym(h, "ncclGroupStart"));
+        n.group_end = reinterpret_cast<decltype(n.group_end)>(dlsym(h, "ncclGroupEnd"));
+        n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
+        if (!n.comm_init_all || !n.comm_destroy || !n.all_gather || !n.group_start || !n.group_end || !n.error_string)
+            n.why = "NCCL library lacks an entry point (ncclCommInitAll, ncclCommDestroy, ncclAllGather, ncclGroupStart, "
+                    "ncclGroupEnd, ncclGetErrorString)";
+        return n;
+    }();
+    return lib;
+}
+
+void nck(ncclResult_t r, const char* call) {
+    if (r != ncclSuccess) throw sacc::CudaFail{std::string(call) + ": " + nccl().error_string(r)};
+}
+
+// Restores the caller's current device on every exit.
+struct DeviceGuard {
+    int saved = 0;
+    bool ok = false;
+    DeviceGuard() { ok = cudaGetDevice(&saved) == cudaSuccess; }
+    ~DeviceGuard() {
+        if (ok) cudaSetDevice(saved);
+    }
+};
+} // namespace
+
+struct SaccShardGroup {
+    std::vector<int> devices;
+    std::vector<ncclComm_t> comms;
+};
+
+extern "C" {
+
+int sacc_shard_group_create(int ndev, const int* devices, SaccShardGroup** group) {
+    return guarded([&] {
+        constexpr const char* api = "shard_group";
+        if (group == nullptr) reject(api, "group is required");
+        *group = nullptr;
+        int count = 0;
+        CK(cudaGetDeviceCount(&count));
+        if (ndev <= 0 || devices == nullptr) reject(api, "at least one device is required");
+        for (int i = 0; i < ndev; ++i) {
+            if (devices[i] < 0 || devices[i] >= count) reject(api, "device " + std::to_string(devices[i]) + " does not exist");
+            for (int j = 0; j < i; ++j)
+                if (devices[j] == devices[i]) reject(api, "device " + std::to_string(devices[i]) + " is listed twice");
+        }
+        const Nccl& n = nccl();
+        if (!n.why.empty()) throw CudaFail{std::string(api) + ": " + n.why};
+        DeviceGuard keep;
+        auto* g = new SaccShardGroup{std::vector<int>(devices, devices + ndev), std::vector<ncclComm_t>(ndev, nullptr)};
+        const ncclResult_t r = n.comm_init_all(g->comms.data(), ndev, devices);
+        if (r != ncclSuccess) {
+            delete g;
+            nck(r, "ncclCommInitAll");
+        }
+        *group = g;
+    });
+}
+
+int sacc_shard_group_destroy(SaccShardGroup* group) {
+    return guarded([&] {
+        if (group == nullptr) return;
+        DeviceGuard keep;
+        std::string first_error;
+        for (ncclComm_t c : group->comms) {
+            const ncclResult_t r = c ? nccl().comm_destroy(c) : ncclSuccess;
+            if (r != ncclSuccess && first_error.empty()) first_error = nccl().error_string(r);
+        }
+        delete group;
+        if (!first_error.empty()) throw CudaFail{std::string("ncclCommDestroy: ") + first_error};
+    });
+}
+
+int sacc_scan_sharded_forward(SaccShardGroup* group, const SaccScanExArgs* args, const cudaStream_t* streams,
+                              void* const* gather, size_t shard_y_bytes) {
+    return guarded([&] {
+        constexpr const char* api = "scan_sharded";
+        if (group == nullptr || args == nullptr || streams == nullptr) reject(api, "group, args and streams are required");
+        const int ndev = static_cast<int>(group->devices.size());
+        DeviceGuard keep;
+        // Every shard is checked on the host before any device gets work.
+        for (int i = 0; i < ndev; ++i) {
+            const std::string shard = std::string(api) + " shard " + std::to_string(i);
+            CK(cudaSetDevice(group->devices[i]));
+            int stream_device = -1;
+            if (streams[i] != nullptr && streams[i] != cudaStreamLegacy && streams[i] != cudaStreamPerThread) {
+                CK(cudaStreamGetDevice(streams[i], &stream_device));
+                if (stream_device != group->devices[i]) reject(shard.c_str(), "stream belongs to another CUDA device");
+            }
+            validate_scan_ex(shard.c_str(), args[i], streams[i]);
+            if (gather) {
+                const std::size_t ybytes = args[i].batch * args[i].length * args[i].channels * dtype_bytes(args[i].dtype);
+                if (ybytes != shard_y_bytes) reject(shard.c_str(), "y must hold exactly shard_y_bytes bytes to be gathered");
+                if (gather[i] == nullptr) reject(shard.c_str(), "gather buffer is null");
+            }
+        }
+        for (int i = 0; i < ndev; ++i) {
+            CK(cudaSetDevice(group->devices[i]));
+            CK(launch_scan_ex(args[i], sm_count(), streams[i]));
+        }
+        if (gather) {
+            const Nccl& n = nccl();
+            nck(n.group_start(), "ncclGroupStart");
+            ncclResult_t r = ncclSuccess;
+            for (int i = 0; i < ndev && r == ncclSuccess; ++i)
+                r = n.all_gather(args[i].y, gather[i], shard_y_bytes, ncclUint8, group->comms[i], streams[i]);
+            const ncclResult_t e = n.group_end();
+            nck(r, "ncclAllGather");
+            nck(e, "ncclGroupEnd");
+        }
     });
 }
 

@@ -106,3 +106,21 @@ def test_gather_batch_rejects_wrong_shard():
     from saccade_v1_b200.shard import Shard
     with pytest.raises(ValueError):
         gather_batch(torch.zeros(3, 2), Shard(0, 2, 0, 2, 2), 4)
+
+
+def test_c_abi_shard_rows_matches_python_split():
+    """sacc_shard_rows (include/sacc_shard.h) splits rows exactly as shard.shard_rows."""
+    import ctypes
+
+    from saccade_v1_b200 import _lib
+    from saccade_v1_b200.shard import shard_rows
+    L = _lib.load()
+    r0, n = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    for total in (0, 1, 7, 64, 65, 511, 4096):
+        for world in (1, 2, 3, 4, 8):
+            for rank in range(world):
+                assert L.sacc_shard_rows(total, world, rank, ctypes.byref(r0), ctypes.byref(n)) == _lib.SACC_OK
+                s = shard_rows(total, world, rank)
+                assert (r0.value, r0.value + n.value) == (s.begin, s.end), (total, world, rank)
+    assert L.sacc_shard_rows(8, 2, 2, ctypes.byref(r0), ctypes.byref(n)) == _lib.SACC_EINVAL
+    assert "rank must be in [0, world)" in _lib.last_error()

@@ -12,11 +12,11 @@
  *   SaccScanStatus / SACC_SCAN_*    include/saccade/selective_scan_cuda.hpp:21-46
  *   SaccScanShape                   include/saccade/selective_scan.hpp:19-27
  *   SaccScanInputs                  include/saccade/selective_scan_cuda.hpp:48-55
- *   sacc_scan_load_kernels          selective_scan_cuda_load_kernels, cuda/selective_scan.cu:341-357
- *   sacc_selective_scan_f32         selective_scan_cuda, cuda/selective_scan.cu:359-400
- *   sacc_cross_scan_expand_f32      cross_scan_expand_cuda, cuda/selective_scan.cu:402-417
- *   sacc_cross_scan_merge_f32       cross_scan_merge_cuda, cuda/selective_scan.cu:419-434
- *   sacc_scan_identity              selective_scan_cuda_identity, cuda/selective_scan.cu:436-446
+ *   sacc_scan_load_kernels          selective_scan_cuda_load_kernels, cuda/selective_scan.cu:252-268
+ *   sacc_selective_scan_f32         selective_scan_cuda, cuda/selective_scan.cu:270-311
+ *   sacc_cross_scan_expand_f32      cross_scan_expand_cuda, cuda/selective_scan.cu:313-328
+ *   sacc_cross_scan_merge_f32       cross_scan_merge_cuda, cuda/selective_scan.cu:330-345
+ *   sacc_scan_identity              selective_scan_cuda_identity, cuda/selective_scan.cu:347-357
  *   sacc_selective_scan_f16         no counterpart: the FP16-activation form behind plugin
  *                                   SelectiveScan v3 (the reference's FP16 engine keeps its scan
  *                                   plugins FP32 and casts around them,

@@ -34,8 +34,8 @@
  *   saccade::CrossScanMerge  v1  fields: height, width (INT32)
  * Each entry point below implements one IPluginV3 / IPluginCreatorV3One method
  * with the reference's semantics and messages, on plain structs; a TensorRT
- * adapter only translates TensorRT's descriptors and fields into these
- * (INTEGRATION.md).  Errors: SACC_EINVAL (nothing enqueued) or SACC_ECUDA,
+ * adapter only translates TensorRT's descriptors (PluginTensorDesc) and fields
+ * (PluginField) into these.  Errors: SACC_EINVAL (nothing enqueued) or SACC_ECUDA,
  * message from sacc_plugin_last_error().
  */
 #ifndef SACC_SCAN_PLUGIN_H

@@ -26,9 +26,9 @@
 #define ORACLE_INVALID 1
 #define ORACLE_RANGE 2
 
-/* src/selective_scan.cpp:79 -- the deployed kernel indexes with int32. */
+/* src/selective_scan.cpp:15 -- the deployed kernel indexes with int32. */
 static const size_t kMaxElements = 2147483647u;
-/* src/selective_scan.cpp:80 */
+/* src/selective_scan.cpp:16 */
 static const double kFp32Max = 3.4028234663852886e38;
 
 typedef struct {
@@ -41,10 +41,10 @@ static int fail(char* msg, size_t cap, int code, const char* text) {
     return code;
 }
 
-/* src/selective_scan.cpp:123 -- threshold 20, log1p(exp(x)) below it. */
+/* src/selective_scan.cpp:59 -- threshold 20, log1p(exp(x)) below it. */
 double sacc_oracle_softplus(double x) { return x > 20.0 ? x : log1p(exp(x)); }
 
-/* src/selective_scan.cpp:84-92: product of dims with an int32 capacity check. */
+/* src/selective_scan.cpp:20-28: product of dims with an int32 capacity check. */
 static int elements(const uint64_t* dims, int n, size_t* out) {
     size_t product = 1;
     for (int i = 0; i < n; ++i) {
@@ -57,7 +57,7 @@ static int elements(const uint64_t* dims, int n, size_t* out) {
 
 static int is_finite_f(float v) { return isfinite(v); }
 
-/* src/selective_scan.cpp:99-102 */
+/* src/selective_scan.cpp:35-38 */
 static int expect_finite(const float* v, size_t n, const char* name, char* msg, size_t cap) {
     for (size_t i = 0; i < n; ++i)
         if (!is_finite_f(v[i])) {
@@ -67,7 +67,7 @@ static int expect_finite(const float* v, size_t n, const char* name, char* msg, 
     return 1;
 }
 
-/* src/selective_scan.cpp:104-109 */
+/* src/selective_scan.cpp:40-45 */
 static int in_range(double value, const char* quantity, size_t b, size_t t, size_t d, char* msg, size_t cap) {
     if (!(fabs(value) <= kFp32Max)) {
         if (msg && cap)
@@ -78,7 +78,7 @@ static int in_range(double value, const char* quantity, size_t b, size_t t, size
 }
 
 /*
- * src/selective_scan.cpp:125-173 (selective_scan_reference).
+ * src/selective_scan.cpp:61-109 (selective_scan_reference).
  * Tensors are dense row-major FP32 with the reference ABI layouts:
  *   u, delta, y: (batch, length, channels); a: (a_rows, state);
  *   b: (batch, length, state); c: (batch, length, c_width); d: (channels).
@@ -196,7 +196,7 @@ void sacc_oracle_scan_bound(const OracleShape* s, const float* u, const float* d
  * Extended scan (no counterpart in the reference: the reference contract has
  * zero initial state, no final state, no varlen and no fused gate/bias,
  * include/saccade/selective_scan.hpp:17-18).  The core recurrence is the one
- * of src/selective_scan.cpp:152-170 and reduces to it exactly when every
+ * of src/selective_scan.cpp:88-107 and reduces to it exactly when every
  * extension is off (tests/test_oracle.py checks that equality bit for bit).
  *
  * layout 0 ("BLD", the reference ABI): u, delta, z, y (batch, length, D);
@@ -319,7 +319,7 @@ void sacc_oracle_neg_exp(const float* a_log, size_t n, double* a) {
     for (size_t i = 0; i < n; ++i) a[i] = -exp((double)a_log[i]);
 }
 
-/* src/selective_scan.cpp:175-180 (cross_scan_source).  Returns (size_t)-1 on a bad argument. */
+/* src/selective_scan.cpp:111-116 (cross_scan_source).  Returns (size_t)-1 on a bad argument. */
 size_t sacc_oracle_cross_scan_source(size_t direction, size_t token, size_t height, size_t width) {
     if (direction > 3 || height == 0 || width == 0 || token / width >= height) return (size_t)-1;
     const size_t row = token / width, col = token % width;
@@ -327,7 +327,7 @@ size_t sacc_oracle_cross_scan_source(size_t direction, size_t token, size_t heig
     return (flip_h ? height - 1 - row : row) * width + (flip_w ? width - 1 - col : col);
 }
 
-/* src/selective_scan.cpp:182-197: x (batch, C, H, W) -> tokens (4 batch, H W, C). */
+/* src/selective_scan.cpp:118-133: x (batch, C, H, W) -> tokens (4 batch, H W, C). */
 void sacc_oracle_cross_scan_expand(const float* x, size_t batch, size_t channels, size_t height, size_t width, float* out) {
     const size_t L = height * width;
     for (size_t k = 0; k < 4; ++k)
@@ -339,7 +339,7 @@ void sacc_oracle_cross_scan_expand(const float* x, size_t batch, size_t channels
             }
 }
 
-/* src/selective_scan.cpp:199-216: tokens -> (batch, C, H, W), mean of the four directions. */
+/* src/selective_scan.cpp:135-154: tokens -> (batch, C, H, W), mean of the four directions. */
 void sacc_oracle_cross_scan_merge(const double* y, size_t batch, size_t channels, size_t height, size_t width, double* out) {
     const size_t L = height * width;
     for (size_t i = 0; i < batch; ++i)

@@ -1,7 +1,7 @@
 // capi.cpp -- extern "C" entry points of libsacc_scan.so (include/sacc_scan.h).
 //
 // Host validation restates the reference's selective_scan_cuda host side
-// (cuda/selective_scan.cu:285-400) with the same diagnostics, but reports
+// (cuda/selective_scan.cu:198-311) with the same diagnostics, but reports
 // them as return codes plus a thread-local message instead of exceptions.
 // A rejected call enqueues nothing, so the caller's status words stay as they
 // were.
@@ -77,7 +77,7 @@ bool overlaps(const Region& a, const Region& b) {
 }
 
 // Outputs (output tensor, status) must not overlap inputs or each other
-// (reference cuda/selective_scan.cu:315-325).
+// (reference cuda/selective_scan.cu:227-236).
 void require_regions(const char* api, std::initializer_list<Region> inputs, const Region& out, const Region& status) {
     for (const auto& r : inputs) require_pointer(api, r);
     require_pointer(api, out);
@@ -130,7 +130,7 @@ int guarded(F&& body) {
 
 std::size_t dtype_bytes(int dtype) { return dtype == SACC_DTYPE_F32 ? 4 : 2; }
 
-// Host side of the reference ABI (cuda/selective_scan.cu:285-400): FP32
+// Host side of the reference ABI (cuda/selective_scan.cu:198-311): FP32
 // activations, or FP16 ones (u, delta, B, C, y) with `half`.
 void reference_scan(const char* api, const SaccScanShape& s, const void* u, const void* delta, const float* a, const void* b,
                     const void* c, const float* d, void* y, SaccScanStatus* status, cudaStream_t stream, bool half) {
@@ -281,7 +281,7 @@ int sacc_scan_load_kernels(char* report, size_t report_bytes) {
     });
 }
 
-// reference cuda/selective_scan.cu:359-400
+// reference cuda/selective_scan.cu:270-311
 int sacc_selective_scan_f32(const SaccScanShape* shape, const SaccScanInputs* in, float* y, SaccScanStatus* status,
                             cudaStream_t stream) {
     return guarded([&] {
@@ -306,7 +306,7 @@ static std::size_t cross_total(const char* api, const SaccCrossScanShape& s) {
     return elements(api, {4, s.batch, s.height, s.width, s.channels}, "tokens");
 }
 
-// reference cuda/selective_scan.cu:402-417
+// reference cuda/selective_scan.cu:313-328
 int sacc_cross_scan_expand_f32(const SaccCrossScanShape* shape, const float* x, float* tokens, SaccScanStatus* status,
                                cudaStream_t stream) {
     return guarded([&] {
@@ -326,7 +326,7 @@ int sacc_cross_scan_expand_f32(const SaccCrossScanShape* shape, const float* x, 
     });
 }
 
-// reference cuda/selective_scan.cu:419-434
+// reference cuda/selective_scan.cu:330-345
 int sacc_cross_scan_merge_f32(const SaccCrossScanShape* shape, const float* y, float* out, SaccScanStatus* status,
                               cudaStream_t stream) {
     return guarded([&] {

@@ -34,7 +34,7 @@ namespace {
 
 constexpr int kTile = 32, kRows = 8;
 
-// Position of direction k's token t (reference src/selective_scan.cpp:175-180).
+// Position of direction k's token t (reference src/selective_scan.cpp:111-116).
 __device__ __forceinline__ unsigned src_pos(unsigned k, unsigned t, unsigned H, unsigned W) {
     const unsigned row = t / W, col = t % W;
     const bool flip_h = k == 1 || k == 3, flip_w = k == 1 || k == 2;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(256) cross_conv_kernel(const T* __restrict__ x
 // One thread per (image b, position p, 8 channels): the mean of the four
 // directions' gated outputs at p, ((y0 + y1) + y2) + y3 times 0.25, the
 // quarters summed instead when the sum overflows (the reference merge,
-// cuda/selective_scan.cu:180-192), stored position-major in T.
+// cuda/selective_scan.cu:177-192), stored position-major in T.
 template <typename T>
 __global__ void __launch_bounds__(256) cross_mean_kernel(const T* __restrict__ y, unsigned batch, unsigned H, unsigned W,
                                                          unsigned D, T* __restrict__ mean) {

@@ -26,7 +26,7 @@ constexpr int kRows = 8; // 32 x 8 threads per tile
 __device__ __forceinline__ bool finite32(float x) { return fabsf(x) <= FLT_MAX; }
 
 // Source position (h * W + w) of token t in direction k (reference
-// src/selective_scan.cpp:175-180; each flip is an involution, so this is also
+// src/selective_scan.cpp:111-116; each flip is an involution, so this is also
 // the token of position t in direction k).
 __device__ __forceinline__ unsigned long long cross_source(unsigned k, unsigned long long t, unsigned long long H,
                                                            unsigned long long W) {

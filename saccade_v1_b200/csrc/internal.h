@@ -31,7 +31,7 @@ inline cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, std::size_t
 }
 
 // int32 element capacity of every tensor of the reference ABI
-// (reference src/selective_scan.cpp:79, cuda/selective_scan.cu:119).
+// (reference src/selective_scan.cpp:15, cuda/selective_scan.cu:30).
 constexpr std::size_t kMaxElements = 2147483647u;
 
 struct CheckedTensor {

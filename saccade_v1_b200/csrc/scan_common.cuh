@@ -63,7 +63,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 // softplus with the reference's threshold (x > 20 passes through,
-// src/selective_scan.cpp:123), FP32 library functions.
+// src/selective_scan.cpp:59), FP32 library functions.
 __device__ __forceinline__ float softplus_precise(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // Same threshold; e^x from the special-function unit, log1p from the library
@@ -73,18 +73,20 @@ __device__ __forceinline__ float softplus_fast(float x) {
 }
 
 // softplus(x) = max(x, 0) + log1p(e^-|x|) with log1p(e) = e * P(e) on
-// e in (0, 1] (degree-7 least-squares fit, relative error 3.2e-7 in FP32):
-// one special-function exp and eight FMAs, no library call.  x > 20 passes
-// through as in the reference (src/selective_scan.cpp:123).
+// e in (0, 1]: P of degree 7, the minimax fit of the relative error
+// (gen_softplus_poly.py in this directory: Remez exchange in binary64,
+// coefficients rounded to FP32; the FP32 Horner evaluation is within 3.3e-7
+// relative of log1p(e)): one special-function exp and eight FMAs, no library
+// call.  x > 20 passes through as in the reference (src/selective_scan.cpp:59).
 __device__ __forceinline__ float softplus_poly(float x) {
     const float e = fast_exp2(-fabsf(x) * kLog2e);
-    float q = fmaf(-8.336497e-3f, e, 4.337085e-2f);
-    q = fmaf(q, e, -1.0667790e-1f);
-    q = fmaf(q, e, 1.7675494e-1f);
-    q = fmaf(q, e, -2.4470469e-1f);
-    q = fmaf(q, e, 3.3271188e-1f);
-    q = fmaf(q, e, -4.9997127e-1f);
-    q = fmaf(q, e, 9.9999976e-1f);
+    float q = fmaf(-8.53920821e-3f, e, 4.40896340e-2f);
+    q = fmaf(q, e, -1.07681714e-1f);
+    q = fmaf(q, e, 1.77452415e-1f);
+    q = fmaf(q, e, -2.44954631e-1f);
+    q = fmaf(q, e, 3.32754791e-1f);
+    q = fmaf(q, e, -4.99974042e-1f);
+    q = fmaf(q, e, 9.99999821e-1f);
     const float r = fmaf(e, q, fmaxf(x, 0.0f));
     return x > 20.0f ? x : r;
 }

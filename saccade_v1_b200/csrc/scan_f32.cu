@@ -1,7 +1,7 @@
 // scan_f32.cu -- reference-ABI FP32 selective scan for sm_100a.
 //
-// Contract: reference cuda/selective_scan.cu:359-400 (selective_scan_cuda),
-// arithmetic: cuda/selective_scan.cu:130-221.  Layouts (B,L,Dc) row-major FP32.
+// Contract: reference cuda/selective_scan.cu:270-311 (selective_scan_cuda),
+// arithmetic: cuda/selective_scan.cu:41-132.  Layouts (B,L,Dc) row-major FP32.
 //
 // B200 design (differs from the reference's one-thread-per-(b,d,n) kernel):
 //  * one thread owns a (batch, channel) lane and keeps all N states of that
@@ -84,7 +84,7 @@ __device__ __forceinline__ Scaled split(float x) {
 
 // softplus(x) with the reference's threshold (x > 20 passes through), kept as
 // (m, e) so that a Delta below the FP32 normal range keeps full precision
-// (reference cuda/selective_scan.cu:49-59).  For -1024 <= x < -80 the result is
+// (reference cuda/selective_scan.cu:49-61).  For -1024 <= x < -80 the result is
 // e^x (log1p(e^x) = e^x to 1e-35 relative there), formed as e^r * 2^k with the
 // Cody-Waite reduction k = rint(x / ln2), r = (x - k ln2_hi) - k ln2_lo
 // (ln2_hi = 0x3f317200 has 16 significant bits, so k * ln2_hi is exact).
@@ -185,7 +185,7 @@ __device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a
     return fast;
 }
 
-// The reference's scaled per-token state update (cuda/selective_scan.cu:189-192).
+// The reference's scaled per-token state update (cuda/selective_scan.cu:100-103).
 template <int N, int CW>
 __device__ __forceinline__ void states_scaled(const float (&h)[N], const float (&a)[N], const Token<N, CW>& k, float (&hn)[N],
                                            float (&decay)[N], float (&drive)[N]) {
@@ -212,7 +212,7 @@ __device__ __forceinline__ void step_carry(float (&h)[N], float (&prod)[N], cons
 }
 
 // Pass 2: one token with output and the reference's failure order
-// (cuda/selective_scan.cu:193-212).  Returns the failure bits (0 = ok).  With
+// (cuda/selective_scan.cu:104-129).  Returns the failure bits (0 = ok).  With
 // kHalfOut an output that FP16 cannot hold is an output range failure.
 template <int N, int CW, bool kHalfOut>
 __device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N], const Token<N, CW>& k, bool has_d, float skip_d,
@@ -238,7 +238,7 @@ __device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N],
     float out = has_d ? __fadd_rn(sum, skip) : sum;
     if (!finite32(out)) {
         // Every term is finite but a partial sum left the FP32 range: repeat
-        // with exact power-of-two scaling (reference cuda/selective_scan.cu:205-211).
+        // with exact power-of-two scaling (reference cuda/selective_scan.cu:116-122).
 #pragma unroll
         for (int n = 0; n < N; ++n) s[n] = __fmul_rn(term[n], 0x1p-8f);
         const float scaled = tree_sum<N>(s);
@@ -251,7 +251,7 @@ __device__ __forceinline__ unsigned step_out(float (&h)[N], const float (&a)[N],
     return 0;
 }
 
-// Exact NaN/Inf test over the listed tensors (reference cuda/selective_scan.cu:226-234).
+// Exact NaN/Inf test over the listed tensors (reference cuda/selective_scan.cu:137-147).
 __device__ void check_tensors(const CheckList& list, unsigned long long first, unsigned long long stride,
                               SaccScanStatus* status) {
     std::uint32_t found = 0;
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kThreads) check_kernel(CheckList list, SaccSca
 
 // Last kernel of every call: poison every output on failure (the FP32 quiet
 // NaN 0x7fc00000, or the FP16 one 0x7e00), then write done (reference
-// cuda/selective_scan.cu:238-244).
+// cuda/selective_scan.cu:149-155).
 template <typename W, unsigned kPoison>
 __global__ void __launch_bounds__(kThreads) finalize_kernel(W* out, unsigned long long count, SaccScanStatus* status) {
     pdl_wait(); // launched with programmatic stream serialization: the previous grid's status bits first

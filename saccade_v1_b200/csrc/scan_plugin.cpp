@@ -8,9 +8,9 @@
 // TensorRT's workspace, and saccade::CrossScanMambaBlock v1 a head level's
 // expand -> block -> merge on the FP32 maps (sacc_cross_scan_block_forward).  TensorRT itself is not available on this
 // platform, so the plugin's logic lives here behind a C ABI whose calls map
-// one to one onto the IPluginV3 methods; a thin TensorRT adapter (see
-// INTEGRATION.md) translates TensorRT's descriptor and field types into these
-// structs and forwards:
+// one to one onto the IPluginV3 methods; a thin TensorRT adapter translates
+// TensorRT's descriptor and field types (PluginTensorDesc, PluginField) into
+// these structs and forwards:
 //
 //   sacc_plugin_create           IPluginCreatorV3One::createPlugin   :365-393
 //   sacc_plugin_fields           getFieldsToSerialize                :244

@@ -1,7 +1,7 @@
 // scan_step.cu -- one L = 1 selective-scan update of carried per-track state
 // (a tracker's per-frame step).  No counterpart in the
 // reference, whose operator has no carried state (docs/SCAN_CONTRACT.md:60);
-// the recurrence is the reference's (src/selective_scan.cpp:152-170) applied
+// the recurrence is the reference's (src/selective_scan.cpp:88-107) applied
 // to one token starting from the stored state.
 //
 // HBM-bound: per (track, channel) lane the 16 FP32 states (64 bytes) are read

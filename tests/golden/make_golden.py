@@ -1,8 +1,9 @@
 """Generates the golden fixtures under tests/golden/ from the reference.
 
-Run from the repository root in a checkout that has the reference sources:
-    make -C oracle            # builds oracle/_ref/libref_scan.so from them
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+Run from the repository root, naming the reference checkout on the command
+line or in SACC_REFERENCE_ROOT:
+    make -C oracle REF=<reference checkout>   # builds oracle/_ref/libref_scan.so from it
+    python tests/golden/make_golden.py <reference checkout>
 
 Writes
   scan_expected.json  the bc-derived closed-form values of the reference's
@@ -52,7 +53,9 @@ def expected_table(ref_root: str) -> dict[str, list[float]]:
 
 
 def main() -> None:
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SACC_REFERENCE_ROOT", "")
+    if not ref_root or not os.path.isdir(ref_root):
+        sys.exit("usage: make_golden.py <reference checkout> (or set SACC_REFERENCE_ROOT)")
     with open(os.path.join(OUT, "scan_expected.json"), "w") as f:
         json.dump(expected_table(ref_root), f, indent=0)
 

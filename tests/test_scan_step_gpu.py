@@ -1,6 +1,6 @@
 """GPU parity of the per-frame step (sacc_selective_scan_step).
 
-The step is the reference recurrence (src/selective_scan.cpp:152-170) applied
+The step is the reference recurrence (src/selective_scan.cpp:88-107) applied
 to one token from carried state.  It is pinned by:
   - the oracle's extended scan with L = 1, initial and final state;
   - T consecutive steps == one T-token scan from the same initial state;

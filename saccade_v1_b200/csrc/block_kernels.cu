@@ -63,12 +63,20 @@ __global__ void __launch_bounds__(256) scale_columns_kernel(const T* __restrict_
 // special-function exp and a fast divide.  One thread per (sequence, channel)
 // walks the tokens keeping the last K - 1 inputs in registers; consecutive
 // threads take consecutive channels, so every load and store is coalesced.
+// Block 0 of a launch clears `zero` (after griddepcontrol.wait: every earlier
+// kernel of the stream, the previous user of these words included, is done).
+__device__ __forceinline__ void clear_span(const ZeroSpan& zero) {
+    if (zero.words != 0 && blockIdx.x == 0 && blockIdx.y == 0)
+        for (unsigned long long i = threadIdx.x; i < zero.words; i += blockDim.x) zero.ptr[i] = 0ull;
+}
+
 template <typename T, int K>
 __global__ void __launch_bounds__(256) conv_silu_kernel(const T* __restrict__ x, unsigned long long ldx,
                                                         const float* __restrict__ w, const float* __restrict__ bias,
                                                         unsigned long long batch, unsigned long long len,
-                                                        unsigned long long dim, T* __restrict__ u) {
+                                                        unsigned long long dim, T* __restrict__ u, ZeroSpan zero) {
     pdl_wait();
+    clear_span(zero);
     const unsigned long long lane = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
     if (lane >= batch * dim) return;
     const unsigned long long b = lane / dim, d = lane % dim;
@@ -102,8 +110,9 @@ template <typename T>
 __global__ void __launch_bounds__(256) conv4_silu_rows_kernel(const T* __restrict__ x, unsigned long long ldx,
                                                               const float* __restrict__ w, const float* __restrict__ bias,
                                                               unsigned long long batch, unsigned long long len,
-                                                              unsigned long long dim, T* __restrict__ u) {
+                                                              unsigned long long dim, T* __restrict__ u, ZeroSpan zero) {
     pdl_wait();
+    clear_span(zero);
     constexpr int K = 4, R = 4; // taps, rows per thread
     // 32-bit index arithmetic (the launcher keeps the thread count below 2^32).
     const unsigned groups = static_cast<unsigned>(dim / 8), quads = static_cast<unsigned>((len + R - 1) / R);
@@ -173,8 +182,9 @@ template <typename T>
 __global__ void __launch_bounds__(kConvCh) conv4_silu_tile_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                  const float* __restrict__ w, const float* __restrict__ bias,
                                                                  unsigned long long len, unsigned long long dim,
-                                                                 unsigned tiles_per_seq, T* __restrict__ u) {
+                                                                 unsigned tiles_per_seq, T* __restrict__ u, ZeroSpan zero) {
     pdl_wait();
+    clear_span(zero);
     __shared__ alignas(128) T tile[(kConvRows + 3) * kConvCh];
     __shared__ alignas(8) std::uint64_t bar;
     const int tid = threadIdx.x;
@@ -285,7 +295,7 @@ cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, un
 
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
                              unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, ZeroSpan zero) {
     if (kwidth != 4) return cudaErrorInvalidConfiguration;
     const auto al16 = [](const void* ptr) { return reinterpret_cast<std::uintptr_t>(ptr) % 16 == 0; };
     // TMA tiles: channels in 128-wide blocks, 16-byte aligned rows.
@@ -305,9 +315,9 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
             const unsigned tps = static_cast<unsigned>(tiles_per_seq);
             if (dtype == SACC_DTYPE_BF16)
                 return launch_pdl_k(conv4_silu_tile_kernel<__nv_bfloat16>, grid, dim3(kConvCh), 0, stream, tm, w, bias, len, dim,
-                                    tps, static_cast<__nv_bfloat16*>(u));
+                                    tps, static_cast<__nv_bfloat16*>(u), zero);
             return launch_pdl_k(conv4_silu_tile_kernel<__half>, grid, dim3(kConvCh), 0, stream, tm, w, bias, len, dim, tps,
-                                static_cast<__half*>(u));
+                                static_cast<__half*>(u), zero);
         }
     }
     const unsigned long long threads = batch * ((len + 3) / 4) * (dim / 8), row_blocks = (threads + 255) / 256;
@@ -316,18 +326,18 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
         if (dtype == SACC_DTYPE_BF16)
             return launch_pdl_k(conv4_silu_rows_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(row_blocks)), dim3(256), 0,
                                 stream, static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim,
-                                static_cast<__nv_bfloat16*>(u));
+                                static_cast<__nv_bfloat16*>(u), zero);
         return launch_pdl_k(conv4_silu_rows_kernel<__half>, dim3(static_cast<unsigned>(row_blocks)), dim3(256), 0, stream,
-                            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
+                            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u), zero);
     }
     const unsigned long long blocks = (batch * dim + 255) / 256;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
     if (dtype == SACC_DTYPE_BF16)
         conv_silu_kernel<__nv_bfloat16, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u));
+            static_cast<const __nv_bfloat16*>(x), ldx, w, bias, batch, len, dim, static_cast<__nv_bfloat16*>(u), zero);
     else
         conv_silu_kernel<__half, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u));
+            static_cast<const __half*>(x), ldx, w, bias, batch, len, dim, static_cast<__half*>(u), zero);
     return cudaGetLastError();
 }
 

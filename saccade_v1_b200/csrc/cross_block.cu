@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(kTile* kRows) maps_from_rows_kernel(const floa
 template <typename T>
 __global__ void __launch_bounds__(256) cross_conv_kernel(const T* __restrict__ xz, const float* __restrict__ w,
                                                          const float* __restrict__ bias, unsigned batch, unsigned H, unsigned W,
-                                                         unsigned D, T* __restrict__ u, T* __restrict__ z) {
+                                                         unsigned D, T* __restrict__ u, T* __restrict__ z, ZeroSpan zero) {
     pdl_wait();
+    if (zero.words != 0 && blockIdx.x == 0) // the fused scan's hand-off flags (internal.h, ZeroSpan)
+        for (unsigned long long i = threadIdx.x; i < zero.words; i += blockDim.x) zero.ptr[i] = 0ull;
     constexpr int K = 4;
     const unsigned L = H * W, groups = D / 8;
     const unsigned long long gid = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
@@ -223,7 +225,7 @@ cudaError_t launch_maps_from_rows(const float* rows, const float* x, unsigned lo
 
 cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const float* bias, unsigned long long batch,
                               unsigned long long H, unsigned long long W, unsigned long long D, void* u, void* z,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, ZeroSpan zero) {
     const unsigned long long threads = 4 * batch * H * W * (D / 8), blocks = (threads + 255) / 256;
     if (D % 8 != 0 || H * W > 0xffffffffull || 4 * batch > 0xffffffffull || D > 0xffffffffull || blocks > 0x7fffffffull)
         return cudaErrorInvalidConfiguration;
@@ -233,9 +235,10 @@ cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const f
     if (dtype == SACC_DTYPE_BF16)
         return launch_pdl_k(cross_conv_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
                             static_cast<const __nv_bfloat16*>(xz), w, bias, b, h, wd, d, static_cast<__nv_bfloat16*>(u),
-                            static_cast<__nv_bfloat16*>(z));
+                            static_cast<__nv_bfloat16*>(z), zero);
     return launch_pdl_k(cross_conv_kernel<__half>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-                        static_cast<const __half*>(xz), w, bias, b, h, wd, d, static_cast<__half*>(u), static_cast<__half*>(z));
+                        static_cast<const __half*>(xz), w, bias, b, h, wd, d, static_cast<__half*>(u), static_cast<__half*>(z),
+                        zero);
 }
 
 cudaError_t launch_cross_mean(int dtype, const void* y, unsigned long long batch, unsigned long long H, unsigned long long W,

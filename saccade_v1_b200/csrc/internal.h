@@ -94,9 +94,17 @@ cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, uns
                              cudaStream_t stream);
 cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
                                  cudaStream_t stream);
+// Words that a kernel of the block pipeline zeroes as a side job (block 0,
+// after griddepcontrol.wait): the fused chunk-parallel scan's hand-off flags,
+// cleared by the conv kernel that precedes the scan in every block call, so
+// the scan needs no memset node of its own.
+struct ZeroSpan {
+    unsigned long long* ptr = nullptr;
+    unsigned long long words = 0;
+};
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
                              unsigned long long batch, unsigned long long len, unsigned long long dim, void* u,
-                             cudaStream_t stream);
+                             cudaStream_t stream, ZeroSpan zero = {});
 // dst = src (rows x cols) with its last row repeated `copies` times in total.
 cudaError_t launch_repeat_last_row(int dtype, const void* src, unsigned long long rows, unsigned long long copies,
                                    unsigned long long cols, void* dst, cudaStream_t stream);
@@ -124,7 +132,7 @@ cudaError_t launch_maps_from_rows(const float* rows, const float* x, unsigned lo
 // the position-major in_proj rows xz (batch, H W, 2 D) through the flips.
 cudaError_t launch_cross_conv(int dtype, const void* xz, const float* w, const float* bias, unsigned long long batch,
                               unsigned long long H, unsigned long long W, unsigned long long D, void* u, void* z,
-                              cudaStream_t stream);
+                              cudaStream_t stream, ZeroSpan zero = {});
 // mean (batch, H W, D) = the merge of y (4 batch, H W, D) at each position.
 cudaError_t launch_cross_mean(int dtype, const void* y, unsigned long long batch, unsigned long long H, unsigned long long W,
                               unsigned long long D, void* mean, cudaStream_t stream);
@@ -145,10 +153,17 @@ struct DtFusion {
 bool dt_fusable(const SaccScanExArgs& a, const DtFusion& f);
 // `scratch` (optional, 16-byte aligned): lets few-unit long-sequence calls run
 // the chunk-parallel scan as one fused launch; bulk_scan_scratch_bytes() says
-// how much this call would use (0: none).
+// how much this call would use (0: none).  The fused launch's hand-off flags
+// sit at the end of the scratch (bulk_scan_flags) and must be zero when it
+// starts: `flags_zeroed` says that an earlier kernel of the stream cleared
+// them, otherwise the launch clears them with a memset first.
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs = nullptr,
-                             void* scratch = nullptr, std::size_t scratch_bytes = 0, const DtFusion* dtf = nullptr);
+                             void* scratch = nullptr, std::size_t scratch_bytes = 0, const DtFusion* dtf = nullptr,
+                             bool flags_zeroed = false);
 std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf = nullptr);
+// The hand-off flags of a fused scan whose scratch is `scratch_bytes` long
+// (as bulk_scan_scratch_bytes gave it) at `scratch`.
+ZeroSpan bulk_scan_flags(void* scratch, std::size_t scratch_bytes);
 cudaError_t load_scan_bulk_kernels(std::string& report);
 // Fault word of the kernels with bounded waits (host-synchronous read; optionally cleared).
 cudaError_t read_bulk_fault(unsigned* out, bool clear);

@@ -103,6 +103,9 @@ SaccGemmArgs gemm_args(int dtype, std::uint64_t m, std::uint64_t n, std::uint64_
 // u (M, D); the gate z row t at z + t * zld; wx (a rank-1 C's repeated W_x),
 // dbc, delta (unused when fuse_dt), y (M, D) and the scan scratch from the
 // caller's workspace.
+// The scan scratch's hand-off flags were cleared by the conv kernel before
+// (ZeroSpan), so the first scan launch needs no memset; a later batch chunk
+// reuses the scratch and clears them itself.
 cudaError_t xproj_scan(const SaccMambaBlockArgs& a, const void* u, const void* z, std::uint64_t zld, void* wx, void* dbc,
                        void* delta, void* y, unsigned char* scan, std::size_t scan_bytes, bool fuse_dt, cudaStream_t stream) {
     const std::uint64_t M = a.batch * a.length, D = a.d_inner, N = a.d_state, R = a.dt_rank;
@@ -144,8 +147,8 @@ cudaError_t xproj_scan(const SaccMambaBlockArgs& a, const void* u, const void* z
         if (!bulk_eligible(s, &pitch)) return cudaErrorInvalidValue; // shapes are checked by the caller
         const DtFusion dtf{at(dbc, tok * W), W, a.w_dt, static_cast<int>(R)};
         if (fuse_dt && !dt_fusable(s, dtf)) return cudaErrorInvalidValue;
-        if ((err = launch_scan_bulk(s, stream, &pitch, scan_bytes ? scan : nullptr, scan_bytes, fuse_dt ? &dtf : nullptr)) !=
-            cudaSuccess)
+        if ((err = launch_scan_bulk(s, stream, &pitch, scan_bytes ? scan : nullptr, scan_bytes, fuse_dt ? &dtf : nullptr,
+                                    b0 == 0)) != cudaSuccess)
             return err;
     }
     return cudaSuccess;
@@ -230,7 +233,7 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
 
     // Causal depthwise conv1d (width d_conv) + SiLU on the x_in half.
     if ((err = launch_conv_silu(dt_, static_cast<int>(a.d_conv), xz, 2 * D, a.conv_w, a.conv_b, a.batch, a.length, D, u,
-                                stream)) != cudaSuccess)
+                                stream, bulk_scan_flags(l.scan_bytes ? ws + l.scan : nullptr, l.scan_bytes))) != cudaSuccess)
         return err;
 
     // x_proj, dt_proj and the scan; the gate z is the second half of each xz row.
@@ -275,7 +278,9 @@ cudaError_t launch_cross_block(const SaccCrossScanBlockArgs& c, void* workspace,
     if ((err = launch_gemm(g, stream)) != cudaSuccess) return err;
 
     // Every direction's conv + SiLU and gate, read through the flips.
-    if ((err = launch_cross_conv(dt_, xz, a.conv_w, a.conv_b, B, c.height, c.width, D, u, z, stream)) != cudaSuccess) return err;
+    if ((err = launch_cross_conv(dt_, xz, a.conv_w, a.conv_b, B, c.height, c.width, D, u, z, stream,
+                                 bulk_scan_flags(l.scan_bytes ? ws + l.scan : nullptr, l.scan_bytes))) != cudaSuccess)
+        return err;
     if ((err = xproj_scan(v, u, z, D, ws + l.wx, ws + l.dbc, ws + l.delta, ws + l.y, ws + l.scan, l.scan_bytes, l.fuse_dt,
                           stream)) != cudaSuccess)
         return err;

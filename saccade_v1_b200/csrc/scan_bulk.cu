@@ -1478,6 +1478,17 @@ bool dt_fusable(const SaccScanExArgs& a, const DtFusion& f) {
            f.ld >= static_cast<unsigned long long>(f.rank) && f.ld % 8 == 0;
 }
 
+ZeroSpan bulk_scan_flags(void* scratch, std::size_t scratch_bytes) {
+    // units x parts x (17 x 128 FP32 record + 8-byte flag), flags last.
+    const std::size_t per = (kN + 1) * kLanes * sizeof(float) + 8, items = scratch_bytes / per;
+    ZeroSpan z;
+    if (scratch != nullptr && items > 0) {
+        z.ptr = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(scratch) + items * (per - 8));
+        z.words = items;
+    }
+    return z;
+}
+
 std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf) {
     Pick k{};
     const int parts = fused_plan(a, dtf, k);
@@ -1485,7 +1496,7 @@ std::size_t bulk_scan_scratch_bytes(const SaccScanExArgs& a, const DtFusion* dtf
 }
 
 cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const RowStrides* rs, void* scratch,
-                             std::size_t scratch_bytes, const DtFusion* dtf) {
+                             std::size_t scratch_bytes, const DtFusion* dtf, bool flags_zeroed) {
     const RowStrides dense{0, 0, 0};
     if (!rs) rs = &dense;
     if (dtf && !dt_fusable(a, *dtf)) return cudaErrorInvalidValue;
@@ -1551,12 +1562,15 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
             p.epoch = next_epoch();
             // The flags stay in the scratch after the launch (nothing in it
             // overwrites them), and a CUDA graph replays this launch with the
-            // same epoch: clear them on the stream first, so that a part never
-            // sees a flag that an earlier launch or replay left (the epoch is
-            // never zero).
-            const std::size_t records = static_cast<std::size_t>(p.units) * fused * (kN + 1) * kLanes;
-            cudaError_t me = cudaMemsetAsync(p.scratch + records, 0, static_cast<std::size_t>(p.units) * fused * 8, stream);
-            if (me != cudaSuccess) return me;
+            // same epoch: they must be zero when it starts, so that a part
+            // never sees a flag that an earlier launch or replay left (the
+            // epoch is never zero).  The block pipeline's conv kernel clears
+            // them; other callers get a memset here.
+            if (!flags_zeroed) {
+                const std::size_t records = static_cast<std::size_t>(p.units) * fused * (kN + 1) * kLanes;
+                const cudaError_t me = cudaMemsetAsync(p.scratch + records, 0, static_cast<std::size_t>(p.units) * fused * 8, stream);
+                if (me != cudaSuccess) return me;
+            }
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(static_cast<unsigned>(p.units * fused));
             cfg.blockDim = dim3(static_cast<unsigned>(fk.threads));

@@ -966,6 +966,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        # NCCL's initialisation log (communicator size and rank per process) stays on, so a run's output shows
+        # that every rank joined one communicator of `world` ranks; NCCL reads these once, before torch loads it.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
     if args.impl == "reference":
         if rank == 0:
@@ -981,10 +986,6 @@ def main():
         return
     if world > 1:
         import datetime
-        # NCCL's initialisation log (communicator size and rank per process) stays on, so a run's output shows
-        # that every rank joined one communicator of `world` ranks.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))

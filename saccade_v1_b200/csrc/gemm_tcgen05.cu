@@ -452,10 +452,11 @@ size_t gemm_smem() {
 
 template <int BN>
 cudaError_t prepare_gemm() {
-    static const cudaError_t st = cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_kernel<BN>),
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       static_cast<int>(gemm_smem<BN>()));
-    return st;
+    static std::atomic<int> done[64];
+    return once_per_device(done, [] {
+        return cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_kernel<BN>), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(gemm_smem<BN>()));
+    });
 }
 
 // C as a 2D map {n, m} with a 32 x 32 box and the 64-byte swizzle (16-bit

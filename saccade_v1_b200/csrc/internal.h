@@ -4,6 +4,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -28,6 +29,22 @@ inline cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, std::size_t
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// Runs `set` (a kernel attribute setting, which CUDA applies to the current
+// device's copy of the kernel) once per device ordinal; `done` holds one flag
+// per ordinal for the call site.  Concurrent first calls may both run `set`,
+// which is idempotent.
+template <typename F>
+cudaError_t once_per_device(std::atomic<int> (&done)[64], F&& set) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return set();
+    if (done[dev].load(std::memory_order_acquire) == 1) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess) done[dev].store(1, std::memory_order_release);
+    return e;
 }
 
 // int32 element capacity of every tensor of the reference ABI

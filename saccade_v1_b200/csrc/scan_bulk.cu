@@ -1181,9 +1181,11 @@ template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode, int kR = 0>
 struct Variant {
     static const void* fn() { return reinterpret_cast<const void*>(bulk_kernel<T, kBDL, kHasZ, kFullC, kMode, kR>); }
     static cudaError_t prepare() {
-        static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                               static_cast<int>(smem_bytes<T, kBDL && kHasZ>()));
-        return status;
+        static std::atomic<int> done[64];
+        return once_per_device(done, [] {
+            return cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem_bytes<T, kBDL && kHasZ>()));
+        });
     }
     static size_t smem() { return smem_bytes<T, kBDL && kHasZ>(); }
 };
@@ -1280,9 +1282,11 @@ template <typename T, bool kHasZ, int kMode, int kR>
 struct QuadVariant {
     static const void* fn() { return reinterpret_cast<const void*>(quad_kernel<T, kHasZ, kMode, kR>); }
     static cudaError_t prepare() {
-        static const cudaError_t status = cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                               static_cast<int>(smem_bytes<T, false>()));
-        return status;
+        static std::atomic<int> done[64];
+        return once_per_device(done, [] {
+            return cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem_bytes<T, false>()));
+        });
     }
     static size_t smem() { return smem_bytes<T, false>(); }
 };

@@ -428,16 +428,18 @@ const void* pick_kernel(unsigned state, bool half, bool c_full) {
 }
 
 // CTAs of the FP32 scan kernel for (`state`, C width) that one SM holds at
-// once, queried once per kernel and process (every GPU of a process is taken
-// to be alike; the kernel loader fills the figures).  The FP16-activation
-// launch uses the FP32 kernel's figure too, so both split a lane into the same
-// chunks and the FP16 outputs stay the FP32 outputs rounded.
+// once, queried once per kernel and device (the kernel loader fills the
+// figures).  The FP16-activation launch uses the FP32 kernel's figure too, so
+// both split a lane into the same chunks and the FP16 outputs stay the FP32
+// outputs rounded.
 int resident_per_sm(unsigned state, bool c_full) {
-    static std::atomic<int> cache[12] = {};
+    static std::atomic<int> cache[64][12] = {};
     int idx = 0;
     while ((1u << idx) < state && idx < 5) ++idx;
     idx = 2 * idx + (c_full ? 1 : 0);
-    int v = cache[idx].load(std::memory_order_relaxed);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    int v = cache[dev][idx].load(std::memory_order_relaxed);
     if (v > 0) return v;
     const void* fn = pick_kernel(state, false, c_full);
     const size_t smem = static_cast<size_t>(kThreads) * state * sizeof(float2);
@@ -447,7 +449,7 @@ int resident_per_sm(unsigned state, bool c_full) {
         n = 1;
     else if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1)
         n = 1;
-    cache[idx].store(n, std::memory_order_relaxed);
+    cache[dev][idx].store(n, std::memory_order_relaxed);
     return n;
 }
 

@@ -452,14 +452,14 @@ bool state_map(CUtensorMap* map, float* state, unsigned long long channels, unsi
 
 template <typename T>
 cudaError_t prepare_pipe() {
-    static const cudaError_t status = [] {
+    static std::atomic<int> done[64];
+    return once_per_device(done, [] {
         const void* fn = reinterpret_cast<const void*>(step16_pipe_kernel<T>);
         const cudaError_t e =
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pipe_smem_bytes<T>()));
         if (e != cudaSuccess) return e;
         return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-    }();
-    return status;
+    });
 }
 
 // The pipelined path: 16-bit, N = 16, full-width C, at most 8 groups,

@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                                                            const __grid_constant__ CUtensorMap tm_c, GemmParams p) {
     constexpr int S = stages_for<BN>();
     extern __shared__ unsigned char smem_raw[];
-    auto& sm = *reinterpret_cast<GemmSmem<BN>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    auto& sm = shared_window<GemmSmem<BN>>(smem_raw);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int tiles = p.tiles_m * p.tiles_n;
 

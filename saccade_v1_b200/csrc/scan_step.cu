@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kPipeLanes) step16_pipe_kernel(const __grid_co
     pdl_wait();
     constexpr int N = 16;
     extern __shared__ unsigned char smem_raw[];
-    auto& sm = *reinterpret_cast<PipeSmem<T>*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t(1023));
+    auto& sm = shared_window<PipeSmem<T>>(smem_raw);
     const int tid = threadIdx.x;
     const unsigned c0 = blockIdx.y * kPipeLanes;
     const unsigned nch = static_cast<unsigned>(p.channels - c0 < kPipeLanes ? p.channels - c0 : kPipeLanes);

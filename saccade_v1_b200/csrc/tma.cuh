@@ -14,6 +14,19 @@ __device__ __forceinline__ std::uint32_t smem_addr(const void* p) {
     return static_cast<std::uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared-memory window rounded up to a 1024-byte boundary (the
+// 128-byte swizzle atoms of the TMA tiles), as an offset added to the shared
+// array itself.  Rounding the generic address as an integer instead hides the
+// address space from the compiler: every access then goes out as a generic
+// load or store, and on B200 a warp-uniform 16-byte generic load of shared
+// memory costs 4 shared-pipe wavefronts where LDS.128 costs 2.  The launch
+// reserves 1024 bytes of slack for the offset.
+template <typename S>
+__device__ __forceinline__ S& shared_window(unsigned char* raw) {
+    const std::uint32_t off = (1024u - (smem_addr(raw) & 1023u)) & 1023u;
+    return *reinterpret_cast<S*>(raw + off);
+}
+
 __device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }

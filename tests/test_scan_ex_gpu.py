@@ -322,8 +322,8 @@ def test_varlen_entries_are_clamped(dt):
 @pytest.mark.parametrize("layout", ["BDL", "BLD"])
 def test_bulk_split_launch_bitwise_equals_unsplit(layout):
     """A batch large enough that the units exceed one wave of CTAs is split
-    along L (each unit's parts hand their state over through the output, under
-    a cooperative launch); the same rows run as slices small enough for one
+    along L (each unit's parts hand their state over through the output,
+    part-major items on a multi-wave grid); the same rows run as slices small enough for one
     wave are not split.  The hand-off moves exact FP32 states, so outputs and
     final states agree bit for bit.  Gate, h0 and h_final included."""
     B, L, D, N = 64, 1024, 1536, 16  # 768 units of 128 channels: more than one wave in either layout
@@ -361,7 +361,7 @@ def test_bulk_split_launch_bitwise_equals_unsplit(layout):
 
 
 def test_bulk_split_launch_in_cuda_graph():
-    """The split launch (cooperative, one wave) captured in a CUDA graph and
+    """The split launch (parts handing states over through the outputs) captured in a CUDA graph and
     replayed twice gives the eager launch's bits."""
     B, L, D, N = 64, 512, 1536, 16
     s = torch.cuda.Stream()
@@ -388,6 +388,48 @@ def test_bulk_split_launch_in_cuda_graph():
             graph.replay()
         s.synchronize()
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    assert ctypes_fault() == 0
+
+
+@pytest.mark.parametrize("layout,B,L", [("BDL", 62, 1000), ("BLD", 62, 1000), ("BDL", 100, 520), ("BLD", 100, 520)])
+def test_bulk_split_parts_bitwise_equals_unsplit(layout, B, L):
+    """Units just over one wave of CTAs (62 rows x 12 tiles = 744) and about
+    two waves (1200), with L a multiple of 8 but not of 32 (a ragged last
+    chunk, so the last part is shorter): the launch splits each unit into
+    parts handed over through the outputs (part-major items on a multi-wave
+    grid); the same rows as one-wave slices are not split.  Exact FP32
+    hand-offs: outputs and final states agree bit for bit, h0 and a gate
+    included."""
+    D, N = 1536, 16
+    s = torch.cuda.Stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(67 + B + L)
+    bf = torch.bfloat16
+    with torch.cuda.stream(s):
+        shp = (B, D, L) if layout == "BDL" else (B, L, D)
+        bshp = (B, 1, N, L) if layout == "BDL" else (B, L, 1, N)
+        u, dl, z = (torch.randn(shp, device="cuda", generator=g).to(bf) for _ in range(3))
+        bm, cm = (torch.randn(bshp, device="cuda", generator=g).to(bf) for _ in range(2))
+        A = -(torch.rand(D, N, device="cuda", generator=g) * 2 + 0.01)
+        Dv = torch.randn(D, device="cuda", generator=g)
+        bias = torch.full((D,), -4.0, device="cuda")
+        h0 = torch.randn(B, D, N, device="cuda", generator=g) * 0.5
+        hf = torch.empty(B, D, N, device="cuda")
+        y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
+        ys, hs = [], []
+        # Slices of 25..37 rows (300..444 units): one wave of the one-thread-per-lane kernel in every variant, not
+        # split, and above the four-thread kernel's 296 units.
+        rows = 31 if B == 62 else 25
+        for b0 in range(0, B, rows):
+            sl = slice(b0, b0 + rows)
+            hfi = torch.empty(rows, D, N, device="cuda")
+            ys.append(sb.selective_scan_ex(u[sl].contiguous(), dl[sl].contiguous(), A, bm[sl].contiguous(), cm[sl].contiguous(),
+                                           D=Dv, z=z[sl].contiguous(), delta_bias=bias, h0=h0[sl].contiguous(), h_final=hfi,
+                                           layout=layout, stream=s))
+            hs.append(hfi)
+    s.synchronize()
+    assert torch.equal(y.view(torch.int16), torch.cat(ys).view(torch.int16))
+    assert torch.equal(hf.view(torch.int32), torch.cat(hs).view(torch.int32))
     assert ctypes_fault() == 0
 
 

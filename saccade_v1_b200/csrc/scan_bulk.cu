@@ -64,6 +64,9 @@ constexpr int bulk_min_blocks(int mode, int rank, bool ztile) {
 }
 constexpr int kMaxFusedParts = 32;
 
+// The gate staged as a TMA tile (see Smem) unless the scan forms delta itself.
+__host__ __device__ constexpr bool gate_tile(bool has_z, int rank) { return has_z && rank == 0; }
+
 // One item of work: 128 channels of one row (or packed sequence) over the
 // chunk range of one part, with the tensor-map coordinates of the unit.
 struct Item {
@@ -79,9 +82,15 @@ struct Cursor {
     int chunk, more;
 };
 
-// kZTile: the gate z staged by TMA ((B, D, L) with a gate); in (B, L, D) a
-// warp's z of one token is 64 contiguous bytes, read straight from global
-// memory.  The one-thread-per-lane kernel writes a chunk's outputs over its
+// kZTile: the gate z staged by TMA like u and delta, in either layout.  Read
+// from global memory instead, (B, L, D) lane by lane, the gated scan was 36 %
+// slower than ungated (the loads' latency and 64-bit address arithmetic on
+// the FMA pipe; prefetched one token block ahead, slower still), against
+// 1.4 % with the tile (three CTAs per SM: 23 % at config-4 size, where a
+// multi-wave grid would have held five).  The scan that forms delta itself
+// (kR > 0: the block pipeline's short sequences, where four CTAs per SM keep
+// config 1's 512 units in one wave) reads the gate from global memory.
+// The one-thread-per-lane kernel writes a chunk's outputs over its
 // u tile (each thread reads its eight u values of a token block before it
 // writes their eight outputs to the same places, and the y tile has the u
 // tile's layout), so the stage is free again once the y store has read it.
@@ -213,13 +222,15 @@ __device__ __forceinline__ void store_block_bdl(T* y, int tid, int q, const floa
                                                     pack2<T>(out[4], out[5]), pack2<T>(out[6], out[7]));
 }
 
-// (B, L, D): token-major [32][128] tile; lane `tid` is column tid.
-template <typename T, bool kHasZ>
-// The gate of the first `count` tokens from global memory (token rows zrow0 + ...).
-__device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T* zg, unsigned long long zrow0,
+// (B, L, D): token-major [32][128] tiles; lane `tid` is column tid.  With
+// kZTile the gate comes from its own tile (tokens past a tensor's end read as
+// zero), else the first `count` tokens' gate from global memory (token rows
+// zrow0 + ..., pitch zld).
+template <typename T, bool kHasZ, bool kZTile>
+__device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T* z, const T* zg, unsigned long long zrow0,
                                                unsigned long long zld, unsigned long long d, int tid, int q, int count,
                                                Block8& blk) {
-    if constexpr (kHasZ) {
+    if constexpr (kHasZ && !kZTile) {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             blk.z[j] = j < count ? to_f32(zg[(zrow0 + static_cast<unsigned long long>(q * 8 + j)) * zld + d]) : 0.0f;
@@ -229,6 +240,7 @@ __device__ __forceinline__ void load_block_bld(const T* u, const T* dl, const T*
         const int at = (q * 8 + j) * kLanes + tid;
         blk.u[j] = to_f32(u[at]);
         blk.x[j] = to_f32(dl[at]);
+        if constexpr (kHasZ && kZTile) blk.z[j] = to_f32(z[at]);
     }
 }
 
@@ -279,30 +291,35 @@ __device__ __forceinline__ void store_block_bld(T* y, int tid, int q, const floa
 // x = token, y = row (b * D + d).  (B, L, D): 3D maps (channel, token, batch),
 // so that a chunk past the end of a sequence reads zeros instead of the next
 // sequence; a packed varlen sequence reads whatever follows it, unused.
-template <typename T, bool kBDL, bool kHasZ, int kR = 0>
-__device__ __forceinline__ void issue_chunk(Smem<T, kBDL && kHasZ>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
+// kZTile: the gate's tile is staged with the others (the one-thread-per-lane
+// kernel); the four-thread kernel reads the gate from global memory.
+template <typename T, bool kBDL, bool kHasZ, int kR = 0, bool kZTile = false>
+__device__ __forceinline__ void issue_chunk(Smem<T, kZTile>& sm, int s, int t0, int row0, int brow0, int crow0, int bb,
                                             std::uint32_t c_bytes, const CUtensorMap* tu, const CUtensorMap* td,
                                             const CUtensorMap* tz, const CUtensorMap* tb, const CUtensorMap* tc) {
+    static_assert(!kZTile || kHasZ, "a gate tile needs a gate");
     constexpr std::uint32_t tile = kLanes * kT * sizeof(T), btile = kN * kT * sizeof(T);
     if constexpr (kR > 0) {
         // (B, L, D), delta formed in the scan: the chunk's dt rows instead of a delta tile.
-        mbar_arrive_expect_tx(&sm.full[s], tile + kR * kT * sizeof(T) + btile + c_bytes);
+        mbar_arrive_expect_tx(&sm.full[s], tile * (kZTile ? 2u : 1u) + kR * kT * sizeof(T) + btile + c_bytes);
         tma_load_3d(sm.u[s], tu, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.dl[s], td, &sm.full[s], 0, t0, bb);
+        if constexpr (kZTile) tma_load_3d(sm.z[s], tz, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
         tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
         return;
     }
-    mbar_arrive_expect_tx(&sm.full[s], tile * (kBDL && kHasZ ? 3u : 2u) + btile + c_bytes);
+    mbar_arrive_expect_tx(&sm.full[s], tile * (kZTile ? 3u : 2u) + btile + c_bytes);
     if (kBDL) {
         tma_load_2d(sm.u[s], tu, &sm.full[s], t0, row0);
         tma_load_2d(sm.dl[s], td, &sm.full[s], t0, row0);
-        if constexpr (kHasZ) tma_load_2d(sm.z[s], tz, &sm.full[s], t0, row0);
+        if constexpr (kZTile) tma_load_2d(sm.z[s], tz, &sm.full[s], t0, row0);
         tma_load_2d(sm.braw[s], tb, &sm.full[s], t0, brow0);
         tma_load_2d(sm.craw[s], tc, &sm.full[s], t0, crow0);
     } else {
         tma_load_3d(sm.u[s], tu, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.dl[s], td, &sm.full[s], row0, t0, bb);
+        if constexpr (kZTile) tma_load_3d(sm.z[s], tz, &sm.full[s], row0, t0, bb);
         tma_load_3d(sm.braw[s], tb, &sm.full[s], brow0, t0, bb);
         tma_load_3d(sm.craw[s], tc, &sm.full[s], crow0, t0, bb);
     }
@@ -638,7 +655,7 @@ __device__ __forceinline__ bool fused_prefix(const BulkParams& p, const Item& w,
 // chunk loads in flight along the CTA's whole list, so the next item's first
 // chunks arrive while the current item computes.
 template <typename T, bool kBDL, bool kHasZ, bool kFullC, int kMode, int kR>
-__global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, kBDL && kHasZ)) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
+__global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, gate_tile(kHasZ, kR))) bulk_kernel(const __grid_constant__ CUtensorMap tm_u,
                                                                   const __grid_constant__ CUtensorMap tm_d,
                                                                   const __grid_constant__ CUtensorMap tm_z,
                                                                   const __grid_constant__ CUtensorMap tm_b,
@@ -646,7 +663,8 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, kBDL && kHa
                                                                   const __grid_constant__ CUtensorMap tm_y, BulkParams p) {
     pdl_wait();
     extern __shared__ unsigned char smem_raw[];
-    auto& sm = shared_window<Smem<T, kBDL && kHasZ>>(smem_raw);
+    constexpr bool kZTile = gate_tile(kHasZ, kR);
+    auto& sm = shared_window<Smem<T, kZTile>>(smem_raw);
     const int tid = threadIdx.x;
     const unsigned long long D = p.channels;
     const int cw = kFullC ? kN : 1;
@@ -674,7 +692,7 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, kBDL && kHa
             cursor_next<kBDL, kFullC>(c, p); // to the first chunk of the first item with chunks
         }
         for (int s = 0; s < kStages && c.more; ++s) {
-            issue_chunk<T, kBDL, kHasZ, kR>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
+            issue_chunk<T, kBDL, kHasZ, kR, kZTile>(sm, s, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0, c.w.crow0,
                                             c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
             cursor_next<kBDL, kFullC>(c, p);
         }
@@ -786,10 +804,10 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, kBDL && kHa
                         load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
                     else
                     {
-                        load_block_bld<T, kHasZ>(sm.u[s], sm.dl[s], static_cast<const T*>(p.zg),
-                                                 static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
-                                                     static_cast<unsigned long long>(chunk) * kT,
-                                                 p.zld, d, tid, q, valid - q * 8, blk);
+                        load_block_bld<T, kHasZ, kZTile>(sm.u[s], sm.dl[s], sm.z[kZTile ? s : 0], static_cast<const T*>(p.zg),
+                                                         static_cast<unsigned long long>(w.bb) * p.length + w.tok0 +
+                                                             static_cast<unsigned long long>(chunk) * kT,
+                                                         p.zld, d, tid, q, valid - q * 8, blk);
                         if constexpr (kR > 0) delta_from_dt<T, kR>(sm.dl[s], wrow, q, blk);
                     }
                     float out[8];
@@ -807,7 +825,7 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, kBDL && kHa
                         // chunk, the store has had time to drain.
                         bulk_wait_read<0>();
                         Cursor& c = sm.next;
-                        issue_chunk<T, kBDL, kHasZ, kR>(sm, pend, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
+                        issue_chunk<T, kBDL, kHasZ, kR, kZTile>(sm, pend, static_cast<int>(c.w.tok0) + c.chunk * kT, c.w.row0, c.w.brow0,
                                                         c.w.crow0, c.w.bb, c_bytes, &tm_u, &tm_d, &tm_z, &tm_b, &tm_c);
                         cursor_next<kBDL, kFullC>(c, p);
                         pend = -1;
@@ -1215,10 +1233,10 @@ struct Variant {
         static std::atomic<int> done[64];
         return once_per_device(done, [] {
             return cudaFuncSetAttribute(fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem_bytes<Smem<T, kBDL && kHasZ>>()));
+                                        static_cast<int>(smem_bytes<Smem<T, gate_tile(kHasZ, kR)>>()));
         });
     }
-    static size_t smem() { return smem_bytes<Smem<T, kBDL && kHasZ>>(); }
+    static size_t smem() { return smem_bytes<Smem<T, gate_tile(kHasZ, kR)>>(); }
 };
 
 // Chunk-parallel combine, one thread per (batch row, channel): the local

@@ -14,10 +14,11 @@
 //               four times per stage from shared-memory descriptors, then
 //               tcgen05.commit to free the stage and, per tile, to signal
 //               the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, row
-//               scale, bias, residual, conversion; 16-bit results go through a
-//               double-buffered, swizzled 32 x 32 shared tile per warp and a
-//               TMA store (coalesced full lines), FP32 results straight to
+//   warps 2..   epilogue (eight warps, four at BN = 64: two per TMEM lane
+//               quarter, each half the columns): tcgen05.ld 32 lanes x 32 columns at a time, row
+//               scale, bias, residual, conversion; 16-bit results go through
+//               swizzled 32 x 32 shared tiles (sixteen per CTA, all but one per
+//               warp in flight) and TMA stores (coalesced full lines), FP32 results straight to
 //               global memory; then release the accumulator buffer.
 // No multicast, no clusters.  Every mbarrier wait has an iteration limit and
 // sets the library fault word when it runs out.
@@ -42,7 +43,24 @@ __device__ unsigned int g_gemm_fault; // set when a bounded wait ran out; read b
 namespace {
 
 constexpr int kBM = 128, kBK = 64, kStages = 4;
-constexpr int kThreads = 192;
+
+// Epilogue warps E: four (one per TMEM lane quarter) or eight (two per
+// quarter, each half of a tile's columns, so that each scheduler has two to
+// interleave).  Eight pay off when a tile's MMAs are short: with one k-block
+// (K = 64: config 4's dt_proj, 8.6 GB out) four warps stored at 2.0 TB/s, each
+// warp's load - convert - stage - fence - store chain exposed, eight at 4.5
+// TB/s; at K = 1024-2048 eight were up to 5 % slower (the MMA warp shares its
+// scheduler with two of them).  BN = 64 keeps four: two CTAs share an SM.
+template <int E>
+__host__ __device__ constexpr int gemm_threads() {
+    return 64 + 32 * E;
+}
+// 32 x 32 staging tiles per epilogue warp (sixteen in all): a warp keeps all
+// but one of its TMA stores reading shared memory while it fills the next.
+template <int E>
+__host__ __device__ constexpr int stage_bufs() {
+    return 16 / E;
+}
 
 // Ring depth: 4 stages, 3 at BN = 64 so that two CTAs fit on an SM.
 template <int BN>
@@ -50,7 +68,7 @@ __host__ __device__ constexpr int stages_for() {
     return BN == 64 ? 3 : kStages;
 }
 
-template <int BN>
+template <int BN, int E>
 struct GemmSmem {
     alignas(1024) std::uint16_t a[stages_for<BN>()][kBM * kBK];
     alignas(1024) std::uint16_t b[stages_for<BN>()][BN * kBK];
@@ -58,8 +76,9 @@ struct GemmSmem {
     alignas(8) std::uint64_t empty[stages_for<BN>()];
     alignas(8) std::uint64_t acc_full[2];
     alignas(8) std::uint64_t acc_empty[2];
-    // 16-bit epilogue staging: per epilogue warp two 32 x 32 tiles (64-byte swizzle) for TMA stores.
-    alignas(1024) std::uint16_t stage[4][2][32 * 32];
+    // 16-bit epilogue staging: per epilogue warp stage_bufs 32 x 32 tiles (64-byte swizzle) for TMA stores
+    // (at BN = 256 the whole struct is 231,424 bytes: with the 1 KB alignment slack exactly the opt-in limit).
+    alignas(1024) std::uint16_t stage[E][stage_bufs<E>()][32 * 32];
     std::uint32_t tmem_base;
 };
 
@@ -259,13 +278,13 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, unsigned long l
 
 // Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...;
 // two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next.
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+template <int BN, int E>
+__global__ void __launch_bounds__(gemm_threads<E>(), 1) gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                                                            const __grid_constant__ CUtensorMap tm_b,
                                                            const __grid_constant__ CUtensorMap tm_c, GemmParams p) {
     constexpr int S = stages_for<BN>();
     extern __shared__ unsigned char smem_raw[];
-    auto& sm = shared_window<GemmSmem<BN>>(smem_raw);
+    auto& sm = shared_window<GemmSmem<BN, E>>(smem_raw);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int tiles = p.tiles_m * p.tiles_n;
 
@@ -278,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sm.acc_full[b], 1);
-            mbar_init(&sm.acc_empty[b], 4); // one arrival per epilogue warp
+            mbar_init(&sm.acc_empty[b], E); // one arrival per epilogue warp
         }
         fence_barrier_init();
     }
@@ -345,7 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else {
         // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
-        const int quarter = warp % 4;
+        // Warp 2 + e takes TMEM lanes of its quarter (a hardware rule: warp w
+        // reaches lanes 32 (w % 4) .. + 31) and column half e / 4 of each tile.
+        constexpr int kChunks = BN / 32 / (E / 4); // 32-column chunks per warp and tile
+        const int quarter = warp % 4, e = warp - 2, c_first = (e / 4) * kChunks;
         unsigned it = 0, st = 0; // st: staging tiles used by this warp
         if (p.tma_store && lane == 0) prefetch_tensor_map(&tm_c);
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
@@ -358,25 +380,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
             const int r0 = m0 + quarter * 32; // first row of this warp
             const unsigned long long row = static_cast<unsigned long long>(r0 + lane);
-            const std::uint32_t tbase = tmem + ab * BN + (static_cast<std::uint32_t>(quarter * 32) << 16);
+            const std::uint32_t tbase =
+                tmem + ab * BN + static_cast<std::uint32_t>(c_first * 32) + (static_cast<std::uint32_t>(quarter * 32) << 16);
             // Chunk c + 1 loads from TMEM while chunk c is finished and stored.
             std::uint32_t ra[32], rb[32];
             tmem_ld32_issue(tbase, ra);
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = 0; c < kChunks; ++c) {
                 float v[32];
                 if (c % 2 == 0) {
                     tmem_ld32_wait(ra);
-                    if (c + 1 < BN / 32) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), rb);
+                    if (c + 1 < kChunks) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), rb);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
                 } else {
                     tmem_ld32_wait(rb);
-                    if (c + 1 < BN / 32) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), ra);
+                    if (c + 1 < kChunks) tmem_ld32_issue(tbase + static_cast<std::uint32_t>((c + 1) * 32), ra);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rb[i]);
                 }
-                const unsigned long long col0 = static_cast<unsigned long long>(n0 + c * 32);
+                const unsigned long long col0 = static_cast<unsigned long long>(n0 + (c_first + c) * 32);
                 if (!p.tma_store) {
                     if (row < p.m && col0 < p.n) store_chunk(p, row, col0, v);
                     continue;
@@ -385,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 // Coalesced path: the warp's 32 x 32 block goes through a swizzled
                 // shared tile and one TMA store (rows / columns past C are clipped).
                 if (row < p.m) apply_chunk(p, row, col0, v);
-                std::uint16_t* buf = sm.stage[quarter][st & 1u];
-                if (lane == 0) bulk_wait_read<1>(); // the store that last used this buffer has read it
+                std::uint16_t* buf = sm.stage[e][st % stage_bufs<E>()];
+                if (lane == 0) bulk_wait_read<stage_bufs<E>() - 1>(); // the store that last used this buffer has read it
                 __syncwarp();
                 std::uint32_t w[16];
                 pack16(v, p.out_dtype, w);
@@ -445,17 +468,17 @@ bool kmajor_map(CUtensorMap* map, int dtype, const void* base, unsigned long lon
            CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int E>
 size_t gemm_smem() {
-    return sizeof(GemmSmem<BN>) + 1024;
+    return sizeof(GemmSmem<BN, E>) + 1024;
 }
 
-template <int BN>
+template <int BN, int E>
 cudaError_t prepare_gemm() {
     static std::atomic<int> done[64];
     return once_per_device(done, [] {
-        return cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_kernel<BN>), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(gemm_smem<BN>()));
+        return cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_kernel<BN, E>), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(gemm_smem<BN, E>()));
     });
 }
 
@@ -473,10 +496,10 @@ bool c_map(CUtensorMap* map, int dtype, void* base, unsigned long long n, unsign
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int E>
 cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p, int sm_count,
                       cudaStream_t stream) {
-    const cudaError_t e = prepare_gemm<BN>();
+    const cudaError_t e = prepare_gemm<BN, E>();
     if (e != cudaSuccess) return e;
     p.tiles_m = static_cast<int>((p.m + kBM - 1) / kBM);
     p.tiles_n = static_cast<int>((p.n + BN - 1) / BN);
@@ -485,7 +508,7 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
     const long long slots = static_cast<long long>(sm_count) * (BN == 64 ? 2 : 1);
     const unsigned grid = static_cast<unsigned>(tiles < slots ? tiles : slots);
     void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), const_cast<CUtensorMap*>(&tc), &p};
-    return launch_pdl(reinterpret_cast<const void*>(gemm_kernel<BN>), dim3(grid), dim3(kThreads), gemm_smem<BN>(), stream,
+    return launch_pdl(reinterpret_cast<const void*>(gemm_kernel<BN, E>), dim3(grid), dim3(gemm_threads<E>()), gemm_smem<BN, E>(), stream,
                       args);
 }
 
@@ -512,24 +535,29 @@ cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream) {
     p.res_vec = a.residual && (reinterpret_cast<std::uintptr_t>(a.residual) % 16 == 0) && ((a.ldr * eo) % 16 == 0);
     CUtensorMap tc{};
     p.tma_store = a.out_dtype != SACC_DTYPE_F32 && p.vec_store && c_map(&tc, a.out_dtype, a.c, a.n, a.m, a.ldc);
-    if (bn == 64) return launch_bn<64>(ta, tb, tc, p, sms, stream);
-    if (bn == 128) return launch_bn<128>(ta, tb, tc, p, sms, stream);
-    return launch_bn<256>(ta, tb, tc, p, sms, stream);
+    const bool short_k = p.kblocks <= 8; // eight epilogue warps when a tile's MMAs are short (K <= 512)
+    if (bn == 64) return launch_bn<64, 4>(ta, tb, tc, p, sms, stream);
+    if (bn == 128) return short_k ? launch_bn<128, 8>(ta, tb, tc, p, sms, stream) : launch_bn<128, 4>(ta, tb, tc, p, sms, stream);
+    return short_k ? launch_bn<256, 8>(ta, tb, tc, p, sms, stream) : launch_bn<256, 4>(ta, tb, tc, p, sms, stream);
 }
 
 cudaError_t load_gemm_kernels(std::string& report) {
-    const std::pair<const char*, const void*> ks[] = {{"gemm_tcgen05_bn64", reinterpret_cast<const void*>(gemm_kernel<64>)},
-                                                      {"gemm_tcgen05_bn128", reinterpret_cast<const void*>(gemm_kernel<128>)},
-                                                      {"gemm_tcgen05_bn256", reinterpret_cast<const void*>(gemm_kernel<256>)}};
+    const std::pair<const char*, const void*> ks[] = {{"gemm_tcgen05_bn64", reinterpret_cast<const void*>(gemm_kernel<64, 4>)},
+                                                      {"gemm_tcgen05_bn128", reinterpret_cast<const void*>(gemm_kernel<128, 4>)},
+                                                      {"gemm_tcgen05_bn128_e8", reinterpret_cast<const void*>(gemm_kernel<128, 8>)},
+                                                      {"gemm_tcgen05_bn256", reinterpret_cast<const void*>(gemm_kernel<256, 4>)},
+                                                      {"gemm_tcgen05_bn256_e8", reinterpret_cast<const void*>(gemm_kernel<256, 8>)}};
     for (const auto& k : ks) {
         cudaFuncAttributes attr{};
         const cudaError_t e = cudaFuncGetAttributes(&attr, k.second);
         if (e != cudaSuccess) return e;
         report += std::string("kernel=") + k.first + " registers=" + std::to_string(attr.numRegs) + "\n";
     }
-    cudaError_t e = prepare_gemm<64>();
-    if (e == cudaSuccess) e = prepare_gemm<128>();
-    if (e == cudaSuccess) e = prepare_gemm<256>();
+    cudaError_t e = prepare_gemm<64, 4>();
+    if (e == cudaSuccess) e = prepare_gemm<128, 4>();
+    if (e == cudaSuccess) e = prepare_gemm<128, 8>();
+    if (e == cudaSuccess) e = prepare_gemm<256, 4>();
+    if (e == cudaSuccess) e = prepare_gemm<256, 8>();
     return e;
 }
 

@@ -323,9 +323,10 @@ def test_varlen_entries_are_clamped(dt):
 def test_bulk_split_launch_bitwise_equals_unsplit(layout):
     """A batch large enough that the units exceed one wave of CTAs is split
     along L (each unit's parts hand their state over through the output,
-    part-major items on a multi-wave grid); the same rows run as slices small enough for one
-    wave are not split.  The hand-off moves exact FP32 states, so outputs and
-    final states agree bit for bit.  Gate, h0 and h_final included."""
+    part-major items on a multi-wave grid); the same rows run as 32-row slices
+    are split into a different number of parts, or not at all.  The hand-off
+    moves exact FP32 states, so outputs and final states agree bit for bit.
+    Gate, h0 and h_final included."""
     B, L, D, N = 64, 1024, 1536, 16  # 768 units of 128 channels: more than one wave in either layout
     s = torch.cuda.Stream()
     g = torch.Generator(device="cuda")
@@ -346,7 +347,7 @@ def test_bulk_split_launch_bitwise_equals_unsplit(layout):
         hf = torch.empty(B, D, N, device="cuda")
         y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
         ys, hs = [], []
-        rows = 32  # 384 units: one wave of the one-thread-per-lane kernel, not split (the four-thread kernel takes <= 296)
+        rows = 32  # 384 units: the one-thread-per-lane kernel (the four-thread kernel takes <= 296 units)
         for b0 in range(0, B, rows):
             sl = slice(b0, b0 + rows)
             hfi = torch.empty(rows, D, N, device="cuda")
@@ -397,9 +398,9 @@ def test_bulk_split_parts_bitwise_equals_unsplit(layout, B, L):
     two waves (1200), with L a multiple of 8 but not of 32 (a ragged last
     chunk, so the last part is shorter): the launch splits each unit into
     parts handed over through the outputs (part-major items on a multi-wave
-    grid); the same rows as one-wave slices are not split.  Exact FP32
-    hand-offs: outputs and final states agree bit for bit, h0 and a gate
-    included."""
+    grid); the same rows as slices of 25-31 rows split into other part counts
+    or not at all.  Exact FP32 hand-offs: outputs and final states agree bit
+    for bit, h0 and a gate included."""
     D, N = 1536, 16
     s = torch.cuda.Stream()
     g = torch.Generator(device="cuda")
@@ -417,8 +418,8 @@ def test_bulk_split_parts_bitwise_equals_unsplit(layout, B, L):
         hf = torch.empty(B, D, N, device="cuda")
         y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
         ys, hs = [], []
-        # Slices of 25..37 rows (300..444 units): one wave of the one-thread-per-lane kernel in every variant, not
-        # split, and above the four-thread kernel's 296 units.
+        # Slices of 25..31 rows (300..372 units): the one-thread-per-lane kernel (above the four-thread kernel's
+        # 296 units), split differently from the whole batch or not at all.
         rows = 31 if B == 62 else 25
         for b0 in range(0, B, rows):
             sl = slice(b0, b0 + rows)

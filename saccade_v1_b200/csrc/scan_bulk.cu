@@ -66,10 +66,10 @@ constexpr int kMaxFusedParts = 32;
 
 // How the gate reaches shared memory (see Smem): 0 not at all (no gate, or
 // the scan forms delta itself and reads the gate from global memory), 1 a
-// tile per stage, 2 one chunk's tile as two 16-token halves ((B, L, D) one-item
-// walks: four CTAs per SM instead of three).
+// tile per stage (the fused chunk-parallel walk), 2 one chunk's tile as two
+// 16-token halves (one-item walks: four CTAs per SM instead of three).
 __host__ __device__ constexpr int gate_mode(bool has_z, int rank, bool bdl, int mode) {
-    return !has_z || rank != 0 ? 0 : (!bdl && mode != 2 ? 2 : 1);
+    return !has_z || rank != 0 ? 0 : (mode != 2 ? 2 : 1);
 }
 
 // One item of work: 128 channels of one row (or packed sequence) over the
@@ -198,7 +198,9 @@ struct Block8 {
 
 // (B, D, L): row `tid` of a 64-byte-swizzled [128][32] tile; chunk q of row r
 // sits at q ^ ((r >> 1) & 3) (TMA 64-byte swizzle: address bits [4:5] ^= [7:8]).
-template <typename T, bool kHasZ>
+// kZHalves: the gate from the two-half tile, each half [128 rows][16 tokens]
+// without swizzle (one 16-byte read per token block).
+template <typename T, bool kHasZ, bool kZHalves = false>
 __device__ __forceinline__ void load_block_bdl(const T* u, const T* dl, const T* z, int tid, int q, Block8& blk) {
     const int off = tid * kT + ((q ^ ((tid >> 1) & 3)) << 3);
     const uint4 uq = *reinterpret_cast<const uint4*>(u + off);
@@ -211,7 +213,8 @@ __device__ __forceinline__ void load_block_bdl(const T* u, const T* dl, const T*
         blk.x[2 * j] = b.x; blk.x[2 * j + 1] = b.y;
     }
     if constexpr (kHasZ) {
-        const uint4 zq = *reinterpret_cast<const uint4*>(z + off);
+        const uint4 zq = *reinterpret_cast<const uint4*>(
+            kZHalves ? z + (q >> 1) * (kLanes * kT / 2) + tid * (kT / 2) + ((q & 1) << 3) : z + off);
         const std::uint32_t zw[4] = {zq.x, zq.y, zq.z, zq.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -340,11 +343,13 @@ __device__ __forceinline__ void issue_chunk(Smem<T, kZ>& sm, int s, int t0, int 
 }
 
 // kZ == 2: half h (tokens 16 h .. 16 h + 15) of the gate of the chunk at
-// token t0 into its half of the single gate tile.
-template <typename T>
+// token t0 into its half of the single gate tile ((B, D, L): a 16 x 128 box of
+// the unswizzled half-box map).
+template <typename T, bool kBDL>
 __device__ __forceinline__ void issue_gate_half(Smem<T, 2>& sm, int h, int t0, int row0, int bb, const CUtensorMap* tz) {
     mbar_arrive_expect_tx(&sm.zfull[h], kLanes * (kT / 2) * sizeof(T));
-    tma_load_3d(sm.z[h], tz, &sm.zfull[h], row0, t0 + h * (kT / 2), bb);
+    if constexpr (kBDL) tma_load_2d(sm.z[h], tz, &sm.zfull[h], t0 + h * (kT / 2), row0);
+    else tma_load_3d(sm.z[h], tz, &sm.zfull[h], row0, t0 + h * (kT / 2), bb);
 }
 
 // Eight tokens of one lane through the recurrence; with kGuard only the first
@@ -839,12 +844,12 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, gate_mode(k
                                 break;
                             }
                             if (tid == 0 && chunk + 1 < w.c1)
-                                issue_gate_half<T>(sm, 0, static_cast<int>(w.tok0) + (chunk + 1) * kT, w.row0, w.bb, &tm_z);
+                                issue_gate_half<T, kBDL>(sm, 0, static_cast<int>(w.tok0) + (chunk + 1) * kT, w.row0, w.bb, &tm_z);
                         }
                     }
                     Block8 blk;
                     if constexpr (kBDL)
-                        load_block_bdl<T, kHasZ>(sm.u[s], sm.dl[s], sm.z[kHasZ ? s : 0], tid, q, blk);
+                        load_block_bdl<T, kHasZ, kZ == 2>(sm.u[s], sm.dl[s], kZ == 2 ? &sm.z[0][0] : sm.z[kHasZ ? s : 0], tid, q, blk);
                     else
                     {
                         load_block_bld<T, kHasZ, kZ != 0>(sm.u[s], sm.dl[s], kZ == 2 ? &sm.z[0][0] : sm.z[kZTile ? s : 0],
@@ -908,8 +913,8 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, gate_mode(k
                         // The next chunk's gate: the second half (all of it after a
                         // short chunk, whose first half was not taken mid-chunk).
                         if (chunk + 1 < w.c1) {
-                            if (blocks8 <= 2) issue_gate_half<T>(sm, 0, tc0 + kT, w.row0, w.bb, &tm_z);
-                            issue_gate_half<T>(sm, 1, tc0 + kT, w.row0, w.bb, &tm_z);
+                            if (blocks8 <= 2) issue_gate_half<T, kBDL>(sm, 0, tc0 + kT, w.row0, w.bb, &tm_z);
+                            issue_gate_half<T, kBDL>(sm, 1, tc0 + kT, w.row0, w.bb, &tm_z);
                         }
                     }
                     // Stage s takes the chunk kStages ahead in this CTA's list once
@@ -923,8 +928,8 @@ __global__ void __launch_bounds__(kLanes, bulk_min_blocks(kMode, kR, gate_mode(k
             // the chunk before them computes).
             if (tid == 0 && w.c1 > w.c0) {
                 const int t0z = static_cast<int>(w.tok0) + w.c0 * kT;
-                issue_gate_half<T>(sm, 0, t0z, w.row0, w.bb, &tm_z);
-                issue_gate_half<T>(sm, 1, t0z, w.row0, w.bb, &tm_z);
+                issue_gate_half<T, kBDL>(sm, 0, t0z, w.row0, w.bb, &tm_z);
+                issue_gate_half<T, kBDL>(sm, 1, t0z, w.row0, w.bb, &tm_z);
             }
         }
         if (pw) run_chunks(std::true_type{});
@@ -1706,6 +1711,11 @@ cudaError_t launch_scan_bulk(const SaccScanExArgs& a, cudaStream_t stream, const
             cfg.numAttrs = 1;
             return cudaLaunchKernelExC(&cfg, fk.fn, args);
         }
+    }
+    if (bdl && a.z) {
+        // The walks below take the (B, D, L) gate as two 16-token halves per
+        // chunk: an unswizzled map with a 16 x 128 box.
+        if (!make_map_2d(&tz, dt, a.z, L, B * D, L * 2, kT / 2, kLanes, CU_TENSOR_MAP_SWIZZLE_NONE)) return cudaErrorInvalidValue;
     }
     const int chunked = p.cu ? 0 : chunk_parts(p.units, static_cast<unsigned long long>(sms), p.nchunks, L);
     if (chunked) {

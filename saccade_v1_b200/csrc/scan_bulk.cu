@@ -87,14 +87,16 @@ struct Cursor {
     int chunk, more;
 };
 
-// kZTile: the gate z staged by TMA like u and delta, in either layout.  Read
-// from global memory instead, (B, L, D) lane by lane, the gated scan was 36 %
+// kZ (gate_mode): the gate z staged by TMA, in either layout.  Read from
+// global memory instead, (B, L, D) lane by lane, the gated scan was 36 %
 // slower than ungated (the loads' latency and 64-bit address arithmetic on
-// the FMA pipe; prefetched one token block ahead, slower still), against
-// 1.4 % with the tile (three CTAs per SM: 23 % at config-4 size, where a
-// multi-wave grid would have held five).  The scan that forms delta itself
-// (kR > 0: the block pipeline's short sequences, where four CTAs per SM keep
-// config 1's 512 units in one wave) reads the gate from global memory.
+// the FMA pipe; prefetched one token block ahead, slower still).  A gate tile
+// per stage (kZ == 1, the fused chunk-parallel walk) holds three CTAs per SM;
+// one chunk's tile as two 16-token halves with a barrier each (kZ == 2, the
+// one-item walks) holds four: each half of the next chunk's gate loads once
+// the current chunk is past that half.  The scan that forms delta itself
+// (kR > 0: the block pipeline's short sequences) reads the gate from global
+// memory.
 // The one-thread-per-lane kernel writes a chunk's outputs over its
 // u tile (each thread reads its eight u values of a token block before it
 // writes their eight outputs to the same places, and the y tile has the u

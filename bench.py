@@ -79,6 +79,35 @@ def committed_traffic():
     return None
 
 
+def committed_fma_cycles():
+    """FMA-pipe cycles per warp and token of the scan from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "scan_bulk_c2.md")
+    try:
+        for line in open(path):
+            if line.startswith("fma_pipe_cycles_per_warp_token:"):
+                return float(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def pipe_roof(torch, device, kernel_ms, sm_mhz, batch):
+    """The scan's FP32 FMA-pipe roof: the measured FMA-pipe cycles per warp and
+    token (packed f32x2 instructions count two) times the launch's warp-tokens,
+    spread over every SM's four schedulers at the sampled SM clock; frac is that
+    time over the launch's event-timed duration."""
+    cycles = committed_fma_cycles()
+    if cycles is None or not sm_mhz:
+        return None
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    warp_tokens = batch * D * L / 32
+    roof_ms = cycles * warp_tokens / (sms * 4) / (sm_mhz * 1e3)
+    return {"pipe": "fp32 fma (packed pairs hold it two cycles)", "cycles_per_warp_token": cycles,
+            "warp_tokens_per_launch": int(warp_tokens), "sm_mhz": sm_mhz, "roof_ms": round(roof_ms, 4),
+            "kernel_ms": round(kernel_ms, 4), "frac": round(roof_ms / kernel_ms, 4),
+            "source": "profiles/scan_bulk_c2.md (ncu: sm__pipe_fma_cycles_active per warp-token)"}
+
+
 class NvmlClocks:
     """Samples SM clock and throttle reasons through NVML every 2 ms while the timed region runs (a query
     takes well under 0.1 ms, so short timed regions still get several samples)."""
@@ -353,6 +382,7 @@ def run_ours(args, rank, world, local_rank):
     value = nbytes * world / per_step_s / 1e9
     peak, peak_kind = peaks()
     achieved = nbytes / (kernel_ms / 1e3) / 1e9
+    clock_summary = clocks.summary()
     cpu = cpu_baseline(args) if world == 1 and not args.no_cpu_baseline else None
     extra = secondary(torch, device, stream, peaks()[0]) if not args.no_secondary else None
     if extra is not None and c4 is not None:
@@ -371,7 +401,8 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": committed_traffic(), "peak_kind": peak_kind,
                      "kernel": "scan (sacc_selective_scan_ex)", "algorithmic_bytes_per_launch": nbytes},
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
+        "pipe_roof": pipe_roof(torch, device, kernel_ms, clock_summary.get("sm_mhz"), args.batch),
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
         "secondary": extra,

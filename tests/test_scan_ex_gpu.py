@@ -577,36 +577,40 @@ def test_power_form_per_lane_rows_and_scales():
     assert ctypes_fault() == 0
 
 
+@pytest.mark.parametrize("layout", ["BLD", "BDL"])
 @pytest.mark.parametrize("B", [32, 64])
-def test_bulk_gated_bld_matches_oracle_lanes(B):
-    """(B, L, D) with a gate and a full C in the one-thread-per-lane kernel, whose gate comes from a TMA tile
-    like u and delta: 32 rows x 12 tiles = 384 units in one wave, 64 rows = 768 units split into parts
-    (handed over through the outputs).  L = 520: a partial last chunk.  h0 in, h_final out; sampled lanes
-    against the binary64 oracle on the same 16-bit inputs."""
+def test_bulk_gated_matches_oracle_lanes(B, layout):
+    """A gate and a full C in the one-thread-per-lane kernel, whose gate comes in two 16-token halves of a TMA
+    tile: 32 rows x 12 tiles = 384 units (a split launch at four CTAs per SM), 64 rows = 768 units (split into
+    more parts).  L = 520: a last chunk of 8 tokens, whose gate's second half arrives unread.  h0 in, h_final
+    out; sampled lanes against the binary64 oracle on the same 16-bit inputs, in both layouts."""
     L, D, N = 520, 1536, 16
     s = torch.cuda.Stream()
     g = torch.Generator(device="cuda")
-    g.manual_seed(90 + B)
+    g.manual_seed(90 + B + (7 if layout == "BDL" else 0))
     bf = torch.bfloat16
+    shp = (B, L, D) if layout == "BLD" else (B, D, L)
+    bshp = (B, L, 1, N) if layout == "BLD" else (B, 1, N, L)
     with torch.cuda.stream(s):
-        u, dl, z = (torch.randn(B, L, D, device="cuda", generator=g).to(bf) for _ in range(3))
-        bm, cm = (torch.randn(B, L, 1, N, device="cuda", generator=g).to(bf) for _ in range(2))
+        u, dl, z = (torch.randn(shp, device="cuda", generator=g).to(bf) for _ in range(3))
+        bm, cm = (torch.randn(bshp, device="cuda", generator=g).to(bf) for _ in range(2))
         A = -(torch.rand(D, N, device="cuda", generator=g) * 2 + 0.01)
         Dv = torch.randn(D, device="cuda", generator=g)
         bias = torch.full((D,), -3.0, device="cuda")
         h0 = torch.randn(B, D, N, device="cuda", generator=g) * 0.5
         hf = torch.empty(B, D, N, device="cuda")
-        y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout="BLD", stream=s)
+        y = sb.selective_scan_ex(u, dl, A, bm, cm, D=Dv, z=z, delta_bias=bias, h0=h0, h_final=hf, layout=layout, stream=s)
     s.synchronize()
     f = lambda x: x.float().cpu().numpy()
     An, Dn, hn = f(A), f(Dv), f(h0)
+    lane = (lambda t, b, d: t[b:b + 1, :, d:d + 1]) if layout == "BLD" else (lambda t, b, d: t[b:b + 1, d:d + 1])
     rng = np.random.default_rng(91 + B)
     for b, d in zip(rng.integers(0, B, 10), rng.integers(0, D, 10)):
         b, d = int(b), int(d)
-        ref, href = oracle.scan_ex(f(u[b:b + 1, :, d:d + 1]), f(dl[b:b + 1, :, d:d + 1]), An[d:d + 1], f(bm[b:b + 1]),
-                                   f(cm[b:b + 1]), layout="BLD", d=Dn[d:d + 1], z=f(z[b:b + 1, :, d:d + 1]),
-                                   delta_bias=np.full(1, -3.0, np.float32), h0=hn[b:b + 1, d:d + 1], want_final=True)
-        check_16bit(f"gated_bld_{B}_{b}_{d}", f(y[b:b + 1, :, d:d + 1]), ref)
+        ref, href = oracle.scan_ex(f(lane(u, b, d)), f(lane(dl, b, d)), An[d:d + 1], f(bm[b:b + 1]), f(cm[b:b + 1]),
+                                   layout=layout, d=Dn[d:d + 1], z=f(lane(z, b, d)), delta_bias=np.full(1, -3.0, np.float32),
+                                   h0=hn[b:b + 1, d:d + 1], want_final=True)
+        check_16bit(f"gated_{layout}_{B}_{b}_{d}", f(lane(y, b, d)), ref)
         np.testing.assert_allclose(f(hf[b:b + 1, d:d + 1]), href, rtol=1e-3, atol=1e-3)
     assert ctypes_fault() == 0
 

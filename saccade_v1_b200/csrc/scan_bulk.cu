@@ -16,14 +16,15 @@
 // that all threads read with broadcast loads.  Every input byte crosses HBM
 // once, every output byte once.
 //
-// Arithmetic: with N = 16 the scan is bound by the special-function unit, not
-// by HBM: every state update needs one 2^x (MUFU ex2, 16 per SM per clock) and
-// four FP32 operations (Delta*A, Delta*u*B, the state FMA and the C*h FMA),
-// against 6 bytes of bf16 traffic per 16 updates.  softplus runs on the FMA
-// pipe except for one ex2 (log1p(e) = e * P(e), a degree-7 minimax fit with
-// 3.3e-7 relative error, gen_softplus_poly.py), so the special-function unit
-// spends its cycles on the decays.  For S4D-real A (A[n] = (n + 1) A[0]) the
-// 16 decays of a token are powers of one exponential (scan_block8_pow).
+// Arithmetic: with N = 16 the scan is bound by its arithmetic, not by HBM.
+// Every state update needs its decay exp(Delta A[n]) and three FP32
+// operations (Delta u B, the state FMA and the C h FMA) against 6 bytes of
+// bf16 traffic per 16 updates.  For S4D-real A (A[n] = (n + 1) A[0]) the 16
+// decays of a token are powers of one exponential, a product tree of packed
+// multiplies (scan_block8_pow), and the FP32 FMA pipe binds; for any other A
+// each decay is one 2^x on the special-function unit, which binds.  softplus
+// runs on the FMA pipe except for one ex2 (log1p(e) = e * P(e), a degree-5
+// minimax fit with 8.5e-6 relative error, gen_softplus_poly.py).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>

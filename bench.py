@@ -15,8 +15,10 @@ metric "scan GB/s": algorithmic bytes (u, delta, y, B, C and the FP32
 parameters, each counted once) / time.  `value` is device-timed with CUDA
 events over K steps on the launching stream, max over ranks; `e2e` is the
 same metric through the public API with the inputs copied from pinned host
-memory and y copied back inside the timed region.  `roofline` compares the
-scan kernel against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+memory and y copied back inside the timed region, with `e2e.pcie_roof` its
+bound from the pinned copy rates measured on the same GPU.  `roofline`
+compares the scan kernel against the measured HBM copy bandwidth
+(MEASURED_PEAKS.json).
 
 `secondary` (skipped with --no-secondary; `--only NAME` runs one alone) times
 the other rows of the path on the device: config 3's L = 1 step, packed
@@ -106,6 +108,60 @@ def pipe_roof(torch, device, kernel_ms, sm_mhz, batch):
             "warp_tokens_per_launch": int(warp_tokens), "sm_mhz": sm_mhz, "roof_ms": round(roof_ms, 4),
             "kernel_ms": round(kernel_ms, 4), "frac": round(roof_ms / kernel_ms, 4),
             "source": "profiles/scan_bulk_c2.md (ncu: sm__pipe_fma_cycles_active per warp-token)"}
+
+
+def pcie_roof(torch, device, u_host, y_dev, y_host, h2d, d2h, e2e_step_ms, max_over_ranks):
+    """The `e2e` leg's PCIe roof on this GPU: pinned copies of one whole
+    sequence-batch tensor timed host-to-device alone, device-to-host alone and
+    both at once on two streams (best of five each).  The step cannot move its
+    bytes faster than min(h2d, d2h) of them in both directions at the joint
+    rate plus the rest in the larger direction alone; frac is that time over
+    the measured e2e step.  Every rank measures its own link; the bound is the
+    slowest rank's."""
+    scratch = torch.empty(u_host.shape, dtype=u_host.dtype, device=device)
+    s_in, s_out = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+
+    def best(fn):
+        fn()
+        torch.cuda.synchronize(device)
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s_in)
+            s_out.wait_event(a)
+            fn()
+            done = torch.cuda.Event()
+            done.record(s_out)
+            s_in.wait_event(done)
+            b.record(s_in)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return min(ts)
+
+    def h2d_only():
+        with torch.cuda.stream(s_in):
+            scratch.copy_(u_host, non_blocking=True)
+
+    def d2h_only():
+        with torch.cuda.stream(s_out):
+            y_host.copy_(y_dev, non_blocking=True)
+
+    def both():
+        h2d_only()
+        d2h_only()
+
+    n_in, n_out = u_host.numel() * u_host.element_size(), y_dev.numel() * y_dev.element_size()
+    r_in = n_in / best(h2d_only) / 1e6
+    r_out = n_out / best(d2h_only) / 1e6
+    r_both = min(n_in, n_out) / best(both) / 1e6
+    joint = min(h2d, d2h)
+    rest, r_rest = (h2d - joint, r_in) if h2d >= d2h else (d2h - joint, r_out)
+    bound_ms = max_over_ranks(joint / r_both / 1e6 + rest / r_rest / 1e6)
+    del scratch
+    return {"h2d_GBs": round(r_in, 1), "d2h_GBs": round(r_out, 1), "both_directions_GBs_each": round(r_both, 1),
+            "bound_ms": round(bound_ms, 3), "e2e_ms_per_step": round(e2e_step_ms, 3),
+            "frac": round(bound_ms / e2e_step_ms, 4),
+            "model": "min(h2d, d2h) bytes at the joint rate + the rest at the larger direction's own rate"}
 
 
 class NvmlClocks:
@@ -369,6 +425,7 @@ def run_ours(args, rank, world, local_rank):
     e1.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    pcie = pcie_roof(torch, device, host["u"], y, y_host, h2d, d2h, e2e_ms / e2e_steps, max_over_ranks)
 
     # Config 4 (4-layer stack, batch-sharded): every rank takes part.
     c4 = None
@@ -397,7 +454,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "inputs 1.2 GB > 126 MB L2, no flush"},
         "tracks_frames_per_s": round(args.batch * world / per_step_s, 1),
         "e2e": {"value": round(nbytes * world / (e2e_ms / 1e3 / e2e_steps) / 1e9, 3), "unit": UNIT,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps, "pcie_roof": pcie},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": committed_traffic(), "peak_kind": peak_kind,
                      "kernel": "scan (sacc_selective_scan_ex)", "algorithmic_bytes_per_launch": nbytes},

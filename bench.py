@@ -826,7 +826,7 @@ def c1_block(torch, device, stream):
     flops = 2 * B1 * L1 * (dm * 2 * D1 + D1 * (R1 + 2 * N1) + R1 * D1 + D1 * dm)
     return {"us_graph": round(graph_us, 2), "us_eager": round(eager_us, 2),
             "tracks_frames_per_s": round(B1 / (graph_us * 1e-6), 1), "gflop": round(flops / 1e9, 3),
-            "kernels_per_forward": 7,  # dt_proj runs inside the scan at dt_rank 8
+            "kernels_per_forward": 6,  # RMSNorm prep in one launch; dt_proj runs inside the scan at dt_rank 8
             "workload": "256 tracks x 32 frames, d_model 128, D 256, N 16, dt_rank 8, fp16, RMSNorm + residual"}
 
 

@@ -28,31 +28,31 @@ __device__ unsigned int g_block_fault; // set when a bounded wait of a block ker
 
 namespace {
 
-// One warp per token row: r[m] = 1 / sqrt(mean_k x[m,k]^2 + eps).
+// RMSNorm folded into in_proj, in one launch: blocks [0, rms_blocks) give the
+// per-token scales r[m] = 1 / sqrt(mean_k x[m,k]^2 + eps), one warp per token
+// row; the blocks after them give W'[i, k] = W_in[i, k] * w[k] (the norm
+// weight folded into W_in's columns, n rows).  Both parts are independent.
 template <typename T>
-__global__ void __launch_bounds__(256) rms_scale_kernel(const T* __restrict__ x, unsigned long long m, unsigned k,
-                                                        float eps, float* __restrict__ r) {
+__global__ void __launch_bounds__(256) rms_prep_kernel(const T* __restrict__ x, unsigned long long m, unsigned k, float eps,
+                                                       float* __restrict__ r, unsigned rms_blocks, const T* __restrict__ w_in,
+                                                       const float* __restrict__ w, unsigned long long n, T* __restrict__ out) {
     pdl_wait();
-    const unsigned long long row = (static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x) / 32;
-    const int lane = threadIdx.x % 32;
-    if (row >= m) return;
-    const T* xr = x + row * k;
-    float acc = 0.0f;
-    for (unsigned i = lane; i < k; i += 32) {
-        const float v = to_f32(xr[i]);
-        acc = fmaf(v, v, acc);
-    }
+    if (blockIdx.x < rms_blocks) {
+        const unsigned long long row = (static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x) / 32;
+        const int lane = threadIdx.x % 32;
+        if (row >= m) return;
+        const T* xr = x + row * k;
+        float acc = 0.0f;
+        for (unsigned i = lane; i < k; i += 32) {
+            const float v = to_f32(xr[i]);
+            acc = fmaf(v, v, acc);
+        }
 #pragma unroll
-    for (int off = 16; off > 0; off /= 2) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) r[row] = rsqrtf(acc / static_cast<float>(k) + eps);
-}
-
-// W'[n, k] = W[n, k] * w[k].
-template <typename T>
-__global__ void __launch_bounds__(256) scale_columns_kernel(const T* __restrict__ w_in, const float* __restrict__ w,
-                                                            unsigned long long n, unsigned k, T* __restrict__ out) {
-    pdl_wait();
-    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * 256 + threadIdx.x;
+        for (int off = 16; off > 0; off /= 2) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) r[row] = rsqrtf(acc / static_cast<float>(k) + eps);
+        return;
+    }
+    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x - rms_blocks) * 256 + threadIdx.x;
     if (i >= n * k) return;
     out[i] = from_f32<T>(to_f32(w_in[i]) * w[i % k]);
 }
@@ -271,26 +271,17 @@ cudaError_t launch_repeat_last_row(int dtype, const void* src, unsigned long lon
                         static_cast<const std::uint16_t*>(src), rows, copies, cols, static_cast<std::uint16_t*>(dst));
 }
 
-cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
-                             cudaStream_t stream) {
-    const unsigned long long blocks = (m * 32 + 255) / 256;
-    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+cudaError_t launch_rms_prep(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r, const void* w_in,
+                            const float* w, unsigned long long n, void* out, cudaStream_t stream) {
+    const unsigned long long rms_blocks = (m * 32 + 255) / 256, col_blocks = (n * k + 255) / 256;
+    if (rms_blocks + col_blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    const dim3 grid(static_cast<unsigned>(rms_blocks + col_blocks));
+    const unsigned rb = static_cast<unsigned>(rms_blocks);
     if (dtype == SACC_DTYPE_BF16)
-        return launch_pdl_k(rms_scale_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-                            static_cast<const __nv_bfloat16*>(x), m, k, eps, r);
-    return launch_pdl_k(rms_scale_kernel<__half>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-                        static_cast<const __half*>(x), m, k, eps, r);
-}
-
-cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
-                                 cudaStream_t stream) {
-    const unsigned long long blocks = (n * k + 255) / 256;
-    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
-    if (dtype == SACC_DTYPE_BF16)
-        return launch_pdl_k(scale_columns_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-                            static_cast<const __nv_bfloat16*>(w_in), w, n, k, static_cast<__nv_bfloat16*>(out));
-    return launch_pdl_k(scale_columns_kernel<__half>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-                        static_cast<const __half*>(w_in), w, n, k, static_cast<__half*>(out));
+        return launch_pdl_k(rms_prep_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(x), m, k,
+                            eps, r, rb, static_cast<const __nv_bfloat16*>(w_in), w, n, static_cast<__nv_bfloat16*>(out));
+    return launch_pdl_k(rms_prep_kernel<__half>, grid, dim3(256), 0, stream, static_cast<const __half*>(x), m, k, eps, r, rb,
+                        static_cast<const __half*>(w_in), w, n, static_cast<__half*>(out));
 }
 
 cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long long ldx, const float* w, const float* bias,
@@ -342,10 +333,8 @@ cudaError_t launch_conv_silu(int dtype, int kwidth, const void* x, unsigned long
 }
 
 cudaError_t load_block_kernels(std::string& report) {
-    const void* ks[] = {reinterpret_cast<const void*>(rms_scale_kernel<__nv_bfloat16>),
-                        reinterpret_cast<const void*>(rms_scale_kernel<__half>),
-                        reinterpret_cast<const void*>(scale_columns_kernel<__nv_bfloat16>),
-                        reinterpret_cast<const void*>(scale_columns_kernel<__half>),
+    const void* ks[] = {reinterpret_cast<const void*>(rms_prep_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(rms_prep_kernel<__half>),
                         reinterpret_cast<const void*>(conv_silu_kernel<__nv_bfloat16, 4>),
                         reinterpret_cast<const void*>(conv_silu_kernel<__half, 4>),
                         reinterpret_cast<const void*>(conv4_silu_rows_kernel<__nv_bfloat16>),
@@ -358,7 +347,7 @@ cudaError_t load_block_kernels(std::string& report) {
         const cudaError_t e = cudaFuncGetAttributes(&attr, k);
         if (e != cudaSuccess) return e;
     }
-    report += "kernels_loaded=block (rms_scale, scale_columns, conv_silu, repeat_last_row) x11\n";
+    report += "kernels_loaded=block (rms_prep, conv_silu, repeat_last_row) x9\n";
     return cudaSuccess;
 }
 

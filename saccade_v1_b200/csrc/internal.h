@@ -107,10 +107,11 @@ struct RowStrides {
 bool bulk_eligible(const SaccScanExArgs& a, const RowStrides* rs = nullptr);
 cudaError_t launch_scan_step(const SaccScanStepArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm(const SaccGemmArgs& a, cudaStream_t stream);
-cudaError_t launch_rms_scale(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r,
-                             cudaStream_t stream);
-cudaError_t launch_scale_columns(int dtype, const void* w_in, const float* w, unsigned long long n, unsigned k, void* out,
-                                 cudaStream_t stream);
+// RMSNorm folded into in_proj, one launch: r[i] = 1 / sqrt(mean_k x[i, k]^2
+// + eps) for the m rows of x (k wide), and out = W_in (n x k) with column j
+// scaled by w[j].
+cudaError_t launch_rms_prep(int dtype, const void* x, unsigned long long m, unsigned k, float eps, float* r, const void* w_in,
+                            const float* w, unsigned long long n, void* out, cudaStream_t stream);
 // Words that a kernel of the block pipeline zeroes as a side job (block 0,
 // after griddepcontrol.wait): the fused chunk-parallel scan's hand-off flags,
 // cleared by the conv kernel that precedes the scan in every block call, so

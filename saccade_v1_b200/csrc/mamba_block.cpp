@@ -3,7 +3,8 @@
 // (src/head_trt_network.cpp:181-233; binary64 twin
 // src/head_reference.cpp:471-495), plus BASELINE's RMSNorm prologue:
 //
-//   r      = 1 / sqrt(mean(x^2) + eps)                    rms_scale            (x once)
+//   r      = 1 / sqrt(mean(x^2) + eps)                    rms_prep (x once), which also forms
+//                                                          W_in diag(w) in the same launch
 //   xz     = diag(r) x (W_in diag(w))^T                   one tcgen05 GEMM, row scale epilogue
 //   u      = silu(causal_conv1d(x_in) + conv_b)           conv_silu on the x_in half of xz
 //   dbc    = u W_x^T = [dt | B | C]                       one tcgen05 GEMM (N = dt_rank + 2 d_state)
@@ -221,8 +222,8 @@ cudaError_t launch_mamba_block(const SaccMambaBlockArgs& a, void* workspace, cud
     const bool norm = a.norm_w != nullptr;
     const void* w_in = a.w_in;
     if (norm) {
-        if ((err = launch_rms_scale(dt_, a.x, M, static_cast<unsigned>(dm), a.eps, r, stream)) != cudaSuccess) return err;
-        if ((err = launch_scale_columns(dt_, a.w_in, a.norm_w, 2 * D, static_cast<unsigned>(dm), wn, stream)) != cudaSuccess)
+        if ((err = launch_rms_prep(dt_, a.x, M, static_cast<unsigned>(dm), a.eps, r, a.w_in, a.norm_w, 2 * D, wn, stream)) !=
+            cudaSuccess)
             return err;
         w_in = wn;
     }
@@ -267,8 +268,7 @@ cudaError_t launch_cross_block(const SaccCrossScanBlockArgs& c, void* workspace,
     const bool norm = a.norm_w != nullptr;
     const void* w_in = a.w_in;
     if (norm) {
-        if ((err = launch_rms_scale(dt_, rows, P, static_cast<unsigned>(dm), a.eps, r, stream)) != cudaSuccess) return err;
-        if ((err = launch_scale_columns(dt_, a.w_in, a.norm_w, 2 * D, static_cast<unsigned>(dm), ws + l.wn, stream)) !=
+        if ((err = launch_rms_prep(dt_, rows, P, static_cast<unsigned>(dm), a.eps, r, a.w_in, a.norm_w, 2 * D, ws + l.wn, stream)) !=
             cudaSuccess)
             return err;
         w_in = ws + l.wn;

@@ -7,7 +7,8 @@
 //  * one thread owns a (batch, channel) lane and keeps all N states of that
 //    lane in registers, so per-token work (softplus, u/delta loads, D skip,
 //    output store) is done once per lane instead of N times and the state sum
-//    needs no shuffles;
+//    needs no shuffles; for N = 16, four threads share a lane, four states
+//    each (scan_f32_quad_kernel), for four times the warps per SM;
 //  * the length axis is split into K chunks (K a power of two) when there are
 //    too few lanes to fill 148 SMs.  Chunk k of a lane first runs the
 //    recurrence from zero over its tokens (pass 1) and publishes
@@ -40,6 +41,8 @@
 #include <cfloat>
 #include <climits>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 #include <type_traits>
 
@@ -383,6 +386,177 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
     if (blockIdx.x == 0 && threadIdx.x == 0) pdl_wait();
 }
 
+// N = 16 with four threads per lane (scan_f32_quad_kernel): thread q of a
+// lane owns states q, q + 4, q + 8 and q + 12, so the reference's butterfly
+// sum (offset 8 first) runs its first two levels inside each thread and its
+// last two as xor shuffles over the four threads (offsets 2, then 1): the same
+// association, so the same bits.  A thread holds a quarter of the states, a
+// CTA four times the warps, and the per-token softplus is formed by each of
+// the four threads.
+constexpr int kQuad = 4, kQuadStates = 4;
+
+template <typename T, int CW>
+__device__ __forceinline__ void load_token_quad(const Params& p, unsigned long long token, unsigned long long d, int q,
+                                                Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k) {
+    const unsigned long long at = token * p.channels + d;
+    k.u = load_act(static_cast<const T*>(p.u) + at);
+    k.x = load_act(static_cast<const T*>(p.delta) + at);
+    const T* b = static_cast<const T*>(p.b) + token * 16 + q;
+#pragma unroll
+    for (int j = 0; j < kQuadStates; ++j) k.b[j] = load_act(b + 4 * j);
+    if constexpr (CW > 1) {
+        const T* c = static_cast<const T*>(p.c) + token * 16 + q;
+#pragma unroll
+        for (int j = 0; j < kQuadStates; ++j) k.c[j] = load_act(c + 4 * j);
+    } else {
+        k.c[0] = load_act(static_cast<const T*>(p.c) + token);
+    }
+}
+
+// The four lanes of the calling thread's group: the groups of a warp walk
+// different chunks and lanes, so every shuffle names its own group only.
+__device__ __forceinline__ unsigned quad_mask() { return 0xfu << (threadIdx.x & 28u); }
+
+// The sum over all 16 states of one token in the reference's association:
+// in-thread levels (states q + (q + 8), (q + 4) + (q + 12), then their sum),
+// then the partner at xor 2 and at xor 1.  Every thread of the four gets the
+// same bits (IEEE addition is commutative).
+__device__ __forceinline__ float quad_sum(const float (&t)[kQuadStates]) {
+    const unsigned m = quad_mask();
+    float v = __fadd_rn(__fadd_rn(t[0], t[2]), __fadd_rn(t[1], t[3]));
+    v = __fadd_rn(v, __shfl_xor_sync(m, v, 2));
+    return __fadd_rn(v, __shfl_xor_sync(m, v, 1));
+}
+
+// step_out for a quarter of the states: the four threads' failure bits are
+// combined (each state's first failure in the reference's order, OR-ed over
+// the states as the reference's group does), so all four return together.
+template <int CW, bool kHalfOut>
+__device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const float (&a)[kQuadStates],
+                                                  const Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k, bool has_d,
+                                                  float skip_d, float& y) {
+    constexpr int CQ = CW > 1 ? kQuadStates : 1;
+    float hn[kQuadStates], decay[kQuadStates], drive[kQuadStates];
+    if (!states_fast<kQuadStates, CQ>(h, a, k, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
+    unsigned fail = 0;
+    float term[kQuadStates];
+#pragma unroll
+    for (int j = 0; j < kQuadStates; ++j) {
+        term[j] = __fmul_rn(k.c[CQ > 1 ? j : 0], hn[j]);
+        fail |= !finite32(decay[j]) ? kDecay : !finite32(drive[j]) ? kDrive : !finite32(hn[j]) ? kState
+              : !finite32(term[j]) ? kTerm : 0u;
+        h[j] = hn[j];
+    }
+    fail |= __shfl_xor_sync(quad_mask(), fail, 1);
+    fail |= __shfl_xor_sync(quad_mask(), fail, 2);
+    if (fail) return fail;
+    const float sum = quad_sum(term);
+    const float skip = __fmul_rn(skip_d, k.u);
+    if (has_d && !finite32(skip)) return kSkip;
+    float out = has_d ? __fadd_rn(sum, skip) : sum;
+    if (!finite32(out)) {
+        // Every term is finite but a partial sum left the FP32 range: repeat
+        // with exact power-of-two scaling (reference cuda/selective_scan.cu:116-122).
+        float sc[kQuadStates];
+#pragma unroll
+        for (int j = 0; j < kQuadStates; ++j) sc[j] = __fmul_rn(term[j], 0x1p-8f);
+        const float scaled = quad_sum(sc);
+        out = has_d ? __fadd_rn(scaled, __fmul_rn(skip, 0x1p-8f)) : scaled;
+        if (fabsf(out) <= FLT_MAX * 0x1p-8f) out = __fmul_rn(out, 0x1p8f);
+        else return kOutput;
+    }
+    if (kHalfOut && !(fabsf(out) < kHalfOverflow)) return kOutput;
+    y = out;
+    return 0;
+}
+
+// scan_f32_kernel for N = 16 at four threads per lane: the same chunks, carry
+// fold and failure rules, each (lane, chunk) a group of four consecutive
+// threads.  With the same chunk count its outputs are scan_f32_kernel's bits.
+template <typename T, int CW>
+__global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccScanStatus* status) {
+    constexpr int CQ = CW > 1 ? kQuadStates : 1;
+    extern __shared__ float2 carry[]; // [chunk][lane in CTA][state]: (decay product, local state)
+    __shared__ int chunk_failed[kThreads / kQuad];
+    const int K = p.chunks, LPC = p.lanes_per_cta;
+    const int tid = threadIdx.x, q = tid % kQuad, g = tid / kQuad, li = g % LPC, k = g / LPC;
+    const unsigned long long lane = static_cast<unsigned long long>(blockIdx.x) * LPC + li;
+    const bool active = lane < p.lanes; // uniform over a lane's four threads
+    const unsigned long long L = p.length, Dc = p.channels;
+    const unsigned long long bb = active ? lane / Dc : 0, d = active ? lane % Dc : 0;
+    const unsigned long long t0 = L * k / K, t1 = L * (k + 1) / K;
+
+    float a[kQuadStates];
+#pragma unroll
+    for (int j = 0; j < kQuadStates; ++j) a[j] = active ? __ldg(p.a + (p.a_shared ? 0 : d * 16) + q + 4 * j) : 0.0f;
+    const float skip_d = (active && p.has_d) ? __ldg(p.d + d) : 0.0f;
+    float h[kQuadStates];
+#pragma unroll
+    for (int j = 0; j < kQuadStates; ++j) h[j] = 0.0f;
+
+    if (K > 1) {
+        float prod[kQuadStates];
+#pragma unroll
+        for (int j = 0; j < kQuadStates; ++j) prod[j] = 1.0f;
+        if (active && k < K - 1) {
+            Token<kQuadStates, CQ> cur;
+            if (t0 < t1) load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
+            for (unsigned long long t = t0; t < t1; ++t) {
+                Token<kQuadStates, CQ> nxt;
+                if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
+                step_carry<kQuadStates, CQ>(h, prod, a, cur);
+                cur = nxt;
+            }
+        }
+        float2* mine = carry + (static_cast<size_t>(k) * LPC + li) * 16;
+#pragma unroll
+        for (int j = 0; j < kQuadStates; ++j) mine[q + 4 * j] = make_float2(prod[j], h[j]);
+        __syncthreads();
+        // Fold the carries of chunks 0..k-1: H = prod_j * H + local_j.
+#pragma unroll
+        for (int j = 0; j < kQuadStates; ++j) h[j] = 0.0f;
+        for (int c = 0; c < k; ++c) {
+            const float2* cj = carry + (static_cast<size_t>(c) * LPC + li) * 16;
+#pragma unroll
+            for (int j = 0; j < kQuadStates; ++j) {
+                const float2 v = cj[q + 4 * j];
+                h[j] = h[j] == 0.0f ? v.y : __fmaf_rn(v.x, h[j], v.y);
+            }
+        }
+    }
+
+    unsigned fail = 0;
+    if (active && t0 < t1) {
+        Token<kQuadStates, CQ> cur;
+        load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
+        for (unsigned long long t = t0; t < t1; ++t) {
+            Token<kQuadStates, CQ> nxt;
+            if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
+            float y = 0.0f;
+            fail = step_out_quad<CW, std::is_same_v<T, __half>>(h, a, cur, p.has_d != 0, skip_d, y);
+            if (fail) break;
+            if (q == 0) store_act(static_cast<T*>(p.y) + (bb * L + t) * Dc + d, y);
+            cur = nxt;
+        }
+    }
+    if (K > 1) {
+        // A lane reports the failure of its earliest failing chunk only, as the
+        // sequential recurrence stops at its first failure.
+        if (q == 0) chunk_failed[g] = fail ? 1 : 0;
+        __syncthreads();
+        if (fail && q == 0) {
+            bool earlier = false;
+            for (int c = 0; c < k; ++c) earlier |= chunk_failed[c * LPC + li] != 0;
+            if (!earlier) atomicOr(&status->flags, fail);
+        }
+    } else if (fail && q == 0) {
+        atomicOr(&status->flags, fail);
+    }
+    // The check grid released this grid before it finished: one thread waits
+    // for it here, so this grid completes only after the check has.
+    if (blockIdx.x == 0 && threadIdx.x == 0) pdl_wait();
+}
+
 // Exact NaN / Inf bits of the inputs.  Releases the next kernel of the stream
 // at once when that one is launched with programmatic stream serialization
 // (the scan, which does not read what the check writes).
@@ -423,7 +597,23 @@ const void* pick_kernel_t(unsigned state, bool c_full) {
     }
 }
 
+// Threads per lane: four for N = 16 (scan_f32_quad_kernel), one otherwise.
+// SACC_F32_KERNEL=one_thread keeps N = 16 on scan_f32_kernel, the kernel the
+// four-thread one reproduces bit for bit when both split a lane into the same
+// chunks (tests compare the two).
+int threads_per_lane(unsigned state) {
+    if (state != 16) return 1;
+    const char* v = std::getenv("SACC_F32_KERNEL");
+    return (v && std::strcmp(v, "one_thread") == 0) ? 1 : kQuad;
+}
+
 const void* pick_kernel(unsigned state, bool half, bool c_full) {
+    if (threads_per_lane(state) == kQuad) {
+        if (half) return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16>)
+                                : reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 1>);
+        return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16>)
+                      : reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 1>);
+    }
     return half ? pick_kernel_t<__half>(state, c_full) : pick_kernel_t<float>(state, c_full);
 }
 
@@ -433,16 +623,17 @@ const void* pick_kernel(unsigned state, bool half, bool c_full) {
 // both split a lane into the same chunks and the FP16 outputs stay the FP32
 // outputs rounded.
 int resident_per_sm(unsigned state, bool c_full) {
-    static std::atomic<int> cache[64][12] = {};
+    static std::atomic<int> cache[64][14] = {};
     int idx = 0;
     while ((1u << idx) < state && idx < 5) ++idx;
-    idx = 2 * idx + (c_full ? 1 : 0);
+    const int tpl = threads_per_lane(state);
+    idx = tpl == kQuad ? 12 + (c_full ? 1 : 0) : 2 * idx + (c_full ? 1 : 0);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
     int v = cache[dev][idx].load(std::memory_order_relaxed);
     if (v > 0) return v;
     const void* fn = pick_kernel(state, false, c_full);
-    const size_t smem = static_cast<size_t>(kThreads) * state * sizeof(float2);
+    const size_t smem = static_cast<size_t>(kThreads / tpl) * state * sizeof(float2);
     int n = 0;
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
@@ -483,16 +674,17 @@ cudaError_t launch_scan_f32(const ScanF32Launch& s, SaccScanStatus* status, int 
     // lanes x 960 tokens runs 32 chunks in 128 CTAs.
     const unsigned long long target =
         static_cast<unsigned long long>(sm_count) * static_cast<unsigned long long>(resident_per_sm(s.state, s.c_full)) * kThreads;
+    const int tpl = threads_per_lane(s.state);
     int K = 1;
-    while (K < 64 && s.lanes * static_cast<unsigned long long>(K) * 2ull <= target &&
+    while (K < 64 && s.lanes * static_cast<unsigned long long>(K * tpl) * 2ull <= target &&
            s.length >= static_cast<unsigned long long>(K) * 2ull * 2ull)
         K *= 2;
     p.chunks = K;
-    p.lanes_per_cta = kThreads / K;
+    p.lanes_per_cta = kThreads / tpl / K;
     const unsigned long long blocks = (s.lanes + p.lanes_per_cta - 1) / p.lanes_per_cta;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidValue;
     p.scan_blocks = static_cast<unsigned>(blocks);
-    const size_t smem = K > 1 ? static_cast<size_t>(kThreads) * s.state * sizeof(float2) : 0;
+    const size_t smem = K > 1 ? static_cast<size_t>(kThreads / tpl) * s.state * sizeof(float2) : 0;
     void* args[] = {&p, &status};
     const void* fn = pick_kernel(s.state, s.half, s.c_full);
     if (smem > 48 * 1024) {
@@ -547,6 +739,10 @@ cudaError_t load_scan_f32_kernels(std::string& report) {
         {"scan_f16io_c1_n8", scan_kernel_ptr<__half, 8, 1>(), kThreads * 8 * sizeof(float2)},
         {"scan_f16io_c1_n16", scan_kernel_ptr<__half, 16, 1>(), kThreads * 16 * sizeof(float2)},
         {"scan_f16io_c1_n32", scan_kernel_ptr<__half, 32, 1>(), kThreads * 32 * sizeof(float2)},
+        {"scan_f32_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16>), 0},
+        {"scan_f32_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 1>), 0},
+        {"scan_f16io_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16>), 0},
+        {"scan_f16io_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 1>), 0},
         {"check", reinterpret_cast<const void*>(check_kernel), 0},
         {"finalize", reinterpret_cast<const void*>(finalize_kernel<unsigned, 0x7fc00000u>), 0},
         {"finalize_f16", reinterpret_cast<const void*>(finalize_kernel<unsigned short, 0x7e00u>), 0},

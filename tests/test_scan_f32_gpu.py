@@ -179,3 +179,20 @@ def test_deploy_shapes_random():
     for length in (960, 240, 60, 25):
         k = random_case(Shape(4, length, 256, 16, 1, 1, True), 456 + length)
         scan_case(f"deploy_L{length}", k)
+
+
+def test_four_threads_per_lane_equal_one_thread(monkeypatch):
+    """N = 16 runs four threads per lane (states q, q + 4, q + 8, q + 12 each, the reference's butterfly sum
+    finished by two xor shuffles); with the one-thread kernel (SACC_F32_KERNEL=one_thread) splitting the
+    lanes into the same chunks, outputs and status bits are identical, at the deploy shapes (rank-1 C), with a
+    full C, and on the failure cases."""
+    cases = {f"deploy_L{L}": random_case(Shape(4, L, 256, 16, 1, 1, True), 900 + L) for L in (960, 240, 60, 7)}
+    cases["full_c_per_channel_a"] = random_case(Shape(3, 200, 64, 16, 64, 16, True), 77)
+    cases.update({name: k for name, k, _, _, _ in sc.failure_cases() if k.shape.state == 16})
+    for name, k in cases.items():
+        monkeypatch.setenv("SACC_F32_KERNEL", "one_thread")
+        want = gu.run_f32(k)
+        monkeypatch.delenv("SACC_F32_KERNEL")
+        got = gu.run_f32(k)
+        assert got[1] == want[1], (name, got[1], want[1])
+        assert np.array_equal(got[0].view(np.uint32), want[0].view(np.uint32)), name

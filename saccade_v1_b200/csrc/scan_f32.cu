@@ -171,11 +171,31 @@ __device__ __forceinline__ void load_token(const Params& p, unsigned long long t
 
 // New states of one token; returns false when the plain FP32 products may
 // differ from the reference's scaled ones (then the caller uses the scaled form).
+// softplus as the plain FP32 path forms it (x > 20 passes through).
+__device__ __forceinline__ float softplus_plain(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// states_fast with Delta = softplus_plain(k.x) already formed (dv).
+template <int N, int CW>
+__device__ __forceinline__ bool states_fast_dv(const float (&h)[N], const float (&a)[N], const Token<N, CW>& k, float dv,
+                                               float (&hn)[N], float (&decay)[N], float (&drive)[N]) {
+    if (!(k.x >= -80.0f)) return false;
+    bool fast = true;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        decay[n] = expf(__fmul_rn(dv, a[n]));
+        const float db = __fmul_rn(dv, k.b[n]);
+        drive[n] = __fmul_rn(db, k.u);
+        fast = fast & (fabsf(db) >= 0x1p-126f) & (fabsf(drive[n]) >= 0x1p-126f) & (fabsf(drive[n]) <= FLT_MAX);
+        hn[n] = __fmaf_rn(decay[n], h[n], drive[n]);
+    }
+    return fast;
+}
+
 template <int N, int CW>
 __device__ __forceinline__ bool states_fast(const float (&h)[N], const float (&a)[N], const Token<N, CW>& k, float (&hn)[N],
                                             float (&decay)[N], float (&drive)[N]) {
     if (!(k.x >= -80.0f)) return false;
-    const float dv = k.x > 20.0f ? k.x : log1pf(expf(k.x));
+    const float dv = softplus_plain(k.x);
     bool fast = true;
 #pragma unroll
     for (int n = 0; n < N; ++n) {
@@ -433,11 +453,11 @@ __device__ __forceinline__ float quad_sum(const float (&t)[kQuadStates]) {
 // the states as the reference's group does), so all four return together.
 template <int CW, bool kHalfOut>
 __device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const float (&a)[kQuadStates],
-                                                  const Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k, bool has_d,
+                                                  const Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k, float dv, bool has_d,
                                                   float skip_d, float& y) {
     constexpr int CQ = CW > 1 ? kQuadStates : 1;
     float hn[kQuadStates], decay[kQuadStates], drive[kQuadStates];
-    if (!states_fast<kQuadStates, CQ>(h, a, k, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
+    if (!states_fast_dv<kQuadStates, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
     unsigned fail = 0;
     float term[kQuadStates];
 #pragma unroll
@@ -470,6 +490,42 @@ __device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const
     return 0;
 }
 
+// Pass 1 step for a quarter of the states, Delta given.
+template <int CQ>
+__device__ __forceinline__ void step_carry_quad(float (&h)[kQuadStates], float (&prod)[kQuadStates], const float (&a)[kQuadStates],
+                                                const Token<kQuadStates, CQ>& k, float dv) {
+    float hn[kQuadStates], decay[kQuadStates], drive[kQuadStates];
+    if (!states_fast_dv<kQuadStates, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
+#pragma unroll
+    for (int j = 0; j < kQuadStates; ++j) {
+        h[j] = hn[j];
+        prod[j] = __fmul_rn(prod[j], decay[j]);
+    }
+}
+
+// Delta of token t of a walk from t0: every fourth token, thread q of the
+// lane forms softplus_plain of token t + q from the raw delta it loaded a
+// group earlier (`next`; past t1: unused) and loads the one of token
+// t + 4 + q; token t's Delta comes from thread (t - t0) % 4 of the group.
+struct QuadDelta {
+    float mine, next;
+};
+template <typename T>
+__device__ __forceinline__ float quad_delta_load(const Params& p, unsigned long long row0, unsigned long long t,
+                                                 unsigned long long t1, unsigned long long d) {
+    return t < t1 ? load_act(static_cast<const T*>(p.delta) + (row0 + t) * p.channels + d) : 0.0f;
+}
+template <typename T>
+__device__ __forceinline__ float quad_delta(const Params& p, unsigned long long row0, unsigned long long t, unsigned long long t0,
+                                            unsigned long long t1, unsigned long long d, int q, QuadDelta& qd) {
+    const int j = static_cast<int>((t - t0) & 3u);
+    if (j == 0) {
+        qd.mine = softplus_plain(qd.next);
+        qd.next = quad_delta_load<T>(p, row0, t + 4 + static_cast<unsigned long long>(q), t1, d);
+    }
+    return __shfl_sync(quad_mask(), qd.mine, static_cast<int>(threadIdx.x & 28u) | j);
+}
+
 // scan_f32_kernel for N = 16 at four threads per lane: the same chunks, carry
 // fold and failure rules, each (lane, chunk) a group of four consecutive
 // threads.  With the same chunk count its outputs are scan_f32_kernel's bits.
@@ -500,11 +556,13 @@ __global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccS
         for (int j = 0; j < kQuadStates; ++j) prod[j] = 1.0f;
         if (active && k < K - 1) {
             Token<kQuadStates, CQ> cur;
+            QuadDelta sp{0.0f, quad_delta_load<T>(p, bb * L, t0 + static_cast<unsigned long long>(q), t1, d)};
             if (t0 < t1) load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
             for (unsigned long long t = t0; t < t1; ++t) {
+                const float dv = quad_delta<T>(p, bb * L, t, t0, t1, d, q, sp);
                 Token<kQuadStates, CQ> nxt;
                 if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
-                step_carry<kQuadStates, CQ>(h, prod, a, cur);
+                step_carry_quad<CQ>(h, prod, a, cur, dv);
                 cur = nxt;
             }
         }
@@ -528,12 +586,14 @@ __global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccS
     unsigned fail = 0;
     if (active && t0 < t1) {
         Token<kQuadStates, CQ> cur;
+        QuadDelta sp{0.0f, quad_delta_load<T>(p, bb * L, t0 + static_cast<unsigned long long>(q), t1, d)};
         load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
         for (unsigned long long t = t0; t < t1; ++t) {
+            const float dv = quad_delta<T>(p, bb * L, t, t0, t1, d, q, sp);
             Token<kQuadStates, CQ> nxt;
             if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
             float y = 0.0f;
-            fail = step_out_quad<CW, std::is_same_v<T, __half>>(h, a, cur, p.has_d != 0, skip_d, y);
+            fail = step_out_quad<CW, std::is_same_v<T, __half>>(h, a, cur, dv, p.has_d != 0, skip_d, y);
             if (fail) break;
             if (q == 0) store_act(static_cast<T*>(p.y) + (bb * L + t) * Dc + d, y);
             cur = nxt;

@@ -7,7 +7,7 @@
 //  * one thread owns a (batch, channel) lane and keeps all N states of that
 //    lane in registers, so per-token work (softplus, u/delta loads, D skip,
 //    output store) is done once per lane instead of N times and the state sum
-//    needs no shuffles; for N = 16, four threads share a lane, four states
+//    needs no shuffles; for N >= 8, four threads share a lane, N / 4 states
 //    each (scan_f32_quad_kernel), for four times the warps per SM;
 //  * the length axis is split into K chunks (K a power of two) when there are
 //    too few lanes to fill 148 SMs.  Chunk k of a lane first runs the
@@ -406,28 +406,29 @@ __global__ void __launch_bounds__(kThreads) scan_f32_kernel(Params p, SaccScanSt
     if (blockIdx.x == 0 && threadIdx.x == 0) pdl_wait();
 }
 
-// N = 16 with four threads per lane (scan_f32_quad_kernel): thread q of a
-// lane owns states q, q + 4, q + 8 and q + 12, so the reference's butterfly
-// sum (offset 8 first) runs its first two levels inside each thread and its
-// last two as xor shuffles over the four threads (offsets 2, then 1): the same
-// association, so the same bits.  A thread holds a quarter of the states, a
-// CTA four times the warps, and the per-token softplus is formed by each of
-// the four threads.
-constexpr int kQuad = 4, kQuadStates = 4;
+// N >= 8 with four threads per lane (scan_f32_quad_kernel): thread q of a
+// lane owns states q, q + 4, ..., q + N - 4, so the reference's butterfly sum
+// (offset N/2 first) runs its levels of offset 4 and more inside each thread
+// (offset w pairs the thread's values j and j + w/4: tree_sum over them) and
+// its last two as xor shuffles over the four threads (offsets 2, then 1): the
+// same association, so the same bits.  A thread holds a quarter of the states
+// and a CTA four times the warps.
+constexpr int kQuad = 4;
 
-template <typename T, int CW>
+template <typename T, int N, int CW>
 __device__ __forceinline__ void load_token_quad(const Params& p, unsigned long long token, unsigned long long d, int q,
-                                                Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k) {
+                                                Token<N / kQuad, (CW > 1 ? N / kQuad : 1)>& k) {
+    constexpr int S = N / kQuad;
     const unsigned long long at = token * p.channels + d;
     k.u = load_act(static_cast<const T*>(p.u) + at);
     k.x = load_act(static_cast<const T*>(p.delta) + at);
-    const T* b = static_cast<const T*>(p.b) + token * 16 + q;
+    const T* b = static_cast<const T*>(p.b) + token * N + q;
 #pragma unroll
-    for (int j = 0; j < kQuadStates; ++j) k.b[j] = load_act(b + 4 * j);
+    for (int j = 0; j < S; ++j) k.b[j] = load_act(b + 4 * j);
     if constexpr (CW > 1) {
-        const T* c = static_cast<const T*>(p.c) + token * 16 + q;
+        const T* c = static_cast<const T*>(p.c) + token * N + q;
 #pragma unroll
-        for (int j = 0; j < kQuadStates; ++j) k.c[j] = load_act(c + 4 * j);
+        for (int j = 0; j < S; ++j) k.c[j] = load_act(c + 4 * j);
     } else {
         k.c[0] = load_act(static_cast<const T*>(p.c) + token);
     }
@@ -437,13 +438,17 @@ __device__ __forceinline__ void load_token_quad(const Params& p, unsigned long l
 // different chunks and lanes, so every shuffle names its own group only.
 __device__ __forceinline__ unsigned quad_mask() { return 0xfu << (threadIdx.x & 28u); }
 
-// The sum over all 16 states of one token in the reference's association:
-// in-thread levels (states q + (q + 8), (q + 4) + (q + 12), then their sum),
+// The sum over all N states of one token in the reference's association:
+// the in-thread levels (for N = 16: (q + (q + 8)) + ((q + 4) + (q + 12))),
 // then the partner at xor 2 and at xor 1.  Every thread of the four gets the
 // same bits (IEEE addition is commutative).
-__device__ __forceinline__ float quad_sum(const float (&t)[kQuadStates]) {
+template <int S>
+__device__ __forceinline__ float quad_sum(const float (&t)[S]) {
     const unsigned m = quad_mask();
-    float v = __fadd_rn(__fadd_rn(t[0], t[2]), __fadd_rn(t[1], t[3]));
+    float w[S];
+#pragma unroll
+    for (int j = 0; j < S; ++j) w[j] = t[j];
+    float v = tree_sum<S>(w);
     v = __fadd_rn(v, __shfl_xor_sync(m, v, 2));
     return __fadd_rn(v, __shfl_xor_sync(m, v, 1));
 }
@@ -451,17 +456,17 @@ __device__ __forceinline__ float quad_sum(const float (&t)[kQuadStates]) {
 // step_out for a quarter of the states: the four threads' failure bits are
 // combined (each state's first failure in the reference's order, OR-ed over
 // the states as the reference's group does), so all four return together.
-template <int CW, bool kHalfOut>
-__device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const float (&a)[kQuadStates],
-                                                  const Token<kQuadStates, (CW > 1 ? kQuadStates : 1)>& k, float dv, bool has_d,
+template <int N, int CW, bool kHalfOut>
+__device__ __forceinline__ unsigned step_out_quad(float (&h)[N / kQuad], const float (&a)[N / kQuad],
+                                                  const Token<N / kQuad, (CW > 1 ? N / kQuad : 1)>& k, float dv, bool has_d,
                                                   float skip_d, float& y) {
-    constexpr int CQ = CW > 1 ? kQuadStates : 1;
-    float hn[kQuadStates], decay[kQuadStates], drive[kQuadStates];
-    if (!states_fast_dv<kQuadStates, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
+    constexpr int S = N / kQuad, CQ = CW > 1 ? S : 1;
+    float hn[S], decay[S], drive[S];
+    if (!states_fast_dv<S, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<S, CQ>(h, a, k, hn, decay, drive);
     unsigned fail = 0;
-    float term[kQuadStates];
+    float term[S];
 #pragma unroll
-    for (int j = 0; j < kQuadStates; ++j) {
+    for (int j = 0; j < S; ++j) {
         term[j] = __fmul_rn(k.c[CQ > 1 ? j : 0], hn[j]);
         fail |= !finite32(decay[j]) ? kDecay : !finite32(drive[j]) ? kDrive : !finite32(hn[j]) ? kState
               : !finite32(term[j]) ? kTerm : 0u;
@@ -470,17 +475,17 @@ __device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const
     fail |= __shfl_xor_sync(quad_mask(), fail, 1);
     fail |= __shfl_xor_sync(quad_mask(), fail, 2);
     if (fail) return fail;
-    const float sum = quad_sum(term);
+    const float sum = quad_sum<S>(term);
     const float skip = __fmul_rn(skip_d, k.u);
     if (has_d && !finite32(skip)) return kSkip;
     float out = has_d ? __fadd_rn(sum, skip) : sum;
     if (!finite32(out)) {
         // Every term is finite but a partial sum left the FP32 range: repeat
         // with exact power-of-two scaling (reference cuda/selective_scan.cu:116-122).
-        float sc[kQuadStates];
+        float sc[S];
 #pragma unroll
-        for (int j = 0; j < kQuadStates; ++j) sc[j] = __fmul_rn(term[j], 0x1p-8f);
-        const float scaled = quad_sum(sc);
+        for (int j = 0; j < S; ++j) sc[j] = __fmul_rn(term[j], 0x1p-8f);
+        const float scaled = quad_sum<S>(sc);
         out = has_d ? __fadd_rn(scaled, __fmul_rn(skip, 0x1p-8f)) : scaled;
         if (fabsf(out) <= FLT_MAX * 0x1p-8f) out = __fmul_rn(out, 0x1p8f);
         else return kOutput;
@@ -491,13 +496,12 @@ __device__ __forceinline__ unsigned step_out_quad(float (&h)[kQuadStates], const
 }
 
 // Pass 1 step for a quarter of the states, Delta given.
-template <int CQ>
-__device__ __forceinline__ void step_carry_quad(float (&h)[kQuadStates], float (&prod)[kQuadStates], const float (&a)[kQuadStates],
-                                                const Token<kQuadStates, CQ>& k, float dv) {
-    float hn[kQuadStates], decay[kQuadStates], drive[kQuadStates];
-    if (!states_fast_dv<kQuadStates, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<kQuadStates, CQ>(h, a, k, hn, decay, drive);
+template <int S, int CQ>
+__device__ __forceinline__ void step_carry_quad(float (&h)[S], float (&prod)[S], const float (&a)[S], const Token<S, CQ>& k, float dv) {
+    float hn[S], decay[S], drive[S];
+    if (!states_fast_dv<S, CQ>(h, a, k, dv, hn, decay, drive)) states_scaled<S, CQ>(h, a, k, hn, decay, drive);
 #pragma unroll
-    for (int j = 0; j < kQuadStates; ++j) {
+    for (int j = 0; j < S; ++j) {
         h[j] = hn[j];
         prod[j] = __fmul_rn(prod[j], decay[j]);
     }
@@ -526,12 +530,12 @@ __device__ __forceinline__ float quad_delta(const Params& p, unsigned long long 
     return __shfl_sync(quad_mask(), qd.mine, static_cast<int>(threadIdx.x & 28u) | j);
 }
 
-// scan_f32_kernel for N = 16 at four threads per lane: the same chunks, carry
+// scan_f32_kernel for N >= 8 at four threads per lane: the same chunks, carry
 // fold and failure rules, each (lane, chunk) a group of four consecutive
 // threads.  With the same chunk count its outputs are scan_f32_kernel's bits.
-template <typename T, int CW>
+template <typename T, int N, int CW>
 __global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccScanStatus* status) {
-    constexpr int CQ = CW > 1 ? kQuadStates : 1;
+    constexpr int S = N / kQuad, CQ = CW > 1 ? S : 1;
     extern __shared__ float2 carry[]; // [chunk][lane in CTA][state]: (decay product, local state)
     __shared__ int chunk_failed[kThreads / kQuad];
     const int K = p.chunks, LPC = p.lanes_per_cta;
@@ -542,41 +546,41 @@ __global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccS
     const unsigned long long bb = active ? lane / Dc : 0, d = active ? lane % Dc : 0;
     const unsigned long long t0 = L * k / K, t1 = L * (k + 1) / K;
 
-    float a[kQuadStates];
+    float a[S];
 #pragma unroll
-    for (int j = 0; j < kQuadStates; ++j) a[j] = active ? __ldg(p.a + (p.a_shared ? 0 : d * 16) + q + 4 * j) : 0.0f;
+    for (int j = 0; j < S; ++j) a[j] = active ? __ldg(p.a + (p.a_shared ? 0 : d * N) + q + 4 * j) : 0.0f;
     const float skip_d = (active && p.has_d) ? __ldg(p.d + d) : 0.0f;
-    float h[kQuadStates];
+    float h[S];
 #pragma unroll
-    for (int j = 0; j < kQuadStates; ++j) h[j] = 0.0f;
+    for (int j = 0; j < S; ++j) h[j] = 0.0f;
 
     if (K > 1) {
-        float prod[kQuadStates];
+        float prod[S];
 #pragma unroll
-        for (int j = 0; j < kQuadStates; ++j) prod[j] = 1.0f;
+        for (int j = 0; j < S; ++j) prod[j] = 1.0f;
         if (active && k < K - 1) {
-            Token<kQuadStates, CQ> cur;
+            Token<S, CQ> cur;
             QuadDelta sp{0.0f, quad_delta_load<T>(p, bb * L, t0 + static_cast<unsigned long long>(q), t1, d)};
-            if (t0 < t1) load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
+            if (t0 < t1) load_token_quad<T, N, CW>(p, bb * L + t0, d, q, cur);
             for (unsigned long long t = t0; t < t1; ++t) {
                 const float dv = quad_delta<T>(p, bb * L, t, t0, t1, d, q, sp);
-                Token<kQuadStates, CQ> nxt;
-                if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
-                step_carry_quad<CQ>(h, prod, a, cur, dv);
+                Token<S, CQ> nxt;
+                if (t + 1 < t1) load_token_quad<T, N, CW>(p, bb * L + t + 1, d, q, nxt);
+                step_carry_quad<S, CQ>(h, prod, a, cur, dv);
                 cur = nxt;
             }
         }
-        float2* mine = carry + (static_cast<size_t>(k) * LPC + li) * 16;
+        float2* mine = carry + (static_cast<size_t>(k) * LPC + li) * N;
 #pragma unroll
-        for (int j = 0; j < kQuadStates; ++j) mine[q + 4 * j] = make_float2(prod[j], h[j]);
+        for (int j = 0; j < S; ++j) mine[q + 4 * j] = make_float2(prod[j], h[j]);
         __syncthreads();
         // Fold the carries of chunks 0..k-1: H = prod_j * H + local_j.
 #pragma unroll
-        for (int j = 0; j < kQuadStates; ++j) h[j] = 0.0f;
+        for (int j = 0; j < S; ++j) h[j] = 0.0f;
         for (int c = 0; c < k; ++c) {
-            const float2* cj = carry + (static_cast<size_t>(c) * LPC + li) * 16;
+            const float2* cj = carry + (static_cast<size_t>(c) * LPC + li) * N;
 #pragma unroll
-            for (int j = 0; j < kQuadStates; ++j) {
+            for (int j = 0; j < S; ++j) {
                 const float2 v = cj[q + 4 * j];
                 h[j] = h[j] == 0.0f ? v.y : __fmaf_rn(v.x, h[j], v.y);
             }
@@ -585,15 +589,15 @@ __global__ void __launch_bounds__(kThreads) scan_f32_quad_kernel(Params p, SaccS
 
     unsigned fail = 0;
     if (active && t0 < t1) {
-        Token<kQuadStates, CQ> cur;
+        Token<S, CQ> cur;
         QuadDelta sp{0.0f, quad_delta_load<T>(p, bb * L, t0 + static_cast<unsigned long long>(q), t1, d)};
-        load_token_quad<T, CW>(p, bb * L + t0, d, q, cur);
+        load_token_quad<T, N, CW>(p, bb * L + t0, d, q, cur);
         for (unsigned long long t = t0; t < t1; ++t) {
             const float dv = quad_delta<T>(p, bb * L, t, t0, t1, d, q, sp);
-            Token<kQuadStates, CQ> nxt;
-            if (t + 1 < t1) load_token_quad<T, CW>(p, bb * L + t + 1, d, q, nxt);
+            Token<S, CQ> nxt;
+            if (t + 1 < t1) load_token_quad<T, N, CW>(p, bb * L + t + 1, d, q, nxt);
             float y = 0.0f;
-            fail = step_out_quad<CW, std::is_same_v<T, __half>>(h, a, cur, dv, p.has_d != 0, skip_d, y);
+            fail = step_out_quad<N, CW, std::is_same_v<T, __half>>(h, a, cur, dv, p.has_d != 0, skip_d, y);
             if (fail) break;
             if (q == 0) store_act(static_cast<T*>(p.y) + (bb * L + t) * Dc + d, y);
             cur = nxt;
@@ -657,22 +661,32 @@ const void* pick_kernel_t(unsigned state, bool c_full) {
     }
 }
 
-// Threads per lane: four for N = 16 (scan_f32_quad_kernel), one otherwise.
-// SACC_F32_KERNEL=one_thread keeps N = 16 on scan_f32_kernel, the kernel the
+template <typename T>
+const void* pick_quad_t(unsigned state, bool c_full) {
+    switch (state) {
+    case 8: return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 8, 8>)
+                          : reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 8, 1>);
+    case 16: return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 16, 16>)
+                           : reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 16, 1>);
+    default: return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 32, 32>)
+                           : reinterpret_cast<const void*>(scan_f32_quad_kernel<T, 32, 1>);
+    }
+}
+
+// Threads per lane: four for N >= 8 (scan_f32_quad_kernel), one otherwise.
+// SACC_F32_KERNEL=one_thread keeps every N on scan_f32_kernel, the kernel the
 // four-thread one reproduces bit for bit when both split a lane into the same
 // chunks (tests compare the two).
 int threads_per_lane(unsigned state) {
-    if (state != 16) return 1;
+    if (state < 8) return 1;
     const char* v = std::getenv("SACC_F32_KERNEL");
     return (v && std::strcmp(v, "one_thread") == 0) ? 1 : kQuad;
 }
 
 const void* pick_kernel(unsigned state, bool half, bool c_full) {
     if (threads_per_lane(state) == kQuad) {
-        if (half) return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16>)
-                                : reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 1>);
-        return c_full ? reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16>)
-                      : reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 1>);
+        if (half) return pick_quad_t<__half>(state, c_full);
+        return pick_quad_t<float>(state, c_full);
     }
     return half ? pick_kernel_t<__half>(state, c_full) : pick_kernel_t<float>(state, c_full);
 }
@@ -683,11 +697,11 @@ const void* pick_kernel(unsigned state, bool half, bool c_full) {
 // both split a lane into the same chunks and the FP16 outputs stay the FP32
 // outputs rounded.
 int resident_per_sm(unsigned state, bool c_full) {
-    static std::atomic<int> cache[64][14] = {};
+    static std::atomic<int> cache[64][24] = {};
     int idx = 0;
     while ((1u << idx) < state && idx < 5) ++idx;
     const int tpl = threads_per_lane(state);
-    idx = tpl == kQuad ? 12 + (c_full ? 1 : 0) : 2 * idx + (c_full ? 1 : 0);
+    idx = (tpl == kQuad ? 12 : 0) + 2 * idx + (c_full ? 1 : 0);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
     int v = cache[dev][idx].load(std::memory_order_relaxed);
@@ -799,10 +813,18 @@ cudaError_t load_scan_f32_kernels(std::string& report) {
         {"scan_f16io_c1_n8", scan_kernel_ptr<__half, 8, 1>(), kThreads * 8 * sizeof(float2)},
         {"scan_f16io_c1_n16", scan_kernel_ptr<__half, 16, 1>(), kThreads * 16 * sizeof(float2)},
         {"scan_f16io_c1_n32", scan_kernel_ptr<__half, 32, 1>(), kThreads * 32 * sizeof(float2)},
-        {"scan_f32_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16>), 0},
-        {"scan_f32_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 1>), 0},
-        {"scan_f16io_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16>), 0},
-        {"scan_f16io_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 1>), 0},
+        {"scan_f32_quad_n8", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 8, 8>), 0},
+        {"scan_f32_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16, 16>), 0},
+        {"scan_f32_quad_n32", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 32, 32>), 0},
+        {"scan_f32_quad_c1_n8", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 8, 1>), 0},
+        {"scan_f32_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 16, 1>), 0},
+        {"scan_f32_quad_c1_n32", reinterpret_cast<const void*>(scan_f32_quad_kernel<float, 32, 1>), 0},
+        {"scan_f16io_quad_n8", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 8, 8>), 0},
+        {"scan_f16io_quad_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16, 16>), 0},
+        {"scan_f16io_quad_n32", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 32, 32>), 0},
+        {"scan_f16io_quad_c1_n8", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 8, 1>), 0},
+        {"scan_f16io_quad_c1_n16", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 16, 1>), 0},
+        {"scan_f16io_quad_c1_n32", reinterpret_cast<const void*>(scan_f32_quad_kernel<__half, 32, 1>), 0},
         {"check", reinterpret_cast<const void*>(check_kernel), 0},
         {"finalize", reinterpret_cast<const void*>(finalize_kernel<unsigned, 0x7fc00000u>), 0},
         {"finalize_f16", reinterpret_cast<const void*>(finalize_kernel<unsigned short, 0x7e00u>), 0},

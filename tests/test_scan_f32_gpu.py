@@ -182,13 +182,17 @@ def test_deploy_shapes_random():
 
 
 def test_four_threads_per_lane_equal_one_thread(monkeypatch):
-    """N = 16 runs four threads per lane (states q, q + 4, q + 8, q + 12 each, the reference's butterfly sum
-    finished by two xor shuffles); with the one-thread kernel (SACC_F32_KERNEL=one_thread) splitting the
-    lanes into the same chunks, outputs and status bits are identical, at the deploy shapes (rank-1 C), with a
-    full C, and on the failure cases."""
+    """N >= 8 runs four threads per lane (states q, q + 4, ... each, the reference's butterfly sum finished by
+    two xor shuffles); with the one-thread kernel (SACC_F32_KERNEL=one_thread) splitting the lanes into the
+    same chunks, outputs and status bits are identical: at the deploy shapes (rank-1 C), with a full C, for
+    N = 8 and 32, and on the failure cases."""
     cases = {f"deploy_L{L}": random_case(Shape(4, L, 256, 16, 1, 1, True), 900 + L) for L in (960, 240, 60, 7)}
     cases["full_c_per_channel_a"] = random_case(Shape(3, 200, 64, 16, 64, 16, True), 77)
-    cases.update({name: k for name, k, _, _, _ in sc.failure_cases() if k.shape.state == 16})
+    # N = 8 and 32 on 40,960 lanes, where both kernels run one chunk per lane.
+    for n in (8, 32):
+        cases[f"n{n}_full_c"] = random_case(Shape(5, 16, 8192, n, 1, n, True), 80 + n)
+        cases[f"n{n}_rank1_c"] = random_case(Shape(5, 16, 8192, n, 8192, 1, False), 90 + n)
+    cases.update({name: k for name, k, _, _, _ in sc.failure_cases() if k.shape.state >= 8})
     for name, k in cases.items():
         monkeypatch.setenv("SACC_F32_KERNEL", "one_thread")
         want = gu.run_f32(k)
